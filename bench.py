@@ -1,0 +1,440 @@
+"""Benchmark: porch lazy-graph hot path on B200.
+
+Default workload (N=1): config 2 of the baseline, the fused view/indexing
+graph concat(transpose(X[0::2, 1024:7168]) + broadcast(b), Y, 0) ->
+[12288, 4096] fp32, metric "fused-graph HBM GB/s" (algorithmic bytes per
+realisation / time). Other workloads: --workload c1_elementwise |
+c3a_softmax | c3b_relu_logistic | c4_matmul | c5_mlp.
+
+Multi-GPU (python -m torch.distributed.run ... bench.py --gpus N): the
+default graph does not shard, so every rank realises its own replica on its
+own GPU (weak scaling, no data-path collective); torch.distributed (gloo)
+carries only the barrier and the max-over-ranks timing. Row-shardable
+workloads (c3a/c3b/c5) split their rows across ranks (strong scaling).
+
+--impl reference runs the reference's own implementation of the path
+(oracle/_ref/ref_runner: AkhilSamavedam/porch compiled from its sources,
+NVRTC JIT on the same GPU) on rank 0 and prints the same metric.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+SEED = 20261201
+CONFIGS = {
+    # name: (inputs [(shape, dist, a, b)], algorithmic bytes or flops, bound)
+    "c1_elementwise": ([([1 << 24], "uniform", -1, 1), ([1 << 24], "uniform", -1, 1)],
+                       12 * (1 << 24), "hbm"),
+    "c2_view": ([([8192, 8192], "normal", 0, 1), ([4096], "uniform", -0.5, 0.5),
+                 ([6144, 4096], "normal", 0, 1)],
+                4096 * 6144 * 4 + 6144 * 4096 * 4 + 4096 * 4 + 12288 * 4096 * 4, "hbm"),
+    "c3a_softmax": ([([65536, 4096], "normal", 0, 2)], 2 * 65536 * 4096 * 4, "hbm"),
+    "c3b_relu_logistic": ([([65536, 4096], "normal", 0, 2)], 2 * 65536 * 4096 * 4, "hbm"),
+    "c4_matmul": ([([8192, 8192], "uniform", -1 / 90.50966799187808, 1 / 90.50966799187808),
+                   ([8192, 8192], "uniform", -1 / 90.50966799187808, 1 / 90.50966799187808),
+                   ([8192], "uniform", -0.1, 0.1)], 2 * 8192 ** 3, "tensor"),
+    "c5_mlp": ([([16384, 4096], "normal", 0, 1), ([4096, 16384], "normal", 0, 1 / 64),
+                ([16384], "uniform", -0.1, 0.1), ([16384, 4096], "normal", 0, 1 / 128),
+                ([4096], "uniform", -0.1, 0.1)], 4 * 16384 * 4096 * 16384, "tensor"),
+}
+ROW_SHARDED = {"c3a_softmax", "c3b_relu_logistic", "c5_mlp"}
+KEYS = {
+    "c1_elementwise": ["a", "b"], "c2_view": ["x", "bias", "y"], "c3a_softmax": ["x"],
+    "c3b_relu_logistic": ["x"], "c4_matmul": ["a", "b", "bias"],
+    "c5_mlp": ["x", "w1", "b1", "w2", "b2"],
+}
+# Kernel family whose launches the roofline line describes.
+DOMINANT = {"c1_elementwise": "pb_elem", "c2_view": "pb_elem", "c3a_softmax": "pb_softmax",
+            "c3b_relu_logistic": "pb_elem", "c4_matmul": "pb_gemm", "c5_mlp": "pb_gemm"}
+
+
+def peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained"), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self._t.join(timeout=2)
+        return False
+
+    def summary(self) -> dict | None:
+        rows = []
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), parts[5:9]))
+            except ValueError:
+                continue
+        if not rows:
+            return None
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for _, _, flags in rows:
+            for n, f in zip(names, flags):
+                if f.lower().startswith("active"):
+                    reasons.add(n)
+        loaded = [r[0] for r in rows]
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+def dist_setup(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
+        return rank, world, local, dist
+    return 0, 1, 0, None
+
+
+def max_over_ranks(dist, value: float) -> float:
+    if dist is None:
+        return value
+    import torch
+
+    t = torch.tensor([value], dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(dist):
+    if dist is not None:
+        dist.barrier()
+
+
+def make_host_inputs(api, workload: str, rank: int, world: int):
+    specs, _, _ = CONFIGS[workload]
+    arrays = []
+    for i, (shape, dist_name, a, b) in enumerate(specs):
+        shape = list(shape)
+        arr = np.empty(int(np.prod(shape)), dtype=np.float32)
+        api.fill_synthetic(arr, SEED + i, dist_name, a, b)
+        arr = arr.reshape(shape)
+        if workload in ROW_SHARDED and world > 1 and i == 0:
+            rows = shape[0] // world
+            arr = np.ascontiguousarray(arr[rank * rows:(rank + 1) * rows])
+        arrays.append(arr)
+    return arrays
+
+
+def cpu_baseline(workload: str, arrays) -> dict:
+    """The host oracle on a bounded sample of the same workload."""
+    from oracle.graph import Program
+
+    threads = os.cpu_count() or 1
+    P = Program(threads=threads)
+    if workload == "c2_view":
+        # A row band of the output: rows [0, R) of the transposed slice and
+        # rows [0, R) of Y -> 2R output rows; bytes scale accordingly.
+        R = 2048
+        x, bias, y = arrays
+        xs = np.ascontiguousarray(x[:, 1024:1024 + R])
+        X = P.tensor(list(xs.shape), xs)
+        B = P.tensor([4096], bias)
+        Y = P.tensor([R, 4096], np.ascontiguousarray(y[:R]))
+        node = P.concat(P.transpose(X[0::2, 0:R]) + P.broadcast_to(B, [R, 4096]), Y, 0)
+        nbytes = (R * 4096 * 4) * 2 + 4096 * 4 + (2 * R * 4096 * 4)
+        sample = f"output rows 0..{R} and {6144}..{6144 + R} (2*{R} of 12288 rows)"
+    elif workload == "c1_elementwise":
+        n = 1 << 22
+        a, b = (P.tensor([n], arr[:n]) for arr in arrays)
+        node = (a + b) * 2.0 - 1.0
+        nbytes = 12 * n
+        sample = f"first {n} of {1 << 24} elements"
+    elif workload in ("c3a_softmax", "c3b_relu_logistic"):
+        rows = 2048
+        xs = np.ascontiguousarray(arrays[0][:rows])
+        X = P.tensor(list(xs.shape), xs)
+        node = P.softmax(X, 1) if workload == "c3a_softmax" else P.logistic(P.relu(X))
+        nbytes = 2 * xs.size * 4
+        sample = f"{rows} of {arrays[0].shape[0]} rows"
+    else:
+        rows = 16
+        a = np.ascontiguousarray(arrays[0][:rows])
+        A = P.tensor(list(a.shape), a)
+        if workload == "c4_matmul":
+            Bm = P.tensor(list(arrays[1].shape), arrays[1])
+            Bi = P.tensor([arrays[2].shape[0]], arrays[2])
+            node = P.relu(P.matmul(A, Bm) + P.broadcast_to(Bi, [rows, arrays[1].shape[1]]))
+            nbytes = 2 * rows * arrays[0].shape[1] * arrays[1].shape[1]
+        else:
+            W1 = P.tensor(list(arrays[1].shape), arrays[1])
+            B1 = P.tensor([arrays[2].shape[0]], arrays[2])
+            W2 = P.tensor(list(arrays[3].shape), arrays[3])
+            B2 = P.tensor([arrays[4].shape[0]], arrays[4])
+            h = P.logistic(P.matmul(A, W1) + P.broadcast_to(B1, [rows, arrays[1].shape[1]]))
+            node = P.softmax(P.matmul(h, W2) + P.broadcast_to(B2, [rows, arrays[3].shape[1]]), 1)
+            nbytes = 4 * rows * arrays[1].shape[0] * arrays[1].shape[1]
+        sample = f"{rows} output rows"
+    t0 = time.perf_counter()
+    P.evaluate(node)
+    dt = time.perf_counter() - t0
+    unit = "GFLOP/s" if CONFIGS[workload][2] == "tensor" else "GB/s"
+    value = nbytes / dt / 1e9
+    return {"value": round(value, 3), "unit": unit, "cores": threads, "kind": "port",
+            "sample": sample, "seconds": round(dt, 3)}
+
+
+def run_ours(args, rank, world, local, dist):
+    from porch_b200 import api
+
+    workload = args.workload
+    specs, work, bound = CONFIGS[workload]
+    keys = KEYS[workload]
+    device = local
+    arrays = make_host_inputs(api, workload, rank, world)
+    work_rank = work
+    if workload in ROW_SHARDED and world > 1:
+        work_rank = work // world
+    # Device-resident input sets, rotated so each step reads memory the
+    # previous step did not (every set is larger than the 126 MB L2).
+    n_sets = 2
+    sets = []
+    for s in range(n_sets):
+        sets.append({k: api.tensor(list(a.shape), a, device=device) for k, a in zip(keys, arrays)})
+    graphs = [api.config_graph(workload, t) for t in sets]
+
+    def step(i):
+        return api.materialize(graphs[i % n_sets])
+
+    # Warm-up (first call lowers + compiles; later calls hit the plan cache).
+    for i in range(max(3, args.warmup)):
+        out = step(i)
+    api.device_synchronize(device)
+    del out
+
+    api.profile_enable(True)
+    api.profile_read()  # clear
+    barrier(dist)
+    api.device_synchronize(device)
+    launches0 = api.launch_count()
+    outs = []
+    with ClockSampler(device) as clocks:
+        with api.DeviceTimer(device) as timer:
+            for i in range(args.steps):
+                outs.append(step(i))
+                if len(outs) > 2:
+                    outs.pop(0)
+        api.device_synchronize(device)
+    launches = api.launch_count() - launches0
+    prof = api.profile_read()
+    api.profile_enable(False)
+    barrier(dist)
+    ms_rank = timer.ms / args.steps
+    ms = max_over_ranks(dist, ms_rank)
+    total_work = work_rank * world
+    unit = "GB/s" if bound == "hbm" else "TFLOP/s"
+    scale = 1e9 if bound == "hbm" else 1e12
+    value = total_work / (ms * 1e-3) / scale
+
+    # Roofline of the dominant kernel family from live per-launch events.
+    fam = DOMINANT[workload]
+    k_launches = sum(n for name, (n, _) in prof.items() if name.startswith(fam))
+    k_ms = sum(t for name, (_, t) in prof.items() if name.startswith(fam))
+    pk = peaks()
+    roofline = None
+    if k_launches:
+        per_launch_ms = k_ms / k_launches
+        per_launch_work = work_rank / max(1, k_launches // args.steps)
+        achieved = per_launch_work / (per_launch_ms * 1e-3) / scale
+        peak = pk["hbm_gbs"] if bound == "hbm" else pk["bf16_tflops"]
+        traffic = None
+        tfile = ROOT / "profiles" / "ncu_traffic.json"
+        if tfile.exists():
+            traffic = json.loads(tfile.read_text()).get(workload)
+        roofline = {"bound": bound, "achieved": round(achieved, 2), "peak": peak,
+                    "unit": unit, "frac": round(achieved / peak, 4), "traffic": traffic,
+                    "peak_source": pk["source"], "kernel": fam,
+                    "kernel_ms": round(per_launch_ms, 5)}
+
+    # End to end through the C-ABI with host buffers in pinned memory.
+    pinned = [api.PinnedBuffer(a.size) for a in arrays]
+    for pb, a in zip(pinned, arrays):
+        pb.array[:] = a.reshape(-1)
+    out_count = int(np.prod(api.materialize(graphs[0]).shape()))
+    out_buf = api.PinnedBuffer(out_count)
+    h2d = sum(a.size * 4 for a in arrays)
+    d2h = out_count * 4
+
+    def e2e_step():
+        ts = {k: api.tensor_from_pointer(list(a.shape), pb.address, a.size, device=device)
+              for k, a, pb in zip(keys, arrays, pinned)}
+        t = api.materialize(api.config_graph(workload, ts))
+        t.cpu(out_buf.array)
+
+    e2e_steps = max(1, min(args.steps, 10))
+    for _ in range(2):
+        e2e_step()
+    barrier(dist)
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        e2e_step()
+    api.device_synchronize(device)
+    e2e_ms_rank = (time.perf_counter() - t0) * 1e3 / e2e_steps
+    e2e_ms = max_over_ranks(dist, e2e_ms_rank)
+    e2e_value = total_work / (e2e_ms * 1e-3) / scale
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            cpu = cpu_baseline(workload, arrays)
+        except Exception as exc:  # the baseline must not sink the bench line
+            cpu = {"error": str(exc)}
+
+    if rank == 0:
+        line = {
+            "metric": CONFIG_METRIC[workload], "value": round(value, 3), "unit": unit,
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 5), "higher_is_better": True,
+            "scaling": "strong" if workload in ROW_SHARDED else "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic (seeded; distributions as the baseline config)",
+            "config": {"workload": workload, "shapes": {k: s for k, (s, *_) in zip(keys, specs)},
+                       "parallelism": (f"row-shard x{world}" if workload in ROW_SHARDED and world > 1
+                                       else (f"replicas x{world}" if world > 1 else "single GPU")),
+                       "l2": f"inputs rotated over {n_sets} device-resident sets, each larger than L2"},
+            "e2e": {"value": round(e2e_value, 3), "unit": unit, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4),
+                    "path": "pb_tensor_create from pinned host -> pb_materialize -> pb_tensor_read"},
+            "gpu_launches": launches,
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "clocks": clocks.summary(),
+            "kernels": {k: {"launches": n, "ms": round(t, 4)} for k, (n, t) in prof.items()},
+        }
+        print(json.dumps(line), flush=True)
+
+
+CONFIG_METRIC = {
+    "c1_elementwise": "fused-graph HBM GB/s (config 1: (a+b)*2-1, [2^24])",
+    "c2_view": "fused-graph HBM GB/s (config 2: slice/transpose/bias/concat -> [12288,4096])",
+    "c3a_softmax": "fused-graph HBM GB/s (config 3: softmax [65536,4096])",
+    "c3b_relu_logistic": "fused-graph HBM GB/s (config 3: logistic(relu) [65536,4096])",
+    "c4_matmul": "fp32 matmul TFLOP/s (config 4: relu(A@B+bias), 8192^3)",
+    "c5_mlp": "fp32 matmul TFLOP/s (config 5: MLP 16384x4096x16384)",
+}
+
+
+def run_reference(args, rank, world, dist):
+    workload = args.workload
+    specs, work, bound = CONFIGS[workload]
+    if rank != 0:
+        return
+    exe = ROOT / "oracle" / "_ref" / "ref_runner"
+    unit = "GB/s" if bound == "hbm" else "TFLOP/s"
+    scale = 1e9 if bound == "hbm" else 1e12
+    if not exe.exists():
+        print(json.dumps({"impl": "reference", "unavailable":
+                          "oracle/_ref/ref_runner was not built (reference sources absent)"}))
+        return
+    steps = args.steps if bound == "hbm" else max(1, min(args.steps, 2))
+    warm = max(1, min(args.warmup, 3))
+    cmd = [str(exe), "bench", workload, str(steps), str(warm), "e2e"]
+    res = subprocess.run(cmd, capture_output=True, text=True, timeout=1800)
+    if res.returncode != 0:
+        print(json.dumps({"impl": "reference", "unavailable": f"ref_runner failed: {res.stderr[-300:]}"}))
+        return
+    r = json.loads(res.stdout.strip().splitlines()[-1])
+    value = work / (r["warm_ms"] * 1e-3) / scale
+    e2e_value = work / (r["e2e_ms"] * 1e-3) / scale
+    line = {
+        "impl": "reference", "metric": CONFIG_METRIC[workload], "value": round(value, 4),
+        "unit": unit, "n_gpus": world, "steps": steps, "warmup": warm,
+        "ms_per_step": round(r["warm_ms"], 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (same seeds and generator as the porch_b200 arm)",
+        "config": {"workload": workload, "reference": "AkhilSamavedam/porch compiled from source",
+                   "path": "materialize(expr) + synchronize() through the reference's C++ API "
+                           "(NVRTC JIT, one GPU)", "staged_c5": r.get("staged")},
+        "e2e": {"value": round(e2e_value, 4), "unit": unit, "h2d_bytes_per_step": r["h2d_bytes"],
+                "d2h_bytes_per_step": r["d2h_bytes"], "ms_per_step": round(r["e2e_ms"], 4)},
+        "cpu_baseline": {"value": round(value, 4), "unit": unit, "cores": 1, "kind": "reference",
+                         "sample": "the reference has no CPU implementation of the path; "
+                                   "this is its own NVRTC-JIT GPU path, timed on the same box"},
+        "cold_ms": r["cold_ms"],
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="porch_b200", choices=["porch_b200", "reference"])
+    ap.add_argument("--workload", default="c2_view", choices=sorted(CONFIGS))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    rank, world, local, dist = dist_setup(args.gpus)
+    try:
+        if args.impl == "reference":
+            run_reference(args, rank, world, dist)
+        else:
+            run_ours(args, rank, world, local, dist)
+    finally:
+        if dist is not None:
+            dist.barrier()
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,175 @@
+/*
+ * porch_b200 flat C-ABI over the porch tensor API.
+ *
+ * The reference is a C++20 library (include/porch/tensor.hpp, ops.hpp,
+ * cuda_jit.hpp) and has no FFI of its own; this header is the binding a
+ * maintainer would add to reach it from C, Python (ctypes), Go (cgo) or any
+ * other FFI. Each entry point forwards to the C++ call named in its comment,
+ * with the same argument meaning, and turns that call's exception into a
+ * status code:
+ *   std::invalid_argument -> PB_ERR_INVALID_ARGUMENT
+ *   std::out_of_range     -> PB_ERR_OUT_OF_RANGE
+ *   cuda_jit::compilation_error -> PB_ERR_COMPILATION
+ *   any other exception   -> PB_ERR_RUNTIME
+ * The message of the last failure on the calling thread is pb_last_error().
+ *
+ * Handles: pb_tensor wraps porch::tensor (a shared handle), pb_expr wraps
+ * porch::tensor_expr. Release every handle you receive; releasing does not
+ * invalidate other handles that share the same storage.
+ */
+#ifndef PORCH_B200_H
+#define PORCH_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum pb_status {
+    PB_OK = 0,
+    PB_ERR_INVALID_ARGUMENT = 1,
+    PB_ERR_OUT_OF_RANGE = 2,
+    PB_ERR_RUNTIME = 3,
+    PB_ERR_COMPILATION = 4,
+};
+
+enum pb_op {
+    PB_ADD = 0,        /* operator+   (include/porch/tensor.hpp:221) */
+    PB_SUBTRACT = 1,   /* operator-   (tensor.hpp:222)               */
+    PB_MULTIPLY = 2,   /* operator*   (tensor.hpp:223)               */
+    PB_DIVIDE = 3,     /* operator/   (tensor.hpp:224)               */
+    PB_MAXIMUM = 4,    /* maximum     (tensor.hpp:212)               */
+    PB_MINIMUM = 5,    /* minimum     (tensor.hpp:213)               */
+    PB_MATMUL = 6,     /* matmul      (tensor.hpp:196)               */
+    PB_EXP = 7,        /* exp         (tensor.hpp:214)               */
+    PB_RECIPROCAL = 8, /* reciprocal  (tensor.hpp:215)               */
+    PB_TRANSPOSE = 9,  /* transpose   (tensor.hpp:201)               */
+    PB_RELU = 10,      /* relu        (include/porch/ops.hpp:7)      */
+    PB_LOGISTIC = 11,  /* logistic    (ops.hpp:9)                    */
+    PB_SUM = 12,       /* sum         (tensor.hpp:208)               */
+    PB_MAX = 13,       /* max         (tensor.hpp:210)               */
+};
+
+enum pb_index_kind { PB_INDEX = 0, PB_SLICE = 1, PB_ALL = 2 };
+
+/* One element of tensor::operator[] (tensor.hpp:43-69: index, slice, all). */
+typedef struct pb_index {
+    int kind;
+    int64_t index;
+    int64_t start;
+    int64_t stop;
+    int64_t step;
+} pb_index;
+
+typedef struct pb_tensor_s pb_tensor;
+typedef struct pb_expr_s pb_expr;
+
+const char* pb_last_error(void);
+/* cuda_jit::is_available (include/porch/cuda_jit.hpp:60) */
+int pb_is_available(void);
+/* backend_name(backend_for(device)) (include/porch/backend.hpp:35-37) */
+const char* pb_backend_name(void);
+/* cuda_jit::synchronize (cuda_jit.hpp:73): drain this thread's streams. */
+int pb_synchronize(void);
+
+/* ---- tensors ------------------------------------------------------------ */
+/* tensor(shape, values, device{device}) (tensor.hpp:99-102). `values` is
+ * read synchronously before return; page-locked memory (pb_host_alloc) makes
+ * the copy a direct DMA. Unlike the C++ constructor no host mirror is kept,
+ * so a later read copies from the device. */
+int pb_tensor_create(const int64_t* shape, size_t rank, const float* values,
+                     size_t count, int device, pb_tensor** out);
+/* full(shape, value, device) (tensor.hpp:184-186) */
+int pb_tensor_full(const int64_t* shape, size_t rank, float value, int device,
+                   pb_tensor** out);
+/* A shape-only tensor without device storage: usable only to build
+ * expressions passed to pb_expr_describe (plan inspection without a GPU). */
+int pb_tensor_placeholder(const int64_t* shape, size_t rank, int device,
+                          pb_tensor** out);
+void pb_tensor_release(pb_tensor* tensor);
+int pb_tensor_rank(const pb_tensor* tensor, size_t* rank);
+int pb_tensor_shape(const pb_tensor* tensor, int64_t* shape, size_t capacity);
+int pb_tensor_strides(const pb_tensor* tensor, int64_t* strides, size_t capacity);
+int pb_tensor_numel(const pb_tensor* tensor, size_t* numel);
+int pb_tensor_storage_offset(const pb_tensor* tensor, int64_t* offset);
+int pb_tensor_is_contiguous(const pb_tensor* tensor, int* contiguous);
+int pb_tensor_device(const pb_tensor* tensor, int* device);
+/* tensor::realize / tensor::synchronize (tensor.hpp:118-119) */
+int pb_tensor_realize(const pb_tensor* tensor);
+int pb_tensor_synchronize(const pb_tensor* tensor);
+/* tensor::cpu() copied into `values` (tensor.hpp:116). Materialises first.
+ * Copies straight from device memory into `values`. */
+int pb_tensor_read(const pb_tensor* tensor, float* values, size_t count);
+/* tensor::device_data() (tensor.hpp:117): device address and size in bytes. */
+int pb_tensor_device_pointer(const pb_tensor* tensor, uint64_t* pointer,
+                             size_t* bytes);
+/* tensor::operator[] (tensor.hpp:120-123) */
+int pb_tensor_index(const pb_tensor* tensor, const pb_index* indices,
+                    size_t count, pb_expr** out);
+
+/* ---- expressions -------------------------------------------------------- */
+/* tensor_expr(const tensor&) / tensor_expr(float) (tensor.hpp:146-147) */
+int pb_expr_from_tensor(const pb_tensor* tensor, pb_expr** out);
+int pb_expr_scalar(float value, pb_expr** out);
+void pb_expr_release(pb_expr* expr);
+/* PB_ADD..PB_MATMUL */
+int pb_expr_binary(int op, const pb_expr* lhs, const pb_expr* rhs, pb_expr** out);
+/* PB_EXP, PB_RECIPROCAL, PB_TRANSPOSE, PB_RELU, PB_LOGISTIC */
+int pb_expr_unary(int op, const pb_expr* value, pb_expr** out);
+/* reshape / broadcast_to (tensor.hpp:197-204) */
+int pb_expr_reshape(const pb_expr* value, const int64_t* shape, size_t rank,
+                    pb_expr** out);
+int pb_expr_broadcast(const pb_expr* value, const int64_t* shape, size_t rank,
+                      pb_expr** out);
+/* unsqueeze / concat (tensor.hpp:200, 205-207) */
+int pb_expr_unsqueeze(const pb_expr* value, size_t axis, pb_expr** out);
+int pb_expr_concat(const pb_expr* lhs, const pb_expr* rhs, size_t axis,
+                   pb_expr** out);
+/* sum / max with keepdim (PB_SUM, PB_MAX) */
+int pb_expr_reduce(int op, const pb_expr* value, size_t axis, int keepdim,
+                   pb_expr** out);
+/* softmax(value, axis) (ops.hpp:8) */
+int pb_expr_softmax(const pb_expr* value, size_t axis, pb_expr** out);
+/* tensor_expr::shape() (tensor.hpp:150). *rank receives the rank; up to
+ * `capacity` extents are written. A scalar expression has rank 0. */
+int pb_expr_shape(const pb_expr* expr, int64_t* shape, size_t capacity,
+                  size_t* rank);
+/* tensor_expr::operator tensor() (tensor.hpp:154): a lazy tensor. */
+int pb_expr_to_tensor(const pb_expr* expr, pb_tensor** out);
+/* materialize(expr) (tensor.hpp:217): a realised tensor. */
+int pb_materialize(const pb_expr* expr, pb_tensor** out);
+/* Describes the kernel plan for `expr` (kernels, schedules, and with
+ * with_source != 0 the generated CUDA). *needed receives the full length
+ * including the terminating NUL; the text is truncated to `capacity`. */
+int pb_expr_describe(const pb_expr* expr, int with_source, char* text,
+                     size_t capacity, size_t* needed);
+
+/* ---- host memory, timing, counters -------------------------------------- */
+int pb_host_alloc(size_t bytes, void** pointer); /* page-locked */
+int pb_host_free(void* pointer);
+/* Device timer on this thread's porch stream of `device`: begin records a
+ * start event, end records a stop event, waits for it and returns the
+ * elapsed milliseconds. */
+int pb_timer_begin(int device, void** timer);
+int pb_timer_end(void* timer, float* milliseconds);
+/* Synchronise this thread's porch stream on `device`. */
+int pb_device_synchronize(int device);
+/* Kernel launches issued by this library since process start. */
+uint64_t pb_launch_count(void);
+/* Per-launch kernel timing (events around each launch); see
+ * pbrt_profile_read for the text format. */
+int pb_profile_enable(int enable);
+int pb_profile_read(char* text, size_t capacity);
+/* Fills `values` (count floats) with seeded synthetic data: dist 0 = uniform
+ * on [a, b), dist 1 = normal(mean a, stddev b). Deterministic for a given
+ * (seed, count, dist, a, b), independent of thread count. Host side only. */
+int pb_fill_synthetic(float* values, size_t count, uint64_t seed, int dist,
+                      double a, double b);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PORCH_B200_H */

@@ -1,0 +1,217 @@
+// Internal declarations shared by the porch_b200 C++ front-end.
+#pragma once
+
+#include "porch/tensor.hpp"
+#include "porch_b200_rt.h"
+
+#include <atomic>
+#include <cstdint>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+namespace porch::detail {
+
+    // ------------------------------------------------------------ errors --
+    // Maps a runtime status to the reference's exception conventions
+    // (std::invalid_argument / std::out_of_range / compilation_error /
+    // std::runtime_error; src/cuda_jit.cpp:304-339, include/porch/cuda_jit.hpp:50-58).
+    [[noreturn]] void throw_status(int status);
+    inline void check(int status) {
+        if (status != PBRT_OK) throw_status(status);
+    }
+
+    // ----------------------------------------------------------- streams --
+    // A stream with shared lifetime: buffers keep their producer stream alive
+    // until their stream-ordered free has been enqueued (the same guarantee
+    // as the reference's shared stream_handle, src/cuda_jit.cpp:479-528).
+    struct stream_ref {
+        int device = 0;
+        pbrt_stream stream = nullptr;
+        stream_ref(int device_index, pbrt_stream s)
+            : device(device_index), stream(s) {}
+        stream_ref(const stream_ref&) = delete;
+        stream_ref& operator=(const stream_ref&) = delete;
+        ~stream_ref();
+    };
+
+    // The calling thread's stream on `device`.
+    std::shared_ptr<stream_ref> current_stream(int device);
+    // Streams the calling thread has created so far.
+    std::vector<std::shared_ptr<stream_ref>> thread_streams();
+
+    // ------------------------------------------------------- dry run --
+    // True while a plan is being inspected without a device (placeholder
+    // tensors); never set on the execution path.
+    bool placeholder_mode();
+
+} // namespace porch::detail
+
+namespace porch::cuda_jit {
+
+    struct device_buffer_state {
+        int device = 0;
+        uint64_t ptr = 0;
+        size_t bytes = 0;
+        std::mutex mutex;
+        std::shared_ptr<detail::stream_ref> producer;
+        std::vector<std::shared_ptr<detail::stream_ref>> readers;
+
+        device_buffer_state() = default;
+        device_buffer_state(const device_buffer_state&) = delete;
+        device_buffer_state& operator=(const device_buffer_state&) = delete;
+        ~device_buffer_state();
+    };
+
+    struct buffer_access {
+        static const std::shared_ptr<device_buffer_state>& state(
+            const device_buffer& buffer
+        ) {
+            return buffer.state_;
+        }
+        static device_buffer wrap(std::shared_ptr<device_buffer_state> state) {
+            device_buffer b;
+            b.state_ = std::move(state);
+            return b;
+        }
+    };
+
+} // namespace porch::cuda_jit
+
+namespace porch::detail {
+
+    // Allocates `bytes` on `device`, stream-ordered on `stream`.
+    cuda_jit::device_buffer allocate(
+        int device, size_t bytes, const std::shared_ptr<stream_ref>& stream
+    );
+    // Makes `stream` wait for the buffer's producer when they differ, and
+    // records `stream` as a reader so the eventual free is ordered after it.
+    void order_read(
+        cuda_jit::device_buffer_state& buffer,
+        const std::shared_ptr<stream_ref>& stream
+    );
+    void set_producer(
+        cuda_jit::device_buffer_state& buffer, std::shared_ptr<stream_ref> stream
+    );
+
+    // Realised storage of a tensor: device values plus a lazily filled host
+    // mirror (the reference zero-fills a host vector of numel floats twice per
+    // materialisation, src/tensor.cpp:1019 and :1073-1076; here the mirror is
+    // allocated only when data()/cpu() is called).
+    struct realized_storage {
+        cuda_jit::device_buffer device_values;
+        size_t count = 0;
+        int device = 0;
+        std::mutex host_mutex;
+        std::vector<float32_t> host;
+        bool host_current = false;
+        bool placeholder = false; // shape-only tensor for plan inspection
+    };
+
+    enum class expr_kind : uint8_t {
+        input,
+        scalar,
+        add,
+        subtract,
+        multiply,
+        divide,
+        matmul,
+        slice,
+        reshape,
+        unsqueeze,
+        transpose,
+        broadcast,
+        concat,
+        sum,
+        max,
+        maximum,
+        minimum,
+        exp,
+        reciprocal,
+    };
+
+    const char* kind_name(expr_kind kind);
+
+} // namespace porch::detail
+
+namespace porch {
+
+    // IR node. Same 19 kinds and parameters as the reference
+    // (src/tensor.cpp:26-60), except that an input holds shared ownership of
+    // the realised storage instead of a raw `const tensor*`.
+    struct tensor_expr::node {
+        detail::expr_kind kind = detail::expr_kind::scalar;
+        std::shared_ptr<detail::realized_storage> storage; // input
+        std::vector<index_t> input_shape;                  // input
+        device placement{};                                // input
+        float32_t scalar = 0.0F;
+        std::shared_ptr<const node> lhs;
+        std::shared_ptr<const node> rhs;
+        std::vector<index_t> slice_shape;
+        std::vector<index_t> slice_strides;
+        std::vector<index_t> shape; // reshape / broadcast target
+        index_t slice_offset = 0;
+        size_t axis = 0;
+        bool keepdim = false;
+    };
+
+    struct expr_access {
+        static const std::shared_ptr<const tensor_expr::node>& root(
+            const tensor_expr& e
+        ) {
+            return e.root_;
+        }
+        static tensor_expr make(std::shared_ptr<const tensor_expr::node> n) {
+            return tensor_expr{std::move(n)};
+        }
+    };
+
+    struct index_access {
+        static int kind(const tensor_index& i) {
+            return static_cast<int>(i.kind_);
+        }
+        static index_t index(const tensor_index& i) { return i.index_; }
+        static slice range(const tensor_index& i) { return i.slice_; }
+    };
+
+    // Internal access to tensor state for the C-ABI binding and the planner.
+    struct tensor_access {
+        static tensor from_storage(
+            std::vector<index_t> shape,
+            std::shared_ptr<detail::realized_storage> storage, device placement
+        );
+        static std::shared_ptr<detail::realized_storage> storage(
+            const tensor& t
+        );
+        static bool is_lazy(const tensor& t);
+        static tensor placeholder(std::vector<index_t> shape, device placement);
+    };
+
+} // namespace porch
+
+namespace porch::detail {
+
+    // Shape inference with the reference's validation and messages
+    // (src/tensor.cpp:279-496). Returns false for scalar expressions.
+    struct shape_info {
+        std::vector<index_t> shape;
+        bool scalar = true;
+        bool has_input = false;
+        device placement{};
+    };
+    shape_info infer(const tensor_expr::node& root);
+
+    size_t checked_numel(std::span<const index_t> shape);
+    std::vector<index_t> contiguous_strides(std::span<const index_t> shape);
+
+    // Lower, compile and launch `root`; the result is a realised tensor on the
+    // graph's device (src/tensor.cpp:1002-1066 is the reference's driver).
+    tensor materialize_graph(const tensor_expr::node& root);
+
+    // Human-readable description of the plan chosen for `root` (kernels,
+    // schedules and generated sources). Works on placeholder inputs without a
+    // device, so the lowering can be inspected on a build machine.
+    std::string describe_plan(const tensor_expr::node& root, bool with_source);
+
+} // namespace porch::detail

@@ -1,0 +1,338 @@
+// Graph canonicalisation, the plan cache and plan execution.
+//
+// Reference counterpart: materialize_expression (src/tensor.cpp:1002-1066),
+// which re-runs shape inference and code emission and recompiles (cache
+// lookup by full source text) on every call, allocates a zero-filled host
+// vector of numel floats, and loads the PTX module on every launch. Here a
+// repeat graph costs one hash walk, the stream-ordered allocations and the
+// launches.
+#include "plan.hpp"
+
+#include <cstring>
+#include <sstream>
+#include <stdexcept>
+#include <unordered_map>
+
+namespace porch::detail {
+
+    namespace {
+
+        uint64_t mix(uint64_t h, uint64_t v) {
+            h ^= v + 0x9e3779b97f4a7c15ULL + (h << 6) + (h >> 2);
+            return h;
+        }
+
+        struct canonicalizer {
+            graph g;
+            std::unordered_map<const tensor_expr::node*, int> memo;
+            std::map<std::string, int> numbering;
+            std::unordered_map<const realized_storage*, int> slot_of;
+
+            int visit(const tensor_expr::node& n) {
+                auto it = memo.find(&n);
+                if (it != memo.end()) return it->second;
+                gnode gn;
+                gn.kind = n.kind;
+                if (n.lhs) gn.a = visit(*n.lhs);
+                if (n.rhs) gn.b = visit(*n.rhs);
+                std::string key;
+                key.reserve(64);
+                auto put = [&](const void* p, size_t s) {
+                    key.append(static_cast<const char*>(p), s);
+                };
+                auto put_i = [&](int64_t v) { put(&v, sizeof v); };
+                auto put_v = [&](const std::vector<index_t>& v) {
+                    put_i(static_cast<int64_t>(v.size()));
+                    for (index_t x : v) put_i(x);
+                };
+                put_i(static_cast<int64_t>(n.kind));
+                put_i(gn.a);
+                put_i(gn.b);
+                switch (n.kind) {
+                    case expr_kind::input: {
+                        auto s = slot_of.find(n.storage.get());
+                        if (s == slot_of.end()) {
+                            const int slot = static_cast<int>(g.slots.size());
+                            slot_of.emplace(n.storage.get(), slot);
+                            g.slots.push_back(n.storage);
+                            g.slot_shapes.push_back(n.input_shape);
+                            gn.slot = slot;
+                        } else {
+                            gn.slot = s->second;
+                        }
+                        put_i(gn.slot);
+                        put_v(n.input_shape);
+                        gn.shape = n.input_shape;
+                        break;
+                    }
+                    case expr_kind::scalar: {
+                        gn.scalar = n.scalar;
+                        gn.is_scalar = true;
+                        uint32_t bits = 0;
+                        std::memcpy(&bits, &n.scalar, 4);
+                        put_i(bits);
+                        break;
+                    }
+                    case expr_kind::slice:
+                        gn.p_shape = n.slice_shape;
+                        gn.p_strides = n.slice_strides;
+                        gn.p_offset = n.slice_offset;
+                        put_v(gn.p_shape);
+                        put_v(gn.p_strides);
+                        put_i(gn.p_offset);
+                        break;
+                    case expr_kind::reshape:
+                    case expr_kind::broadcast:
+                        gn.p_shape = n.shape;
+                        put_v(gn.p_shape);
+                        break;
+                    case expr_kind::unsqueeze:
+                    case expr_kind::concat:
+                    case expr_kind::sum:
+                    case expr_kind::max:
+                        gn.axis = n.axis;
+                        gn.keepdim = n.keepdim;
+                        put_i(static_cast<int64_t>(n.axis));
+                        put_i(n.keepdim ? 1 : 0);
+                        break;
+                    default:
+                        break;
+                }
+                auto num = numbering.find(key);
+                if (num != numbering.end()) {
+                    memo.emplace(&n, num->second);
+                    return num->second;
+                }
+                shape_of(gn);
+                const int id = static_cast<int>(g.nodes.size());
+                g.nodes.push_back(std::move(gn));
+                g.uses.push_back(0);
+                if (g.nodes[id].a >= 0) ++g.uses[g.nodes[id].a];
+                if (g.nodes[id].b >= 0) ++g.uses[g.nodes[id].b];
+                g.hash = mix(g.hash, std::hash<std::string>{}(key));
+                g.key += key;
+                numbering.emplace(std::move(key), id);
+                memo.emplace(&n, id);
+                return id;
+            }
+
+            // Output shape of an already-validated node.
+            void shape_of(gnode& n) {
+                const gnode* a = n.a >= 0 ? &g.nodes[n.a] : nullptr;
+                const gnode* b = n.b >= 0 ? &g.nodes[n.b] : nullptr;
+                switch (n.kind) {
+                    case expr_kind::input:
+                        n.is_scalar = false;
+                        return;
+                    case expr_kind::scalar:
+                        n.is_scalar = true;
+                        return;
+                    case expr_kind::add:
+                    case expr_kind::subtract:
+                    case expr_kind::multiply:
+                    case expr_kind::divide:
+                    case expr_kind::maximum:
+                    case expr_kind::minimum: {
+                        const gnode* t = a->is_scalar ? b : a;
+                        n.is_scalar = t->is_scalar;
+                        n.shape = t->shape;
+                        return;
+                    }
+                    case expr_kind::exp:
+                    case expr_kind::reciprocal:
+                        n.is_scalar = a->is_scalar;
+                        n.shape = a->shape;
+                        return;
+                    case expr_kind::matmul:
+                        n.shape = {a->shape[0], b->shape[1]};
+                        return;
+                    case expr_kind::slice:
+                        n.shape = n.p_shape;
+                        return;
+                    case expr_kind::reshape:
+                    case expr_kind::broadcast:
+                        n.shape = n.p_shape;
+                        return;
+                    case expr_kind::unsqueeze:
+                        n.shape = a->shape;
+                        n.shape.insert(n.shape.begin() + static_cast<ptrdiff_t>(n.axis), 1);
+                        return;
+                    case expr_kind::transpose:
+                        n.shape = {a->shape[1], a->shape[0]};
+                        return;
+                    case expr_kind::concat:
+                        n.shape = a->shape;
+                        n.shape[n.axis] += b->shape[n.axis];
+                        return;
+                    case expr_kind::sum:
+                    case expr_kind::max: {
+                        if (n.keepdim) {
+                            n.shape = a->shape;
+                            n.shape[n.axis] = 1;
+                        } else {
+                            for (size_t d = 0; d < a->shape.size(); ++d)
+                                if (d != n.axis) n.shape.push_back(a->shape[d]);
+                            if (n.shape.empty()) n.shape.push_back(1);
+                        }
+                        return;
+                    }
+                }
+            }
+        };
+
+        struct plan_cache {
+            std::mutex mutex;
+            std::unordered_map<uint64_t, std::vector<std::pair<std::string, std::shared_ptr<plan>>>>
+                plans;
+        };
+
+        plan_cache& plans() {
+            static plan_cache* c = new plan_cache();
+            return *c;
+        }
+
+        std::shared_ptr<plan> lookup_plan(const graph& g) {
+            const std::string& key = g.key;
+            plan_cache& c = plans();
+            {
+                std::scoped_lock lock{c.mutex};
+                auto it = c.plans.find(g.hash);
+                if (it != c.plans.end()) {
+                    for (auto& [k, p] : it->second)
+                        if (k == key) return p;
+                }
+            }
+            std::shared_ptr<plan> p = build_plan(g);
+            std::scoped_lock lock{c.mutex};
+            c.plans[g.hash].emplace_back(key, p);
+            return p;
+        }
+
+    } // namespace
+
+    graph canonicalize(const tensor_expr::node& root) {
+        canonicalizer c;
+        c.g.hash = 0x6a09e667f3bcc909ULL;
+        c.g.root = c.visit(root);
+        c.g.hash = mix(c.g.hash, static_cast<uint64_t>(c.g.root));
+        c.g.key += "|root=" + std::to_string(c.g.root);
+        return std::move(c.g);
+    }
+
+    bool placeholder_mode() { return false; }
+
+    tensor materialize_graph(const tensor_expr::node& root) {
+        shape_info info = infer(root);
+        if (!info.has_input)
+            throw std::invalid_argument("tensor expression must reference at least one tensor");
+        if (info.scalar)
+            throw std::invalid_argument("scalar expression cannot materialize to a tensor");
+
+        const size_t count = checked_numel(info.shape);
+        graph g = canonicalize(root);
+        int device = -1;
+        for (const auto& s : g.slots) {
+            if (s->placeholder)
+                throw std::runtime_error(
+                    "placeholder tensors can only be used to describe plans");
+            if (device < 0) device = s->device;
+        }
+        if (device < 0) device = 0;
+
+        auto storage = std::make_shared<realized_storage>();
+        storage->count = count;
+        storage->device = device;
+        auto stream = current_stream(device);
+        if (count == 0) {
+            // Empty result: no launch (src/tensor.cpp:1023-1028).
+            storage->device_values = allocate(device, 0, stream);
+            storage->host_current = true;
+            return tensor_access::from_storage(std::move(info.shape), std::move(storage),
+                                               info.placement);
+        }
+
+        std::shared_ptr<plan> p = lookup_plan(g);
+
+        for (const auto& s : g.slots) {
+            const auto& st = cuda_jit::buffer_access::state(s->device_values);
+            if (st == nullptr || st->ptr == 0)
+                throw std::invalid_argument("CUDA elementwise input is empty");
+            if (st->device != device)
+                throw std::invalid_argument("tensor expression devices must match");
+            order_read(*st, stream);
+        }
+
+        std::vector<cuda_jit::device_buffer> temps;
+        temps.reserve(p->temp_bytes.size());
+        for (size_t bytes : p->temp_bytes) temps.push_back(allocate(device, bytes, stream));
+
+        uint64_t error_word = 0;
+        std::vector<uint64_t> values;
+        std::vector<void*> params;
+        for (launch_spec& l : p->launches) {
+            pbrt_function fn = nullptr;
+            if (device < static_cast<int>(l.functions.size())) fn = l.functions[device];
+            if (fn == nullptr) {
+                std::scoped_lock lock{p->resolve_mutex};
+                check(pbrt_get_function(device, l.image_key, l.name.c_str(), &fn));
+                if (l.smem > 48 * 1024)
+                    check(pbrt_function_set_max_dynamic_smem(fn, static_cast<int>(l.smem)));
+                if (device < static_cast<int>(l.functions.size())) l.functions[device] = fn;
+            }
+            values.assign(l.args.size(), 0);
+            params.assign(l.args.size(), nullptr);
+            for (size_t i = 0; i < l.args.size(); ++i) {
+                const kernel_arg& a = l.args[i];
+                switch (a.kind) {
+                    case arg_kind::slot:
+                        values[i] = cuda_jit::buffer_access::state(
+                                        g.slots[static_cast<size_t>(a.index)]->device_values)
+                                        ->ptr;
+                        break;
+                    case arg_kind::temp:
+                        values[i] = cuda_jit::buffer_access::state(
+                                        temps[static_cast<size_t>(a.index)])
+                                        ->ptr;
+                        break;
+                    case arg_kind::error_word:
+                        if (error_word == 0) check(pbrt_error_word(device, &error_word));
+                        values[i] = error_word;
+                        break;
+                    case arg_kind::u64:
+                        values[i] = a.value;
+                        break;
+                }
+                params[i] = &values[i];
+            }
+            check(pbrt_launch(device, fn, l.grid.data(), l.block.data(), l.smem,
+                              stream->stream, params.data(), nullptr));
+        }
+
+        storage->device_values = temps[static_cast<size_t>(p->result_temp)];
+        set_producer(*cuda_jit::buffer_access::state(storage->device_values), stream);
+        return tensor_access::from_storage(std::move(info.shape), std::move(storage),
+                                           info.placement);
+    }
+
+    std::string describe_plan(const tensor_expr::node& root, bool with_source) {
+        shape_info info = infer(root);
+        if (!info.has_input)
+            throw std::invalid_argument("tensor expression must reference at least one tensor");
+        if (info.scalar)
+            throw std::invalid_argument("scalar expression cannot materialize to a tensor");
+        graph g = canonicalize(root);
+        std::shared_ptr<plan> p = lookup_plan(g);
+        std::ostringstream os;
+        os << "graph nodes=" << g.nodes.size() << " slots=" << g.slots.size()
+           << " hash=" << std::hex << g.hash << std::dec << "\n";
+        os << "temps=" << p->temp_bytes.size() << " result=t" << p->result_temp << "\n";
+        for (const launch_spec& l : p->launches) {
+            os << "kernel " << l.name << " grid=" << l.grid[0] << "x" << l.grid[1] << "x"
+               << l.grid[2] << " block=" << l.block[0] << " smem=" << l.smem << " : "
+               << l.schedule << "\n";
+            if (with_source) os << l.source << "\n";
+        }
+        return os.str();
+    }
+
+} // namespace porch::detail

@@ -1,0 +1,318 @@
+// porch::cuda_jit public API (include/porch/cuda_jit.hpp) and the stream /
+// buffer plumbing used by the front-end, on top of the runtime C-ABI.
+//
+// Differences from the reference's src/cuda_jit.cpp that matter on B200:
+//  - cross-stream dependencies are stream waits on events, not host
+//    synchronisations of the producer stream (src/cuda_jit.cpp:809-813);
+//  - a buffer's stream-ordered free is ordered after every foreign reader;
+//  - PTX given to launch_* is loaded once per (device, image) instead of
+//    cuModuleLoadData on every launch (src/cuda_jit.cpp:819-823).
+#include "detail.hpp"
+
+#include <cstring>
+#include <map>
+#include <sstream>
+#include <stdexcept>
+
+namespace porch::detail {
+
+    [[noreturn]] void throw_status(int status) {
+        std::string message = pbrt_last_error();
+        switch (status) {
+            case PBRT_ERR_INVALID:
+                throw std::invalid_argument(message);
+            case PBRT_ERR_RANGE:
+                throw std::out_of_range(message);
+            case PBRT_ERR_COMPILE:
+                throw cuda_jit::compilation_error(message);
+            default:
+                throw std::runtime_error(message);
+        }
+    }
+
+    stream_ref::~stream_ref() {
+        if (stream == nullptr) return;
+        (void)pbrt_stream_synchronize(device, stream);
+        (void)pbrt_stream_destroy(device, stream);
+    }
+
+    namespace {
+        struct thread_stream_table {
+            std::vector<std::shared_ptr<stream_ref>> streams;
+        };
+        thread_local thread_stream_table tl_streams;
+    } // namespace
+
+    std::shared_ptr<stream_ref> current_stream(int device) {
+        auto& table = tl_streams.streams;
+        if (device < 0)
+            throw std::invalid_argument("CUDA device ordinal must be non-negative");
+        if (table.size() <= static_cast<size_t>(device))
+            table.resize(static_cast<size_t>(device) + 1);
+        std::shared_ptr<stream_ref>& slot = table[static_cast<size_t>(device)];
+        if (slot == nullptr) {
+            pbrt_stream s = nullptr;
+            check(pbrt_stream_create(device, &s));
+            slot = std::make_shared<stream_ref>(device, s);
+        }
+        return slot;
+    }
+
+    std::vector<std::shared_ptr<stream_ref>> thread_streams() {
+        std::vector<std::shared_ptr<stream_ref>> out;
+        for (const auto& s : tl_streams.streams)
+            if (s != nullptr) out.push_back(s);
+        return out;
+    }
+
+    cuda_jit::device_buffer allocate(
+        int device, size_t bytes, const std::shared_ptr<stream_ref>& stream
+    ) {
+        auto state = std::make_shared<cuda_jit::device_buffer_state>();
+        state->device = device;
+        state->bytes = bytes;
+        if (bytes != 0) {
+            check(pbrt_mem_alloc_async(device, bytes, stream->stream, &state->ptr));
+            state->producer = stream;
+        }
+        return cuda_jit::buffer_access::wrap(std::move(state));
+    }
+
+    void order_read(
+        cuda_jit::device_buffer_state& buffer,
+        const std::shared_ptr<stream_ref>& stream
+    ) {
+        std::shared_ptr<stream_ref> producer;
+        {
+            std::scoped_lock lock{buffer.mutex};
+            producer = buffer.producer;
+            if (producer == nullptr || producer == stream) return;
+            bool known = false;
+            for (const auto& r : buffer.readers) known = known || r == stream;
+            if (!known) buffer.readers.push_back(stream);
+        }
+        if (producer->device == stream->device) {
+            pbrt_event e = nullptr;
+            check(pbrt_event_create(producer->device, 0, &e));
+            check(pbrt_event_record(producer->device, e, producer->stream));
+            check(pbrt_stream_wait_event(stream->device, stream->stream, e));
+            (void)pbrt_event_destroy(producer->device, e);
+        } else {
+            // Different devices: the reader copies or loads over NVLink; keep
+            // it simple and exact by draining the producer first.
+            check(pbrt_stream_synchronize(producer->device, producer->stream));
+        }
+    }
+
+    void set_producer(
+        cuda_jit::device_buffer_state& buffer, std::shared_ptr<stream_ref> stream
+    ) {
+        std::scoped_lock lock{buffer.mutex};
+        buffer.producer = std::move(stream);
+    }
+
+} // namespace porch::detail
+
+namespace porch::cuda_jit {
+
+    device_buffer_state::~device_buffer_state() {
+        if (ptr == 0) return;
+        try {
+            std::shared_ptr<detail::stream_ref> free_stream =
+                producer != nullptr ? producer : detail::current_stream(device);
+            // Order the free after every reader on another stream.
+            for (const auto& reader : readers) {
+                if (reader == free_stream) continue;
+                pbrt_event e = nullptr;
+                if (pbrt_event_create(reader->device, 0, &e) != PBRT_OK) continue;
+                (void)pbrt_event_record(reader->device, e, reader->stream);
+                (void)pbrt_stream_wait_event(free_stream->device, free_stream->stream, e);
+                (void)pbrt_event_destroy(reader->device, e);
+            }
+            (void)pbrt_mem_free_async(device, ptr, free_stream->stream);
+        } catch (...) {
+        }
+    }
+
+    device_buffer::device_buffer(size_t bytes) {
+        if (bytes == 0) return;
+        *this = detail::allocate(0, bytes, detail::current_stream(0));
+    }
+
+    bool device_buffer::empty() const noexcept {
+        return state_ == nullptr || state_->bytes == 0;
+    }
+
+    size_t device_buffer::size_bytes() const noexcept {
+        return state_ == nullptr ? 0 : state_->bytes;
+    }
+
+    compilation_error::compilation_error(std::string log)
+        : std::runtime_error(log), log_(std::move(log)) {}
+
+    const std::string& compilation_error::log() const noexcept { return log_; }
+
+    bool is_available() noexcept { return pbrt_available() == 1; }
+
+    std::string compile_to_ptx(
+        std::string_view source, const std::vector<std::string>& options
+    ) {
+        std::vector<const char*> opts;
+        opts.reserve(options.size());
+        for (const std::string& o : options) opts.push_back(o.c_str());
+        const std::string text{source};
+        uint64_t key = 0;
+        detail::check(pbrt_compile(text.c_str(), opts.empty() ? nullptr : opts.data(),
+                                   static_cast<int>(opts.size()), 0, &key));
+        const void* image = nullptr;
+        size_t size = 0;
+        detail::check(pbrt_compiled_image(key, &image, &size));
+        std::string ptx(static_cast<const char*>(image), size);
+        while (!ptx.empty() && ptx.back() == '\0') ptx.pop_back();
+        return ptx;
+    }
+
+    namespace {
+        void require_device_bytes(
+            const device_buffer& buffer, size_t bytes, const char* name
+        ) {
+            if (buffer.size_bytes() < bytes)
+                throw std::invalid_argument(
+                    std::string{name} + " device buffer is too small"
+                );
+        }
+    } // namespace
+
+    device_buffer make_device_buffer(std::span<const float32_t> source) {
+        device_buffer buffer{source.size_bytes()};
+        copy_to_device(buffer, source);
+        return buffer;
+    }
+
+    void copy_to_device(device_buffer& buffer, std::span<const float32_t> source) {
+        if (source.empty()) return;
+        require_device_bytes(buffer, source.size_bytes(), "target");
+        device_buffer_state& st = *buffer.state_;
+        auto stream = detail::current_stream(st.device);
+        detail::order_read(st, stream);
+        detail::check(pbrt_memcpy_h2d_async(st.device, st.ptr, source.data(),
+                                            source.size_bytes(), stream->stream));
+        // The source span may be pageable and short-lived: complete the copy
+        // before returning, as the reference does (src/cuda_jit.cpp:729-732).
+        detail::check(pbrt_stream_synchronize(st.device, stream->stream));
+        detail::set_producer(st, stream);
+    }
+
+    void copy_to_host(const device_buffer& buffer, std::span<float32_t> target) {
+        if (target.empty()) return;
+        require_device_bytes(buffer, target.size_bytes(), "source");
+        device_buffer_state& st = *buffer.state_;
+        auto stream = detail::current_stream(st.device);
+        detail::order_read(st, stream);
+        detail::check(pbrt_memcpy_d2h_async(st.device, target.data(), st.ptr,
+                                            target.size_bytes(), stream->stream));
+        detail::check(pbrt_stream_synchronize(st.device, stream->stream));
+        int code = 0;
+        detail::check(pbrt_error_check(st.device, stream->stream, &code));
+    }
+
+    void synchronize() {
+        // Drain this thread's streams on every device it has used (the
+        // reference has one device and syncs its one thread-local stream,
+        // src/cuda_jit.cpp:761).
+        for (const auto& stream : detail::thread_streams()) {
+            detail::check(pbrt_stream_synchronize(stream->device, stream->stream));
+            int code = 0;
+            detail::check(pbrt_error_check(stream->device, stream->stream, &code));
+        }
+    }
+
+    namespace {
+        // User-supplied PTX launch (drop-in for the reference's launch_*,
+        // src/cuda_jit.cpp:789-948): same grid conventions, same checks.
+        void launch_ptx(
+            std::string_view ptx, std::string_view function,
+            const std::vector<const device_buffer*>& inputs, device_buffer& out,
+            size_t count, bool reduction
+        ) {
+            if (count == 0) return;
+            const char* what = reduction ? "CUDA reduction input" : "CUDA elementwise input";
+            for (const device_buffer* input : inputs) {
+                if (input == nullptr) throw std::invalid_argument(std::string{what} + " is null");
+                if (input->empty()) throw std::invalid_argument(std::string{what} + " is empty");
+            }
+            require_device_bytes(out, count * sizeof(float32_t), "out");
+            device_buffer_state& ost = *buffer_access::state(out);
+            const int device = ost.device;
+            auto stream = detail::current_stream(device);
+            for (const device_buffer* input : inputs)
+                detail::order_read(*buffer_access::state(*input), stream);
+            detail::order_read(ost, stream);
+
+            const std::string text{ptx};
+            uint64_t key = 0;
+            detail::check(pbrt_register_image(text.c_str(), text.size() + 1, &key));
+            pbrt_function fn = nullptr;
+            const std::string name{function};
+            detail::check(pbrt_get_function(device, key, name.c_str(), &fn));
+
+            std::vector<uint64_t> ptrs;
+            ptrs.reserve(inputs.size());
+            for (const device_buffer* input : inputs) ptrs.push_back(buffer_access::state(*input)->ptr);
+            uint64_t out_ptr = ost.ptr;
+            uint64_t n = count;
+            std::vector<void*> params;
+            for (uint64_t& p : ptrs) params.push_back(&p);
+            params.push_back(&out_ptr);
+            params.push_back(&n);
+            const uint32_t block[3] = {256, 1, 1};
+            const uint32_t grid[3] = {
+                reduction ? static_cast<uint32_t>(count)
+                          : static_cast<uint32_t>((count + 255) / 256),
+                1, 1};
+            detail::check(pbrt_launch(device, fn, grid, block, 0, stream->stream,
+                                      params.data(), nullptr));
+            detail::set_producer(ost, stream);
+        }
+    } // namespace
+
+    void launch_elementwise_binary(
+        std::string_view ptx, std::string_view function,
+        std::span<const float32_t> lhs, std::span<const float32_t> rhs,
+        std::span<float32_t> out
+    ) {
+        if (lhs.size() != rhs.size() || lhs.size() != out.size())
+            throw std::invalid_argument("CUDA elementwise operands must match");
+        device_buffer device_lhs = make_device_buffer(lhs);
+        device_buffer device_rhs = make_device_buffer(rhs);
+        device_buffer device_out{out.size_bytes()};
+        launch_elementwise_binary(ptx, function, device_lhs, device_rhs, device_out,
+                                  out.size());
+        copy_to_host(device_out, out);
+    }
+
+    void launch_elementwise_binary(
+        std::string_view ptx, std::string_view function, const device_buffer& lhs,
+        const device_buffer& rhs, device_buffer& out, size_t count
+    ) {
+        std::vector<const device_buffer*> inputs{&lhs, &rhs};
+        launch_ptx(ptx, function, inputs, out, count, false);
+    }
+
+    void launch_fused_elementwise(
+        std::string_view ptx, std::string_view function,
+        const std::vector<const device_buffer*>& inputs, device_buffer& out,
+        size_t count
+    ) {
+        launch_ptx(ptx, function, inputs, out, count, false);
+    }
+
+    void launch_fused_reduction(
+        std::string_view ptx, std::string_view function,
+        const std::vector<const device_buffer*>& inputs, device_buffer& out,
+        size_t count
+    ) {
+        launch_ptx(ptx, function, inputs, out, count, true);
+    }
+
+} // namespace porch::cuda_jit

@@ -1,0 +1,1586 @@
+// Lowering of canonical graphs to sm_100a kernel templates.
+//
+// Reference counterpart: lower_nested_reductions + emit_expression +
+// fused_kernel_source / fused_reduction_kernel_source (src/tensor.cpp:498-989).
+// The reference turns every graph into one of two string templates (one
+// thread per output element with 64-bit div/mod index chains, or one
+// 256-thread block per reduced output) and materialises every non-root
+// reduction separately.
+//
+// Here a graph is lowered to a short list of kernels chosen from templates:
+//  - elementwise/view graphs: every leaf access is analysed as an affine map
+//    of the output coordinates. concat splits the output into boxes, each
+//    box with its own maps. A box whose leaves stream along the innermost
+//    output dimension runs the ROW schedule (128-bit loads/stores, 4 vectors
+//    per thread in flight); a box with a transposed leaf runs the TILE
+//    schedule (64x64 tiles staged through XOR-swizzled shared memory so
+//    both global reads and writes stay coalesced and shared memory is
+//    bank-conflict free). Graphs that are not affine (reshape of an
+//    unaligned slice and the like) fall back to a per-element gather kernel.
+//  - sum/max along an axis: warp-per-row (contiguous axis) or
+//    thread-per-output (strided axis) with the operand expression fused in.
+//  - the ops.hpp softmax shape over the last axis: one single-pass row kernel
+//    (row held in registers: one HBM read and one write), not four kernels.
+//  - matmul: the pending elementwise consumer is fused as the epilogue.
+//    Large aligned shapes use the tcgen05 3xTF32 path (gemm_tc.cpp); the rest
+//    use a tiled CUDA-core kernel whose per-output FMA chain runs in k order,
+//    the same order as the reference's generated loop.
+#include "plan.hpp"
+
+#include "lower.hpp"
+
+#include <algorithm>
+#include <cinttypes>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <functional>
+#include <sstream>
+#include <stdexcept>
+
+namespace porch::detail {
+
+    const std::vector<std::string>& kernel_options() {
+        static const std::vector<std::string> options = {
+            "--gpu-architecture=sm_100a", "-std=c++17", "--fmad=false",
+            "--prec-div=true", "--prec-sqrt=true", "--ftz=false", "-lineinfo",
+            "-DPB_NVRTC=1"};
+        return options;
+    }
+
+    std::string float_literal(float v) {
+        uint32_t bits = 0;
+        std::memcpy(&bits, &v, 4);
+        char buf[64];
+        if (std::isfinite(v)) {
+            std::snprintf(buf, sizeof buf, "%af", static_cast<double>(v));
+        } else {
+            std::snprintf(buf, sizeof buf, "__int_as_float(0x%08xu)", bits);
+        }
+        return buf;
+    }
+
+    const char* kernel_prelude() {
+        return R"PB(
+typedef unsigned int pb_u32;
+typedef unsigned long long pb_u64;
+#define PB_NEG_FLT_MAX (-3.4028234663852886e+38f)
+static __device__ __forceinline__ float4 pb_ld4(const float* p) {
+    return __ldg(reinterpret_cast<const float4*>(p));
+}
+static __device__ __forceinline__ float pb_ld(const float* p) { return __ldg(p); }
+static __device__ __forceinline__ void pb_st4(float* p, float4 v) {
+    *reinterpret_cast<float4*>(p) = v;
+}
+static __device__ __forceinline__ float pb_get(const float4& v, int e) {
+    return e == 0 ? v.x : (e == 1 ? v.y : (e == 2 ? v.z : v.w));
+}
+)PB";
+    }
+
+    namespace {
+
+        // ------------------------------------------------------ helpers --
+        std::string lit(int64_t v, bool wide) {
+            if (wide) return "((pb_u64)(" + std::to_string(v) + "ll))";
+            return "((pb_u32)(" + std::to_string(v) + "ll))";
+        }
+
+        std::string hex64(uint64_t v) {
+            char b[32];
+            std::snprintf(b, sizeof b, "%016" PRIx64, v);
+            return b;
+        }
+
+        uint64_t hash_string(const std::string& s) {
+            uint64_t h = 0xcbf29ce484222325ULL;
+            for (unsigned char c : s) {
+                h ^= c;
+                h *= 0x100000001b3ULL;
+            }
+            return h;
+        }
+
+    } // namespace
+
+    // ============================================================ lowerer ==
+    lowerer::lowerer(const graph& g, plan& p) : g_(g), p_(p) {}
+
+    int lowerer::new_temp(size_t bytes) {
+        p_.temp_bytes.push_back(bytes == 0 ? 4 : bytes);
+        return static_cast<int>(p_.temp_bytes.size()) - 1;
+    }
+
+    int lowerer::kernel::leaf(arg_kind kind, int index) {
+        for (size_t i = 0; i < leaves.size(); ++i)
+            if (leaves[i].kind == kind && leaves[i].index == index) return static_cast<int>(i);
+        kernel_arg a;
+        a.kind = kind;
+        a.index = index;
+        leaves.push_back(a);
+        return static_cast<int>(leaves.size()) - 1;
+    }
+
+    bool lowerer::match_softmax(int id, int& x, size_t& axis) const {
+        const gnode& n = g_.nodes[static_cast<size_t>(id)];
+        if (n.kind != expr_kind::divide || n.a < 0 || n.b < 0) return false;
+        const gnode& den = g_.nodes[static_cast<size_t>(n.b)];
+        if (den.kind != expr_kind::broadcast) return false;
+        const gnode& s = g_.nodes[static_cast<size_t>(den.a)];
+        if (s.kind != expr_kind::sum || !s.keepdim || s.a != n.a) return false;
+        const gnode& num = g_.nodes[static_cast<size_t>(n.a)];
+        if (num.kind != expr_kind::exp) return false;
+        const gnode& sub = g_.nodes[static_cast<size_t>(num.a)];
+        if (sub.kind != expr_kind::subtract) return false;
+        const gnode& bm = g_.nodes[static_cast<size_t>(sub.b)];
+        if (bm.kind != expr_kind::broadcast) return false;
+        const gnode& m = g_.nodes[static_cast<size_t>(bm.a)];
+        if (m.kind != expr_kind::max || !m.keepdim || m.a != sub.a || m.axis != s.axis)
+            return false;
+        const gnode& xv = g_.nodes[static_cast<size_t>(sub.a)];
+        if (xv.is_scalar) return false;
+        if (den.p_shape != xv.shape || bm.p_shape != xv.shape) return false;
+        x = sub.a;
+        axis = s.axis;
+        return true;
+    }
+
+    bool lowerer::is_barrier(int id) const {
+        const gnode& n = g_.nodes[static_cast<size_t>(id)];
+        if (n.kind == expr_kind::matmul || n.kind == expr_kind::sum ||
+            n.kind == expr_kind::max)
+            return true;
+        int x = 0;
+        size_t axis = 0;
+        return match_softmax(id, x, axis);
+    }
+
+    // Finds the single matmul whose output feeds `id` through elementwise
+    // ops only (the fusable epilogue). Returns -1 when there is none.
+    int lowerer::match_gemm(int id) const {
+        const gnode& root = g_.nodes[static_cast<size_t>(id)];
+        if (root.is_scalar || root.shape.size() != 2) return -1;
+        int found = -1;
+        bool ambiguous = false;
+        std::function<void(int)> walk = [&](int v) {
+            const gnode& n = g_.nodes[static_cast<size_t>(v)];
+            switch (n.kind) {
+                case expr_kind::matmul:
+                    if (n.shape == root.shape) {
+                        if (found >= 0 && found != v) ambiguous = true;
+                        found = v;
+                    }
+                    return;
+                case expr_kind::add:
+                case expr_kind::subtract:
+                case expr_kind::multiply:
+                case expr_kind::divide:
+                case expr_kind::maximum:
+                case expr_kind::minimum:
+                    walk(n.a);
+                    walk(n.b);
+                    return;
+                case expr_kind::exp:
+                case expr_kind::reciprocal:
+                    walk(n.a);
+                    return;
+                default:
+                    return;
+            }
+        };
+        walk(id);
+        if (ambiguous) return -1;
+        return found;
+    }
+
+    int lowerer::materialize(int id) {
+        auto it = done_.find(id);
+        if (it != done_.end()) return it->second;
+        // Nested lowering (a barrier met while building an outer kernel)
+        // must not disturb the outer kernel's coordinate rank.
+        struct rank_guard {
+            int& r;
+            int saved;
+            ~rank_guard() { r = saved; }
+        } guard{rank_, rank_};
+        const gnode& n = g_.nodes[static_cast<size_t>(id)];
+        int t = -1;
+        int x = 0;
+        size_t axis = 0;
+        if (match_softmax(id, x, axis) && axis + 1 == n.shape.size()) {
+            t = emit_softmax(id, x);
+        } else if (n.kind == expr_kind::sum || n.kind == expr_kind::max) {
+            t = emit_reduce(id);
+        } else {
+            const int mm = match_gemm(id);
+            if (mm >= 0) t = emit_gemm(id, mm);
+            if (t < 0) t = emit_elementwise(id);
+        }
+        done_[id] = t;
+        return t;
+    }
+
+    // Operand of a matmul or reduction as a realised contiguous buffer.
+    kernel_arg lowerer::as_buffer(int id) {
+        const gnode& n = g_.nodes[static_cast<size_t>(id)];
+        kernel_arg a;
+        if (n.kind == expr_kind::input) {
+            a.kind = arg_kind::slot;
+            a.index = n.slot;
+        } else {
+            a.kind = arg_kind::temp;
+            a.index = materialize(id);
+        }
+        return a;
+    }
+
+    // ================================================= affine analysis ==
+    std::string lowerer::pos_key(const position& p) {
+        std::string k = p.linear ? "L" : "C";
+        auto put = [&](const affine& a) {
+            k += std::to_string(a.off);
+            for (int64_t s : a.st) k += "," + std::to_string(s);
+            k += ";";
+        };
+        if (p.linear)
+            put(p.lin);
+        else
+            for (const affine& a : p.coords) put(a);
+        return k;
+    }
+
+    affine lowerer::to_linear(const position& p, const std::vector<index_t>& shape) const {
+        if (p.linear) return p.lin;
+        affine r;
+        r.st.assign(static_cast<size_t>(rank_), 0);
+        const std::vector<index_t> cs = contiguous_strides(shape);
+        for (size_t k = 0; k < p.coords.size(); ++k) {
+            r.off += p.coords[k].off * cs[k];
+            for (int d = 0; d < rank_; ++d) r.st[static_cast<size_t>(d)] += p.coords[k].st[static_cast<size_t>(d)] * cs[k];
+        }
+        return r;
+    }
+
+    std::vector<affine> lowerer::to_coords(const position& p, const std::vector<index_t>& shape,
+                                           const box& b) const {
+        if (!p.linear) return p.coords;
+        // Unravel a linear position into the node's coordinates; affine only
+        // when no digit carries inside the box.
+        const size_t R = shape.size();
+        const std::vector<index_t> cs = contiguous_strides(shape);
+        int64_t base = p.lin.off;
+        for (int d = 0; d < rank_; ++d) base += p.lin.st[static_cast<size_t>(d)] * b.lo[static_cast<size_t>(d)];
+        const int64_t numel = static_cast<int64_t>(checked_numel(shape));
+        if (base < 0 || (numel > 0 && base >= numel)) throw not_affine{};
+        std::vector<affine> out(R);
+        std::vector<int64_t> digit(R, 0), reach(R, 0);
+        for (size_t k = 0; k < R; ++k) {
+            digit[k] = shape[k] == 0 ? 0 : (base / cs[k]) % shape[k];
+            out[k].st.assign(static_cast<size_t>(rank_), 0);
+            out[k].off = digit[k];
+        }
+        for (int d = 0; d < rank_; ++d) {
+            const int64_t s = p.lin.st[static_cast<size_t>(d)];
+            const int64_t extent = b.hi[static_cast<size_t>(d)] - b.lo[static_cast<size_t>(d)];
+            if (s == 0 || extent <= 1) continue;
+            if (s < 0) throw not_affine{};
+            size_t k = 0;
+            while (k < R && s % cs[k] != 0) ++k;
+            if (k == R) throw not_affine{};
+            const int64_t m = s / cs[k];
+            out[k].st[static_cast<size_t>(d)] += m;
+            out[k].off -= m * b.lo[static_cast<size_t>(d)];
+            reach[k] += m * (extent - 1);
+        }
+        for (size_t k = 0; k < R; ++k)
+            if (digit[k] + reach[k] >= shape[k]) throw not_affine{};
+        return out;
+    }
+
+    int lowerer::push(box& b, vnode v) {
+        b.nodes.push_back(std::move(v));
+        return static_cast<int>(b.nodes.size()) - 1;
+    }
+
+    int lowerer::build(kernel& k, box& b, int id, const position& pos, int acc_id,
+                       std::map<std::string, int>& memo) {
+        const std::string key = std::to_string(id) + pos_key(pos);
+        auto it = memo.find(key);
+        if (it != memo.end()) return it->second;
+        const gnode& n = g_.nodes[static_cast<size_t>(id)];
+        int out = -1;
+        auto load_from = [&](arg_kind kind, int index) {
+            vnode v;
+            v.kind = vnode::op::load;
+            v.buffer = k.leaf(kind, index);
+            v.map = to_linear(pos, n.shape);
+            return push(b, std::move(v));
+        };
+        if (id == acc_id) {
+            // The GEMM accumulator is only defined at the output position.
+            if (pos.linear) throw not_fusable{};
+            for (int d = 0; d < rank_; ++d) {
+                const affine& a = pos.coords[static_cast<size_t>(d)];
+                if (a.off != 0) throw not_fusable{};
+                for (int e = 0; e < rank_; ++e)
+                    if (a.st[static_cast<size_t>(e)] != (d == e ? 1 : 0)) throw not_fusable{};
+            }
+            vnode v;
+            v.kind = vnode::op::acc;
+            out = push(b, std::move(v));
+            memo.emplace(key, out);
+            return out;
+        }
+        switch (n.kind) {
+            case expr_kind::scalar: {
+                vnode v;
+                v.kind = vnode::op::scalar;
+                v.scalar = n.scalar;
+                out = push(b, std::move(v));
+                break;
+            }
+            case expr_kind::input:
+                out = load_from(arg_kind::slot, n.slot);
+                break;
+            case expr_kind::add:
+            case expr_kind::subtract:
+            case expr_kind::multiply:
+            case expr_kind::divide:
+            case expr_kind::maximum:
+            case expr_kind::minimum: {
+                if (is_barrier(id)) {
+                    out = load_from(arg_kind::temp, materialize(id));
+                    break;
+                }
+                const int l = build(k, b, n.a, pos, acc_id, memo);
+                const int r = build(k, b, n.b, pos, acc_id, memo);
+                vnode v;
+                v.kind = vnode::op::binary;
+                v.ek = n.kind;
+                v.a = l;
+                v.b = r;
+                out = push(b, std::move(v));
+                break;
+            }
+            case expr_kind::exp:
+            case expr_kind::reciprocal: {
+                const int l = build(k, b, n.a, pos, acc_id, memo);
+                vnode v;
+                v.kind = vnode::op::unary;
+                v.ek = n.kind;
+                v.a = l;
+                out = push(b, std::move(v));
+                break;
+            }
+            case expr_kind::matmul:
+            case expr_kind::sum:
+            case expr_kind::max:
+                out = load_from(arg_kind::temp, materialize(id));
+                break;
+            case expr_kind::slice: {
+                const std::vector<affine> c = to_coords(pos, n.shape, b);
+                position child;
+                child.linear = true;
+                child.lin.off = n.p_offset;
+                child.lin.st.assign(static_cast<size_t>(rank_), 0);
+                for (size_t d = 0; d < c.size(); ++d) {
+                    child.lin.off += c[d].off * n.p_strides[d];
+                    for (int e = 0; e < rank_; ++e)
+                        child.lin.st[static_cast<size_t>(e)] += c[d].st[static_cast<size_t>(e)] * n.p_strides[d];
+                }
+                out = build(k, b, n.a, child, acc_id, memo);
+                break;
+            }
+            case expr_kind::reshape:
+            case expr_kind::unsqueeze: {
+                position child;
+                child.linear = true;
+                child.lin = to_linear(pos, n.shape);
+                out = build(k, b, n.a, child, acc_id, memo);
+                break;
+            }
+            case expr_kind::transpose: {
+                const std::vector<affine> c = to_coords(pos, n.shape, b);
+                position child;
+                child.coords = {c[1], c[0]};
+                out = build(k, b, n.a, child, acc_id, memo);
+                break;
+            }
+            case expr_kind::broadcast: {
+                const gnode& src = g_.nodes[static_cast<size_t>(n.a)];
+                if (src.is_scalar) {
+                    out = build(k, b, n.a, pos, acc_id, memo);
+                    break;
+                }
+                const std::vector<affine> c = to_coords(pos, n.shape, b);
+                position child;
+                const size_t off = n.shape.size() - src.shape.size();
+                for (size_t d = 0; d < src.shape.size(); ++d) {
+                    if (src.shape[d] == 1) {
+                        affine z;
+                        z.st.assign(static_cast<size_t>(rank_), 0);
+                        child.coords.push_back(z);
+                    } else {
+                        child.coords.push_back(c[off + d]);
+                    }
+                }
+                out = build(k, b, n.a, child, acc_id, memo);
+                break;
+            }
+            case expr_kind::concat: {
+                const std::vector<affine> c = to_coords(pos, n.shape, b);
+                const size_t ax = n.axis;
+                const int64_t L = g_.nodes[static_cast<size_t>(n.a)].shape[ax];
+                const affine& ca = c[ax];
+                int dim = -1;
+                for (int d = 0; d < rank_; ++d) {
+                    if (ca.st[static_cast<size_t>(d)] == 0) continue;
+                    if (b.hi[static_cast<size_t>(d)] - b.lo[static_cast<size_t>(d)] <= 1) continue;
+                    if (dim >= 0) throw not_affine{};
+                    dim = d;
+                }
+                bool left = false;
+                if (dim < 0) {
+                    int64_t v = ca.off;
+                    for (int d = 0; d < rank_; ++d)
+                        v += ca.st[static_cast<size_t>(d)] * b.lo[static_cast<size_t>(d)];
+                    left = v < L;
+                } else {
+                    const int64_t kk = ca.st[static_cast<size_t>(dim)];
+                    if (kk < 0) throw not_affine{};
+                    int64_t base = ca.off;
+                    for (int d = 0; d < rank_; ++d)
+                        if (d != dim) base += ca.st[static_cast<size_t>(d)] * b.lo[static_cast<size_t>(d)];
+                    const int64_t lo_v = base + kk * b.lo[static_cast<size_t>(dim)];
+                    const int64_t hi_v = base + kk * (b.hi[static_cast<size_t>(dim)] - 1);
+                    if (hi_v < L) {
+                        left = true;
+                    } else if (lo_v >= L) {
+                        left = false;
+                    } else {
+                        // First coordinate on the right-hand side.
+                        const int64_t t = (L - base + kk - 1) / kk;
+                        throw need_split{dim, t};
+                    }
+                }
+                position child;
+                child.coords = c;
+                if (!left) child.coords[ax].off -= L;
+                out = build(k, b, left ? n.a : n.b, child, acc_id, memo);
+                break;
+            }
+        }
+        memo.emplace(key, out);
+        return out;
+    }
+
+    std::vector<box> lowerer::build_boxes(kernel& k, int root, const std::vector<index_t>& shape,
+                                          int acc_id) {
+        rank_ = static_cast<int>(shape.size());
+        std::vector<box> boxes;
+        std::function<void(std::vector<int64_t>, std::vector<int64_t>)> rec =
+            [&](std::vector<int64_t> lo, std::vector<int64_t> hi) {
+                for (int d = 0; d < rank_; ++d)
+                    if (lo[static_cast<size_t>(d)] >= hi[static_cast<size_t>(d)]) return;
+                box b;
+                b.lo = lo;
+                b.hi = hi;
+                std::map<std::string, int> memo;
+                position root_pos;
+                for (int d = 0; d < rank_; ++d) {
+                    affine a;
+                    a.st.assign(static_cast<size_t>(rank_), 0);
+                    a.st[static_cast<size_t>(d)] = 1;
+                    root_pos.coords.push_back(a);
+                }
+                try {
+                    b.root = build(k, b, root, root_pos, acc_id, memo);
+                } catch (const need_split& s) {
+                    auto hi1 = hi;
+                    hi1[static_cast<size_t>(s.dim)] = s.at;
+                    rec(lo, hi1);
+                    auto lo2 = lo;
+                    lo2[static_cast<size_t>(s.dim)] = s.at;
+                    rec(lo2, hi);
+                    return;
+                }
+                boxes.push_back(std::move(b));
+            };
+        std::vector<int64_t> lo(shape.size(), 0);
+        std::vector<int64_t> hi(shape.begin(), shape.end());
+        rec(lo, hi);
+        return boxes;
+    }
+
+    // ================================================= code emission ==
+    // Emits `float pb_e<tag>(float l0, ...)`: the per-element arithmetic of a
+    // box, in the reference's operator order (src/tensor.cpp:629-683, 856-869).
+    std::string lowerer::emit_expr_function(const box& b, const std::string& tag,
+                                            std::vector<int>& load_order) const {
+        load_order.clear();
+        std::ostringstream os;
+        std::vector<std::string> names(b.nodes.size());
+        std::ostringstream body;
+        int params = 0;
+        bool has_acc = false;
+        for (size_t i = 0; i < b.nodes.size(); ++i) {
+            const vnode& v = b.nodes[i];
+            switch (v.kind) {
+                case vnode::op::load:
+                    names[i] = "l" + std::to_string(params++);
+                    load_order.push_back(static_cast<int>(i));
+                    break;
+                case vnode::op::acc:
+                    names[i] = "acc";
+                    has_acc = true;
+                    break;
+                case vnode::op::scalar:
+                    names[i] = float_literal(v.scalar);
+                    break;
+                case vnode::op::unary: {
+                    names[i] = "t" + std::to_string(i);
+                    const std::string& a = names[static_cast<size_t>(v.a)];
+                    body << "    const float " << names[i] << " = ";
+                    if (v.ek == expr_kind::exp)
+                        body << "__expf(" << a << ");\n";
+                    else
+                        body << "(1.0f / " << a << ");\n";
+                    break;
+                }
+                case vnode::op::binary: {
+                    names[i] = "t" + std::to_string(i);
+                    const std::string& a = names[static_cast<size_t>(v.a)];
+                    const std::string& c = names[static_cast<size_t>(v.b)];
+                    body << "    const float " << names[i] << " = ";
+                    switch (v.ek) {
+                        case expr_kind::add: body << "(" << a << " + " << c << ");\n"; break;
+                        case expr_kind::subtract: body << "(" << a << " - " << c << ");\n"; break;
+                        case expr_kind::multiply: body << "(" << a << " * " << c << ");\n"; break;
+                        case expr_kind::divide: body << "(" << a << " / " << c << ");\n"; break;
+                        case expr_kind::maximum:
+                            body << "((" << a << ") > (" << c << ") ? (" << a << ") : (" << c << "));\n";
+                            break;
+                        case expr_kind::minimum:
+                            body << "((" << a << ") < (" << c << ") ? (" << a << ") : (" << c << "));\n";
+                            break;
+                        default: body << "0.0f;\n"; break;
+                    }
+                    break;
+                }
+            }
+        }
+        os << "static __device__ __forceinline__ float pb_e" << tag << "(";
+        bool first = true;
+        if (has_acc) {
+            os << "float acc";
+            first = false;
+        }
+        for (int i = 0; i < params; ++i) {
+            if (!first) os << ", ";
+            os << "float l" << i;
+            first = false;
+        }
+        if (first) os << "void";
+        os << ") {\n" << body.str() << "    return " << names[static_cast<size_t>(b.root)] << ";\n}\n";
+        return os.str();
+    }
+
+    namespace {
+        // Value of an affine map at the box's low corner and its maximum over
+        // the box (to pick 32- or 64-bit index arithmetic).
+        int64_t affine_at(const affine& a, const std::vector<int64_t>& c) {
+            int64_t v = a.off;
+            for (size_t d = 0; d < c.size(); ++d) v += a.st[d] * c[d];
+            return v;
+        }
+        int64_t affine_max(const affine& a, const std::vector<int64_t>& lo,
+                           const std::vector<int64_t>& hi) {
+            int64_t v = a.off;
+            for (size_t d = 0; d < lo.size(); ++d)
+                v += a.st[d] * (a.st[d] >= 0 ? hi[d] - 1 : lo[d]);
+            return v;
+        }
+    } // namespace
+
+    bool lowerer::needs_wide(const std::vector<box>& boxes, const std::vector<index_t>& shape) const {
+        const int64_t numel = static_cast<int64_t>(checked_numel(shape));
+        if (numel >= (int64_t{1} << 31) - 4096) return true;
+        for (const box& b : boxes)
+            for (const vnode& v : b.nodes)
+                if (v.kind == vnode::op::load) {
+                    const int64_t mx = affine_max(v.map, b.lo, b.hi);
+                    if (mx >= (int64_t{1} << 31) - 4096) return true;
+                    if (std::llabs(v.map.off) >= (int64_t{1} << 31) - 4096) return true;
+                }
+        return false;
+    }
+
+    // Address expression of a load for coordinate variables c0..c{R-1}.
+    std::string lowerer::address(const affine& a, const std::vector<std::string>& cvar, bool wide,
+                                 int skip_dim) const {
+        std::string s = lit(a.off, wide);
+        for (int d = 0; d < rank_; ++d) {
+            if (d == skip_dim) continue;
+            const int64_t st = a.st[static_cast<size_t>(d)];
+            if (st == 0) continue;
+            if (st == 1)
+                s += " + " + cvar[static_cast<size_t>(d)];
+            else
+                s += " + " + cvar[static_cast<size_t>(d)] + " * " + lit(st, wide);
+        }
+        return "(" + s + ")";
+    }
+
+    // ROW schedule: 256 threads, U vectors of V consecutive innermost
+    // elements per thread; all loads issued before any arithmetic.
+    std::string lowerer::emit_row_box(const box& b, int tag, const std::vector<index_t>& shape,
+                                      bool wide, int64_t& ctas, std::string& desc) const {
+        const int R = rank_;
+        const int q = R - 1;
+        std::vector<int64_t> E(static_cast<size_t>(R));
+        for (int d = 0; d < R; ++d) E[static_cast<size_t>(d)] = b.hi[static_cast<size_t>(d)] - b.lo[static_cast<size_t>(d)];
+        const std::vector<index_t> ocs = contiguous_strides(shape);
+        bool vec = (E[static_cast<size_t>(q)] % 4 == 0) && (b.lo[static_cast<size_t>(q)] % 4 == 0) &&
+                   (R == 1 || shape[static_cast<size_t>(q)] % 4 == 0);
+        for (const vnode& v : b.nodes)
+            if (v.kind == vnode::op::load) {
+                const int64_t sq = v.map.st[static_cast<size_t>(q)];
+                if (sq != 0 && sq != 1) vec = false;
+            }
+        const int V = vec ? 4 : 1;
+        const int U = 4;
+        int64_t rows = 1;
+        for (int d = 0; d < q; ++d) rows *= E[static_cast<size_t>(d)];
+        const int64_t ipv = E[static_cast<size_t>(q)] / V;
+        const int64_t nvec = rows * ipv;
+        ctas = (nvec + 256 * U - 1) / (256 * U);
+        const std::string I = wide ? "pb_u64" : "pb_u32";
+
+        std::vector<int> order;
+        std::ostringstream os;
+        os << emit_expr_function(b, std::to_string(tag), order);
+        const bool has_acc = false;
+        (void)has_acc;
+        os << "static __device__ __forceinline__ void pb_box" << tag << "(const float* const* L, float* __restrict__ out, pb_u32 cta) {\n";
+        os << "    const " << I << " v0 = (" << I << ")cta * " << 256 * U << "u + threadIdx.x;\n";
+        // Per-leaf load mode: 0 broadcast scalar, 1 vector, 2 strided scalars.
+        std::vector<int> mode(order.size());
+        int nvec_leaves = 0;
+        for (size_t li = 0; li < order.size(); ++li) {
+            const vnode& v = b.nodes[static_cast<size_t>(order[li])];
+            const int64_t sq = v.map.st[static_cast<size_t>(q)];
+            if (sq == 0) {
+                mode[li] = 0;
+            } else if (V == 4 && sq == 1) {
+                bool aligned = affine_at(v.map, b.lo) % 4 == 0;
+                for (int d = 0; d < q; ++d)
+                    if (E[static_cast<size_t>(d)] > 1 && v.map.st[static_cast<size_t>(d)] % 4 != 0) aligned = false;
+                mode[li] = aligned ? 1 : 2;
+                nvec_leaves += aligned;
+            } else {
+                mode[li] = 2;
+            }
+        }
+        os << "    float x[" << U << "][" << (order.empty() ? 1 : order.size()) << "][" << V << "];\n";
+        os << "    " << I << " oa[" << U << "];\n";
+        os << "    #pragma unroll\n    for (int u = 0; u < " << U << "; ++u) {\n";
+        os << "        const " << I << " v = v0 + (" << I << ")u * 256u;\n";
+        os << "        oa[u] = ~(" << I << ")0;\n";
+        os << "        if (v < " << lit(nvec, wide) << ") {\n";
+        std::vector<std::string> cvar(static_cast<size_t>(R));
+        for (int d = 0; d < R; ++d) cvar[static_cast<size_t>(d)] = "c" + std::to_string(d);
+        os << "            " << I << " t = v;\n";
+        os << "            const " << I << " c" << q << " = " << lit(b.lo[static_cast<size_t>(q)], wide)
+           << " + (t % " << lit(ipv, wide) << ") * " << V << "u;\n";
+        if (q > 0) os << "            t /= " << lit(ipv, wide) << ";\n";
+        for (int d = q - 1; d >= 0; --d) {
+            if (d > 0) {
+                os << "            const " << I << " c" << d << " = " << lit(b.lo[static_cast<size_t>(d)], wide)
+                   << " + t % " << lit(E[static_cast<size_t>(d)], wide) << ";\n";
+                os << "            t /= " << lit(E[static_cast<size_t>(d)], wide) << ";\n";
+            } else {
+                os << "            const " << I << " c0 = " << lit(b.lo[0], wide) << " + t;\n";
+            }
+        }
+        // Output address.
+        affine oaff;
+        oaff.st.assign(static_cast<size_t>(R), 0);
+        for (int d = 0; d < R; ++d) oaff.st[static_cast<size_t>(d)] = ocs[static_cast<size_t>(d)];
+        os << "            oa[u] = " << address(oaff, cvar, wide, -1) << ";\n";
+        for (size_t li = 0; li < order.size(); ++li) {
+            const vnode& v = b.nodes[static_cast<size_t>(order[li])];
+            const std::string base = "L[" + std::to_string(v.buffer) + "]";
+            const std::string addr = address(v.map, cvar, wide, -1);
+            if (mode[li] == 0) {
+                os << "            { const float s = pb_ld(" << base << " + " << addr << ");";
+                for (int e = 0; e < V; ++e) os << " x[u][" << li << "][" << e << "] = s;";
+                os << " }\n";
+            } else if (mode[li] == 1) {
+                os << "            { const float4 w = pb_ld4(" << base << " + " << addr
+                   << "); x[u][" << li << "][0] = w.x; x[u][" << li << "][1] = w.y; x[u][" << li
+                   << "][2] = w.z; x[u][" << li << "][3] = w.w; }\n";
+            } else {
+                const int64_t sq = v.map.st[static_cast<size_t>(q)];
+                for (int e = 0; e < V; ++e)
+                    os << "            x[u][" << li << "][" << e << "] = pb_ld(" << base << " + " << addr
+                       << " + " << lit(sq * e, wide) << ");\n";
+            }
+        }
+        os << "        }\n    }\n";
+        os << "    #pragma unroll\n    for (int u = 0; u < " << U << "; ++u) {\n";
+        os << "        if (oa[u] != ~(" << I << ")0) {\n";
+        for (int e = 0; e < V; ++e) {
+            os << "            const float y" << e << " = pb_e" << tag << "(";
+            for (size_t li = 0; li < order.size(); ++li) {
+                if (li) os << ", ";
+                os << "x[u][" << li << "][" << e << "]";
+            }
+            os << ");\n";
+        }
+        if (V == 4)
+            os << "            pb_st4(out + oa[u], make_float4(y0, y1, y2, y3));\n";
+        else
+            os << "            out[oa[u]] = y0;\n";
+        os << "        }\n    }\n}\n";
+        std::ostringstream d;
+        d << "box" << tag << " ROW V=" << V << " U=" << U << " vec_leaves=" << nvec_leaves << "/"
+          << order.size() << " ctas=" << ctas;
+        desc = d.str();
+        return os.str();
+    }
+
+    // TILE schedule for boxes with a transposed leaf: see the file comment.
+    std::string lowerer::emit_tile_box(const box& b, int tag, const std::vector<index_t>& shape,
+                                       bool wide, int p, int64_t& ctas, int& smem_tiles,
+                                       std::string& desc) const {
+        const int R = rank_;
+        const int q = R - 1;
+        std::vector<int64_t> E(static_cast<size_t>(R));
+        for (int d = 0; d < R; ++d) E[static_cast<size_t>(d)] = b.hi[static_cast<size_t>(d)] - b.lo[static_cast<size_t>(d)];
+        const std::vector<index_t> ocs = contiguous_strides(shape);
+        const int64_t tp_n = (E[static_cast<size_t>(p)] + 63) / 64;
+        const int64_t tq_n = (E[static_cast<size_t>(q)] + 63) / 64;
+        int64_t batch = 1;
+        for (int d = 0; d < R; ++d)
+            if (d != p && d != q) batch *= E[static_cast<size_t>(d)];
+        ctas = tp_n * tq_n * batch;
+        const std::string I = wide ? "pb_u64" : "pb_u32";
+        std::vector<int> order;
+        std::ostringstream os;
+        os << emit_expr_function(b, std::to_string(tag), order);
+        // Classify leaves.
+        std::vector<int> tslot(order.size(), -1);
+        std::vector<bool> tvec(order.size(), false);
+        std::vector<int> mode(order.size(), 0);
+        int nt = 0;
+        for (size_t li = 0; li < order.size(); ++li) {
+            const vnode& v = b.nodes[static_cast<size_t>(order[li])];
+            const int64_t sq = v.map.st[static_cast<size_t>(q)];
+            if (sq != 0 && sq != 1) {
+                tslot[li] = nt++;
+                bool aligned = affine_at(v.map, b.lo) % 4 == 0 && sq % 4 == 0;
+                for (int d = 0; d < R; ++d)
+                    if (d != p && d != q && E[static_cast<size_t>(d)] > 1 &&
+                        v.map.st[static_cast<size_t>(d)] % 4 != 0)
+                        aligned = false;
+                tvec[li] = aligned;
+            } else if (sq == 0) {
+                mode[li] = 0;
+            } else {
+                bool aligned = affine_at(v.map, b.lo) % 4 == 0;
+                for (int d = 0; d < q; ++d)
+                    if (E[static_cast<size_t>(d)] > 1 && v.map.st[static_cast<size_t>(d)] % 4 != 0) aligned = false;
+                mode[li] = aligned ? 1 : 2;
+            }
+        }
+        smem_tiles = nt;
+        std::vector<std::string> cvar(static_cast<size_t>(R));
+        for (int d = 0; d < R; ++d) cvar[static_cast<size_t>(d)] = "c" + std::to_string(d);
+        os << "static __device__ __forceinline__ void pb_box" << tag
+           << "(const float* const* L, float* __restrict__ out, pb_u32 cta, float* sm) {\n";
+        os << "    pb_u32 t = cta;\n";
+        os << "    const pb_u32 tq = t % " << tq_n << "u; t /= " << tq_n << "u;\n";
+        os << "    const pb_u32 tp = t % " << tp_n << "u; t /= " << tp_n << "u;\n";
+        // Batch coordinates.
+        for (int d = R - 1; d >= 0; --d) {
+            if (d == p || d == q) continue;
+            os << "    const " << I << " c" << d << " = " << lit(b.lo[static_cast<size_t>(d)], wide) << " + ("
+               << I << ")(t % " << E[static_cast<size_t>(d)] << "u); t /= " << E[static_cast<size_t>(d)] << "u;\n";
+        }
+        os << "    const " << I << " bp = " << lit(b.lo[static_cast<size_t>(p)], wide) << " + (" << I << ")tp * 64u;\n";
+        os << "    const " << I << " bq = " << lit(b.lo[static_cast<size_t>(q)], wide) << " + (" << I << ")tq * 64u;\n";
+        const std::string hp = lit(b.hi[static_cast<size_t>(p)], wide);
+        const std::string hq = lit(b.hi[static_cast<size_t>(q)], wide);
+        // Load phase.
+        os << "    #pragma unroll\n    for (int u = 0; u < 4; ++u) {\n";
+        os << "        const pb_u32 f = threadIdx.x + 256u * u;\n";
+        os << "        const pb_u32 ci = (f & 7u) | ((f >> 9) << 3);\n";
+        os << "        const pb_u32 j = (f >> 3) & 63u;\n";
+        os << "        const pb_u32 i = ci * 4u;\n";
+        os << "        const " << I << " c" << p << " = bp + i;\n";
+        os << "        const " << I << " c" << q << " = bq + j;\n";
+        os << "        const pb_u32 sw = 4u * ((j >> 2) ^ (ci & 7u)) + (j & 3u);\n";
+        for (size_t li = 0; li < order.size(); ++li) {
+            if (tslot[li] < 0) continue;
+            const vnode& v = b.nodes[static_cast<size_t>(order[li])];
+            const std::string base = "L[" + std::to_string(v.buffer) + "]";
+            const std::string addr = address(v.map, cvar, wide, -1);
+            const int64_t sp = v.map.st[static_cast<size_t>(p)];
+            os << "        {\n            float4 w = make_float4(0.f, 0.f, 0.f, 0.f);\n";
+            os << "            if (c" << p << " < " << hp << " && c" << q << " < " << hq << ") {\n";
+            if (tvec[li] && sp == 1) {
+                os << "                w = pb_ld4(" << base << " + " << addr << ");\n";
+            } else {
+                os << "                const " << I << " a = " << addr << ";\n";
+                for (int e = 0; e < 4; ++e) {
+                    const char* comp = e == 0 ? "x" : (e == 1 ? "y" : (e == 2 ? "z" : "w"));
+                    if (e == 0)
+                        os << "                w." << comp << " = pb_ld(" << base << " + a);\n";
+                    else
+                        os << "                if (c" << p << " + " << e << "u < " << hp << ") w." << comp
+                           << " = pb_ld(" << base << " + a + " << lit(sp * e, wide) << ");\n";
+                }
+            }
+            os << "            }\n";
+            const int base_off = tslot[li] * 4096;
+            os << "            float* s = sm + " << base_off << " + i * 64u + sw;\n";
+            os << "            s[0] = w.x; s[64] = w.y; s[128] = w.z; s[192] = w.w;\n";
+            os << "        }\n";
+        }
+        os << "    }\n    __syncthreads();\n";
+        // Output phase.
+        os << "    #pragma unroll\n    for (int u = 0; u < 4; ++u) {\n";
+        os << "        const pb_u32 f = threadIdx.x + 256u * u;\n";
+        os << "        const pb_u32 ch = f & 15u;\n";
+        os << "        const pb_u32 i = f >> 4;\n";
+        os << "        const " << I << " c" << p << " = bp + i;\n";
+        os << "        const " << I << " c" << q << " = bq + 4u * ch;\n";
+        os << "        if (c" << p << " < " << hp << " && c" << q << " < " << hq << ") {\n";
+        for (size_t li = 0; li < order.size(); ++li) {
+            const vnode& v = b.nodes[static_cast<size_t>(order[li])];
+            const std::string base = "L[" + std::to_string(v.buffer) + "]";
+            if (tslot[li] >= 0) {
+                os << "            const float4 x" << li << " = *reinterpret_cast<const float4*>(sm + "
+                   << tslot[li] * 4096 << " + i * 64u + 4u * (ch ^ ((i >> 2) & 7u)));\n";
+            } else if (mode[li] == 0) {
+                const std::string addr = address(v.map, cvar, wide, -1);
+                os << "            const float s" << li << " = pb_ld(" << base << " + " << addr << ");\n";
+                os << "            const float4 x" << li << " = make_float4(s" << li << ", s" << li << ", s"
+                   << li << ", s" << li << ");\n";
+            } else if (mode[li] == 1) {
+                const std::string addr = address(v.map, cvar, wide, -1);
+                os << "            const float4 x" << li << " = pb_ld4(" << base << " + " << addr << ");\n";
+            } else {
+                const std::string addr = address(v.map, cvar, wide, -1);
+                os << "            const float4 x" << li << " = make_float4(pb_ld(" << base << " + " << addr
+                   << "), pb_ld(" << base << " + " << addr << " + 1u), pb_ld(" << base << " + " << addr
+                   << " + 2u), pb_ld(" << base << " + " << addr << " + 3u));\n";
+            }
+        }
+        const char* comps[4] = {"x", "y", "z", "w"};
+        for (int e = 0; e < 4; ++e) {
+            os << "            const float y" << e << " = pb_e" << tag << "(";
+            for (size_t li = 0; li < order.size(); ++li) {
+                if (li) os << ", ";
+                os << "x" << li << "." << comps[e];
+            }
+            os << ");\n";
+        }
+        affine oaff;
+        oaff.st.assign(static_cast<size_t>(R), 0);
+        for (int d = 0; d < R; ++d) oaff.st[static_cast<size_t>(d)] = ocs[static_cast<size_t>(d)];
+        os << "            pb_st4(out + " << address(oaff, cvar, wide, -1) << ", make_float4(y0, y1, y2, y3));\n";
+        os << "        }\n    }\n}\n";
+        std::ostringstream d;
+        d << "box" << tag << " TILE p=" << p << " tiles=" << tp_n << "x" << tq_n << "x" << batch
+          << " transposed_leaves=" << nt;
+        desc = d.str();
+        return os.str();
+    }
+
+    void lowerer::finish_kernel(launch_spec& l) {
+        const auto& opts = kernel_options();
+        std::vector<const char*> o;
+        for (const auto& s : opts) o.push_back(s.c_str());
+        check(pbrt_compile(l.source.c_str(), o.data(), static_cast<int>(o.size()), 1, &l.image_key));
+    }
+
+    int lowerer::emit_elementwise(int id) {
+        const gnode& n = g_.nodes[static_cast<size_t>(id)];
+        std::vector<index_t> shape = n.shape;
+        if (shape.empty()) shape = {1};
+        kernel k;
+        std::vector<box> boxes;
+        try {
+            boxes = build_boxes(k, id, shape, -1);
+        } catch (const not_affine&) {
+            return emit_generic(id);
+        }
+        const int out = new_temp(checked_numel(shape) * sizeof(float));
+        const bool wide = needs_wide(boxes, shape);
+        std::ostringstream src;
+        src << kernel_prelude();
+        std::vector<int64_t> ctas(boxes.size());
+        std::vector<bool> tiled(boxes.size(), false);
+        std::string desc;
+        int max_tiles = 0;
+        for (size_t bi = 0; bi < boxes.size(); ++bi) {
+            const box& b = boxes[bi];
+            const int R = rank_;
+            const int q = R - 1;
+            // Transposed leaves and the dim along which they are contiguous.
+            int p = -1;
+            bool has_t = false;
+            for (const vnode& v : b.nodes) {
+                if (v.kind != vnode::op::load) continue;
+                const int64_t sq = v.map.st[static_cast<size_t>(q)];
+                if (sq != 0 && sq != 1) has_t = true;
+            }
+            if (has_t && R >= 2) {
+                int64_t best = 0;
+                for (int d = 0; d < q; ++d) {
+                    bool ok = true;
+                    for (const vnode& v : b.nodes) {
+                        if (v.kind != vnode::op::load) continue;
+                        const int64_t sq = v.map.st[static_cast<size_t>(q)];
+                        if (sq != 0 && sq != 1 && v.map.st[static_cast<size_t>(d)] != 1) ok = false;
+                    }
+                    const int64_t ext = b.hi[static_cast<size_t>(d)] - b.lo[static_cast<size_t>(d)];
+                    if (ok && ext > best) {
+                        best = ext;
+                        p = d;
+                    }
+                }
+                const int64_t eq = b.hi[static_cast<size_t>(q)] - b.lo[static_cast<size_t>(q)];
+                if (p >= 0 && !(eq % 4 == 0 && b.lo[static_cast<size_t>(q)] % 4 == 0 &&
+                                shape[static_cast<size_t>(q)] % 4 == 0 && best >= 4))
+                    p = -1;
+            }
+            std::string d;
+            if (p >= 0) {
+                int tiles = 0;
+                src << emit_tile_box(b, static_cast<int>(bi), shape, wide, p, ctas[bi], tiles, d);
+                tiled[bi] = true;
+                max_tiles = std::max(max_tiles, tiles);
+            } else {
+                src << emit_row_box(b, static_cast<int>(bi), shape, wide, ctas[bi], d);
+            }
+            desc += (desc.empty() ? "" : "; ") + d;
+        }
+        launch_spec l;
+        const std::string body = src.str();
+        l.name = "pb_elem_" + hex64(hash_string(body)).substr(0, 8);
+        std::ostringstream ker;
+        ker << body;
+        ker << "extern \"C\" __global__ void __launch_bounds__(256) " << l.name << "(";
+        for (size_t i = 0; i < k.leaves.size(); ++i) ker << "const float* __restrict__ in" << i << ", ";
+        ker << "float* __restrict__ out) {\n";
+        ker << "    const float* L[" << std::max<size_t>(1, k.leaves.size()) << "] = {";
+        for (size_t i = 0; i < k.leaves.size(); ++i) ker << (i ? ", " : "") << "in" << i;
+        if (k.leaves.empty()) ker << "nullptr";
+        ker << "};\n";
+        if (max_tiles > 0) ker << "    extern __shared__ float4 pb_dyn_smem[];\n    float* sm = reinterpret_cast<float*>(pb_dyn_smem);\n";
+        ker << "    pb_u32 cta = blockIdx.x;\n";
+        int64_t total = 0;
+        for (size_t bi = 0; bi < boxes.size(); ++bi) {
+            ker << "    if (cta < " << ctas[bi] << "u) { pb_box" << bi << "(L, out, cta"
+                << (tiled[bi] ? ", sm" : "") << "); return; }\n";
+            ker << "    cta -= " << ctas[bi] << "u;\n";
+            total += ctas[bi];
+        }
+        ker << "}\n";
+        l.source = ker.str();
+        l.schedule = "elementwise " + desc;
+        if (total > 0x7fffffff) throw std::invalid_argument("tensor is too large for one launch");
+        l.grid = {static_cast<uint32_t>(std::max<int64_t>(1, total)), 1, 1};
+        l.block = {256, 1, 1};
+        l.smem = static_cast<uint32_t>(max_tiles) * 4096u * 4u;
+        l.args = k.leaves;
+        kernel_arg o;
+        o.kind = arg_kind::temp;
+        o.index = out;
+        l.args.push_back(o);
+        finish_kernel(l);
+        p_.launches.push_back(std::move(l));
+        return out;
+    }
+
+    // ---------------------------------------------------- generic gather --
+    // Fallback for graphs whose index maps are not affine: one thread per
+    // output element, index arithmetic composed node by node on the linear
+    // output index (the same composition rules as src/tensor.cpp:511-614).
+    std::string lowerer::gen_value(kernel& k, int id, const std::string& idx,
+                                   std::ostringstream& stmts, int& counter) {
+        const gnode& n = g_.nodes[static_cast<size_t>(id)];
+        auto coord = [&](const std::vector<index_t>& shape, size_t d) {
+            const std::vector<index_t> cs = contiguous_strides(shape);
+            return "((" + idx + " / " + std::to_string(cs[d]) + "ull) % " + std::to_string(shape[d]) + "ull)";
+        };
+        switch (n.kind) {
+            case expr_kind::scalar:
+                return float_literal(n.scalar);
+            case expr_kind::input:
+                return "pb_ld(in" + std::to_string(k.leaf(arg_kind::slot, n.slot)) + " + (" + idx + "))";
+            case expr_kind::matmul:
+            case expr_kind::sum:
+            case expr_kind::max:
+                return "pb_ld(in" + std::to_string(k.leaf(arg_kind::temp, materialize(id))) + " + (" +
+                       idx + "))";
+            case expr_kind::add:
+            case expr_kind::subtract:
+            case expr_kind::multiply:
+            case expr_kind::divide:
+            case expr_kind::maximum:
+            case expr_kind::minimum: {
+                if (is_barrier(id))
+                    return "pb_ld(in" + std::to_string(k.leaf(arg_kind::temp, materialize(id))) +
+                           " + (" + idx + "))";
+                const std::string a = gen_value(k, n.a, idx, stmts, counter);
+                const std::string c = gen_value(k, n.b, idx, stmts, counter);
+                const std::string t = "g" + std::to_string(counter++);
+                stmts << "    const float " << t << " = ";
+                switch (n.kind) {
+                    case expr_kind::add: stmts << "(" << a << " + " << c << ");\n"; break;
+                    case expr_kind::subtract: stmts << "(" << a << " - " << c << ");\n"; break;
+                    case expr_kind::multiply: stmts << "(" << a << " * " << c << ");\n"; break;
+                    case expr_kind::divide: stmts << "(" << a << " / " << c << ");\n"; break;
+                    case expr_kind::maximum: stmts << "((" << a << ") > (" << c << ") ? (" << a << ") : (" << c << "));\n"; break;
+                    default: stmts << "((" << a << ") < (" << c << ") ? (" << a << ") : (" << c << "));\n"; break;
+                }
+                return t;
+            }
+            case expr_kind::exp:
+            case expr_kind::reciprocal: {
+                const std::string a = gen_value(k, n.a, idx, stmts, counter);
+                const std::string t = "g" + std::to_string(counter++);
+                if (n.kind == expr_kind::exp)
+                    stmts << "    const float " << t << " = __expf(" << a << ");\n";
+                else
+                    stmts << "    const float " << t << " = (1.0f / " << a << ");\n";
+                return t;
+            }
+            case expr_kind::slice: {
+                std::string s = std::to_string(n.p_offset) + "ull";
+                for (size_t d = 0; d < n.shape.size(); ++d)
+                    if (n.p_strides[d] != 0)
+                        s += " + " + coord(n.shape, d) + " * " + std::to_string(n.p_strides[d]) + "ull";
+                const std::string v = "x" + std::to_string(counter++);
+                stmts << "    const pb_u64 " << v << " = " << s << ";\n";
+                return gen_value(k, n.a, v, stmts, counter);
+            }
+            case expr_kind::reshape:
+            case expr_kind::unsqueeze:
+                return gen_value(k, n.a, idx, stmts, counter);
+            case expr_kind::transpose: {
+                const gnode& src = g_.nodes[static_cast<size_t>(n.a)];
+                const std::string v = "x" + std::to_string(counter++);
+                stmts << "    const pb_u64 " << v << " = ((" << idx << ") % " << src.shape[0] << "ull) * "
+                      << src.shape[1] << "ull + (" << idx << ") / " << src.shape[0] << "ull;\n";
+                return gen_value(k, n.a, v, stmts, counter);
+            }
+            case expr_kind::broadcast: {
+                const gnode& src = g_.nodes[static_cast<size_t>(n.a)];
+                if (src.is_scalar) return gen_value(k, n.a, idx, stmts, counter);
+                const std::vector<index_t> scs = contiguous_strides(src.shape);
+                const size_t off = n.shape.size() - src.shape.size();
+                std::string s = "0ull";
+                for (size_t d = 0; d < src.shape.size(); ++d)
+                    if (src.shape[d] != 1)
+                        s += " + " + coord(n.shape, off + d) + " * " + std::to_string(scs[d]) + "ull";
+                const std::string v = "x" + std::to_string(counter++);
+                stmts << "    const pb_u64 " << v << " = " << s << ";\n";
+                return gen_value(k, n.a, v, stmts, counter);
+            }
+            case expr_kind::concat: {
+                const gnode& l = g_.nodes[static_cast<size_t>(n.a)];
+                const gnode& r = g_.nodes[static_cast<size_t>(n.b)];
+                const std::vector<index_t> lcs = contiguous_strides(l.shape);
+                const std::vector<index_t> rcs = contiguous_strides(r.shape);
+                std::string li = "0ull", ri = "0ull";
+                for (size_t d = 0; d < n.shape.size(); ++d) {
+                    const std::string c = coord(n.shape, d);
+                    li += " + " + c + " * " + std::to_string(lcs[d]) + "ull";
+                    if (d == n.axis)
+                        ri += " + (" + c + " - " + std::to_string(l.shape[d]) + "ull) * " + std::to_string(rcs[d]) + "ull";
+                    else
+                        ri += " + " + c + " * " + std::to_string(rcs[d]) + "ull";
+                }
+                const std::string ax = "x" + std::to_string(counter++);
+                stmts << "    const pb_u64 " << ax << " = " << coord(n.shape, n.axis) << ";\n";
+                const std::string t = "g" + std::to_string(counter++);
+                stmts << "    float " << t << ";\n    if (" << ax << " < " << l.shape[n.axis] << "ull) {\n";
+                std::ostringstream lst;
+                const std::string lv = gen_value(k, n.a, "(" + li + ")", lst, counter);
+                stmts << lst.str() << "    " << t << " = " << lv << ";\n    } else {\n";
+                std::ostringstream rst;
+                const std::string rv = gen_value(k, n.b, "(" + ri + ")", rst, counter);
+                stmts << rst.str() << "    " << t << " = " << rv << ";\n    }\n";
+                return t;
+            }
+        }
+        return "0.0f";
+    }
+
+    int lowerer::emit_generic(int id) {
+        const gnode& n = g_.nodes[static_cast<size_t>(id)];
+        const size_t count = checked_numel(n.shape.empty() ? std::vector<index_t>{1} : n.shape);
+        const int out = new_temp(count * sizeof(float));
+        kernel k;
+        std::ostringstream stmts;
+        int counter = 0;
+        const std::string v = gen_value(k, id, "i", stmts, counter);
+        std::ostringstream src;
+        src << kernel_prelude();
+        std::ostringstream body;
+        body << "    for (pb_u64 i = (pb_u64)blockIdx.x * 256u + threadIdx.x; i < " << count
+             << "ull; i += (pb_u64)gridDim.x * 256u) {\n"
+             << stmts.str() << "    out[i] = " << v << ";\n    }\n";
+        launch_spec l;
+        l.name = "pb_gather_" + hex64(hash_string(body.str())).substr(0, 8);
+        src << "extern \"C\" __global__ void __launch_bounds__(256) " << l.name << "(";
+        for (size_t i = 0; i < k.leaves.size(); ++i) src << "const float* __restrict__ in" << i << ", ";
+        src << "float* __restrict__ out) {\n" << body.str() << "}\n";
+        l.source = src.str();
+        l.schedule = "gather (non-affine index maps)";
+        const uint64_t blocks = std::min<uint64_t>((count + 255) / 256, 148u * 16u);
+        l.grid = {static_cast<uint32_t>(std::max<uint64_t>(1, blocks)), 1, 1};
+        l.args = k.leaves;
+        kernel_arg o;
+        o.kind = arg_kind::temp;
+        o.index = out;
+        l.args.push_back(o);
+        finish_kernel(l);
+        p_.launches.push_back(std::move(l));
+        return out;
+    }
+
+    // ------------------------------------------------------ reductions --
+    // Builds the operand of a row-wise kernel (reduction or softmax) as a
+    // single affine box over the operand's coordinates. Falls back to
+    // materialising the operand when it is not a single affine box or its
+    // leaves are not contiguous along `axis`.
+    lowerer::row_operand lowerer::row_prologue(int operand, size_t axis) {
+        const gnode& s = g_.nodes[static_cast<size_t>(operand)];
+        row_operand r;
+        r.shape = s.shape;
+        auto try_build = [&](int src_id) -> bool {
+            r.k = kernel{};
+            std::vector<box> boxes;
+            try {
+                boxes = build_boxes(r.k, src_id, r.shape, -1);
+            } catch (const not_affine&) {
+                return false;
+            }
+            if (boxes.size() != 1) return false;
+            for (const vnode& v : boxes[0].nodes)
+                if (v.kind == vnode::op::load) {
+                    const int64_t sa = v.map.st[axis];
+                    if (axis + 1 == r.shape.size() && sa != 0 && sa != 1) return false;
+                }
+            r.b = std::move(boxes[0]);
+            return true;
+        };
+        if (!try_build(operand)) {
+            // Materialise the operand, then read it back as a plain input.
+            const int t = materialize(operand);
+            r.k = kernel{};
+            rank_ = static_cast<int>(r.shape.size());
+            r.b = box{};
+            r.b.lo.assign(r.shape.size(), 0);
+            r.b.hi.assign(r.shape.begin(), r.shape.end());
+            vnode v;
+            v.kind = vnode::op::load;
+            v.buffer = r.k.leaf(arg_kind::temp, t);
+            v.map.st.assign(r.shape.size(), 0);
+            const std::vector<index_t> cs = contiguous_strides(r.shape);
+            for (size_t d = 0; d < r.shape.size(); ++d) v.map.st[d] = cs[d];
+            r.b.nodes.push_back(v);
+            r.b.root = 0;
+        }
+        return r;
+    }
+
+    int lowerer::emit_reduce(int id) {
+        const gnode& n = g_.nodes[static_cast<size_t>(id)];
+        const bool is_sum = n.kind == expr_kind::sum;
+        row_operand r = row_prologue(n.a, n.axis);
+        const std::vector<index_t>& S = r.shape;
+        rank_ = static_cast<int>(S.size());
+        const int R = rank_;
+        const size_t ax = n.axis;
+        int64_t outer = 1, inner = 1;
+        for (size_t d = 0; d < ax; ++d) outer *= S[d];
+        for (size_t d = ax + 1; d < S.size(); ++d) inner *= S[d];
+        const int64_t A = S[ax];
+        const int64_t outputs = outer * inner;
+        const int out = new_temp(static_cast<size_t>(outputs) * sizeof(float));
+        bool wide = needs_wide({r.b}, S);
+        const std::string I = wide ? "pb_u64" : "pb_u32";
+        std::vector<int> order;
+        std::ostringstream src;
+        src << kernel_prelude();
+        src << emit_expr_function(r.b, "0", order);
+        const std::string init = is_sum ? "0.0f" : "PB_NEG_FLT_MAX";
+        auto combine = [&](const std::string& acc, const std::string& v) {
+            if (is_sum) return acc + " = " + acc + " + " + v + ";";
+            return acc + " = " + acc + " > " + v + " ? " + acc + " : " + v + ";";
+        };
+        std::vector<std::string> cvar(static_cast<size_t>(R));
+        for (int d = 0; d < R; ++d) cvar[static_cast<size_t>(d)] = "c" + std::to_string(d);
+        std::ostringstream body;
+        launch_spec l;
+        std::string desc;
+        if (inner == 1) {
+            // Row reduction: one warp per output row, 8 rows per CTA.
+            bool vec = A % 4 == 0;
+            for (int li : order) {
+                const vnode& v = r.b.nodes[static_cast<size_t>(li)];
+                const int64_t sa = v.map.st[ax];
+                if (sa == 1) {
+                    if (affine_at(v.map, r.b.lo) % 4 != 0) vec = false;
+                    for (size_t d = 0; d < ax; ++d)
+                        if (v.map.st[d] % 4 != 0 && S[d] > 1) vec = false;
+                }
+            }
+            const int V = vec ? 4 : 1;
+            body << "    const pb_u32 warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;\n";
+            body << "    const " << I << " row = (" << I << ")blockIdx.x * 8u + warp;\n";
+            body << "    if (row >= " << lit(outer, wide) << ") return;\n";
+            body << "    " << I << " t = row;\n";
+            for (int d = static_cast<int>(ax) - 1; d >= 0; --d) {
+                body << "    const " << I << " c" << d << " = t % " << lit(S[static_cast<size_t>(d)], wide) << "; t /= "
+                     << lit(S[static_cast<size_t>(d)], wide) << ";\n";
+            }
+            body << "    float acc = " << init << ";\n";
+            body << "    for (" << I << " k = lane * " << V << "u; k < " << lit(A, wide) << "; k += " << 32 * V << "u) {\n";
+            body << "        const " << I << " c" << ax << " = k;\n";
+            for (size_t li = 0; li < order.size(); ++li) {
+                const vnode& v = r.b.nodes[static_cast<size_t>(order[li])];
+                const std::string base = "in" + std::to_string(v.buffer);
+                const std::string addr = address(v.map, cvar, wide, -1);
+                const int64_t sa = v.map.st[ax];
+                if (V == 4 && sa == 1)
+                    body << "        const float4 x" << li << " = pb_ld4(" << base << " + " << addr << ");\n";
+                else if (V == 4)
+                    body << "        const float s" << li << " = pb_ld(" << base << " + " << addr
+                         << "); const float4 x" << li << " = make_float4(s" << li << ", s" << li << ", s" << li
+                         << ", s" << li << ");\n";
+                else
+                    body << "        const float x" << li << " = pb_ld(" << base << " + " << addr << ");\n";
+            }
+            const char* comps[4] = {"x", "y", "z", "w"};
+            for (int e = 0; e < V; ++e) {
+                body << "        { const float v = pb_e0(";
+                for (size_t li = 0; li < order.size(); ++li) {
+                    if (li) body << ", ";
+                    body << "x" << li << (V == 4 ? std::string(".") + comps[e] : "");
+                }
+                body << "); " << combine("acc", "v") << " }\n";
+            }
+            body << "    }\n";
+            body << "    #pragma unroll\n    for (int o = 16; o > 0; o >>= 1) { const float v = __shfl_xor_sync(0xffffffffu, acc, o); "
+                 << combine("acc", "v") << " }\n";
+            body << "    if (lane == 0) out[row] = acc;\n";
+            const int64_t ctas = (outer + 7) / 8;
+            l.grid = {static_cast<uint32_t>(ctas), 1, 1};
+            desc = "row reduction (warp per row) V=" + std::to_string(V);
+        } else {
+            // Strided reduction: one thread per output, coalesced across the
+            // inner dimensions.
+            body << "    const " << I << " o = (" << I << ")blockIdx.x * 256u + threadIdx.x;\n";
+            body << "    if (o >= " << lit(outputs, wide) << ") return;\n";
+            body << "    " << I << " t = o;\n";
+            for (int d = R - 1; d >= 0; --d) {
+                if (static_cast<size_t>(d) == ax) continue;
+                body << "    const " << I << " c" << d << " = t % " << lit(S[static_cast<size_t>(d)], wide) << "; t /= "
+                     << lit(S[static_cast<size_t>(d)], wide) << ";\n";
+            }
+            body << "    float acc = " << init << ";\n";
+            body << "    for (" << I << " k = 0; k < " << lit(A, wide) << "; ++k) {\n";
+            body << "        const " << I << " c" << ax << " = k;\n";
+            for (size_t li = 0; li < order.size(); ++li) {
+                const vnode& v = r.b.nodes[static_cast<size_t>(order[li])];
+                body << "        const float x" << li << " = pb_ld(in" << v.buffer << " + "
+                     << address(v.map, cvar, wide, -1) << ");\n";
+            }
+            body << "        { const float v = pb_e0(";
+            for (size_t li = 0; li < order.size(); ++li) body << (li ? ", " : "") << "x" << li;
+            body << "); " << combine("acc", "v") << " }\n    }\n";
+            body << "    out[o] = acc;\n";
+            const int64_t ctas = (outputs + 255) / 256;
+            l.grid = {static_cast<uint32_t>(ctas), 1, 1};
+            desc = "strided reduction (thread per output)";
+        }
+        l.name = "pb_reduce_" + hex64(hash_string(src.str() + body.str())).substr(0, 8);
+        src << "extern \"C\" __global__ void __launch_bounds__(256) " << l.name << "(";
+        for (size_t i = 0; i < r.k.leaves.size(); ++i) src << "const float* __restrict__ in" << i << ", ";
+        src << "float* __restrict__ out) {\n" << body.str() << "}\n";
+        l.source = src.str();
+        l.schedule = std::string(is_sum ? "sum " : "max ") + desc;
+        l.block = {256, 1, 1};
+        l.args = r.k.leaves;
+        kernel_arg o;
+        o.kind = arg_kind::temp;
+        o.index = out;
+        l.args.push_back(o);
+        finish_kernel(l);
+        p_.launches.push_back(std::move(l));
+        return out;
+    }
+
+    // --------------------------------------------------------- softmax --
+    int lowerer::emit_softmax(int id, int x) {
+        const gnode& n = g_.nodes[static_cast<size_t>(id)];
+        const size_t ax = n.shape.size() - 1;
+        row_operand r = row_prologue(x, ax);
+        const std::vector<index_t>& S = r.shape;
+        rank_ = static_cast<int>(S.size());
+        const int R = rank_;
+        int64_t rows = 1;
+        for (size_t d = 0; d < ax; ++d) rows *= S[d];
+        const int64_t A = S[ax];
+        const int out = new_temp(static_cast<size_t>(rows * A) * sizeof(float));
+        bool wide = needs_wide({r.b}, S) || rows * A >= (int64_t{1} << 31) - 4096;
+        const std::string I = wide ? "pb_u64" : "pb_u32";
+        std::vector<int> order;
+        std::ostringstream src;
+        src << kernel_prelude();
+        src << emit_expr_function(r.b, "0", order);
+        bool vec = A % 4 == 0;
+        for (int li : order) {
+            const vnode& v = r.b.nodes[static_cast<size_t>(li)];
+            if (v.map.st[ax] == 1) {
+                if (affine_at(v.map, r.b.lo) % 4 != 0) vec = false;
+                for (size_t d = 0; d < ax; ++d)
+                    if (v.map.st[d] % 4 != 0 && S[d] > 1) vec = false;
+            }
+        }
+        const int V = vec ? 4 : 1;
+        const int T = A >= 2048 ? 256 : (A >= 512 ? 128 : 32);
+        const int64_t NI = (A + static_cast<int64_t>(T) * V - 1) / (static_cast<int64_t>(T) * V);
+        const bool in_registers = NI * V <= 64;
+        std::vector<std::string> cvar(static_cast<size_t>(R));
+        for (int d = 0; d < R; ++d) cvar[static_cast<size_t>(d)] = "c" + std::to_string(d);
+        const char* comps[4] = {"x", "y", "z", "w"};
+        std::ostringstream body;
+        body << "    __shared__ float red[32];\n";
+        body << "    const pb_u32 warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;\n";
+        body << "    for (" << I << " row = blockIdx.x; row < " << lit(rows, wide) << "; row += gridDim.x) {\n";
+        body << "        " << I << " t = row;\n";
+        for (int d = static_cast<int>(ax) - 1; d >= 0; --d)
+            body << "        const " << I << " c" << d << " = t % " << lit(S[static_cast<size_t>(d)], wide) << "; t /= "
+                 << lit(S[static_cast<size_t>(d)], wide) << ";\n";
+        // Loads the operand value vector at column k into float xv[V].
+        auto emit_load = [&](const std::string& k, const std::string& dst, const std::string& indent) {
+            body << indent << "{\n" << indent << "    const " << I << " c" << ax << " = " << k << ";\n";
+            for (size_t li = 0; li < order.size(); ++li) {
+                const vnode& v = r.b.nodes[static_cast<size_t>(order[li])];
+                const std::string base = "in" + std::to_string(v.buffer);
+                const std::string addr = address(v.map, cvar, wide, -1);
+                if (V == 4 && v.map.st[ax] == 1)
+                    body << indent << "    const float4 x" << li << " = pb_ld4(" << base << " + " << addr << ");\n";
+                else if (V == 4)
+                    body << indent << "    const float s" << li << " = pb_ld(" << base << " + " << addr
+                         << "); const float4 x" << li << " = make_float4(s" << li << ", s" << li << ", s" << li
+                         << ", s" << li << ");\n";
+                else
+                    body << indent << "    const float x" << li << " = pb_ld(" << base << " + " << addr << ");\n";
+            }
+            for (int e = 0; e < V; ++e) {
+                body << indent << "    " << dst << "[" << e << "] = pb_e0(";
+                for (size_t li = 0; li < order.size(); ++li) {
+                    if (li) body << ", ";
+                    body << "x" << li << (V == 4 ? std::string(".") + comps[e] : "");
+                }
+                body << ");\n";
+            }
+            body << indent << "}\n";
+        };
+        auto block_reduce = [&](const std::string& var, bool is_max) {
+            const std::string comb = is_max ? (var + " = " + var + " > v ? " + var + " : v;")
+                                            : (var + " = " + var + " + v;");
+            body << "        #pragma unroll\n        for (int o = 16; o > 0; o >>= 1) { const float v = __shfl_xor_sync(0xffffffffu, "
+                 << var << ", o); " << comb << " }\n";
+            if (T > 32) {
+                body << "        if (lane == 0) red[warp] = " << var << ";\n        __syncthreads();\n";
+                body << "        if (warp == 0) {\n            " << var << " = lane < " << T / 32 << "u ? red[lane] : "
+                     << (is_max ? "PB_NEG_FLT_MAX" : "0.0f") << ";\n";
+                body << "            #pragma unroll\n            for (int o = 16; o > 0; o >>= 1) { const float v = __shfl_xor_sync(0xffffffffu, "
+                     << var << ", o); " << comb << " }\n";
+                body << "            if (lane == 0) red[0] = " << var << ";\n        }\n";
+                body << "        __syncthreads();\n        " << var << " = red[0];\n        __syncthreads();\n";
+            }
+        };
+        const std::string orow = "row * " + lit(A, wide);
+        if (in_registers) {
+            body << "        float x[" << NI << "][" << V << "];\n";
+            body << "        #pragma unroll\n        for (int it = 0; it < " << NI << "; ++it) {\n";
+            body << "            const " << I << " k = ((" << I << ")it * " << T << "u + threadIdx.x) * " << V << "u;\n";
+            body << "            if (k < " << lit(A, wide) << ") ";
+            emit_load("k", "x[it]", "            ");
+            body << "            else { ";
+            for (int e = 0; e < V; ++e) body << "x[it][" << e << "] = PB_NEG_FLT_MAX; ";
+            body << "}\n        }\n";
+            body << "        float m = PB_NEG_FLT_MAX;\n";
+            body << "        #pragma unroll\n        for (int it = 0; it < " << NI << "; ++it)\n";
+            body << "            #pragma unroll\n            for (int e = 0; e < " << V
+                 << "; ++e) m = m > x[it][e] ? m : x[it][e];\n";
+            block_reduce("m", true);
+            body << "        float s = 0.0f;\n";
+            body << "        #pragma unroll\n        for (int it = 0; it < " << NI << "; ++it) {\n";
+            body << "            const " << I << " k = ((" << I << ")it * " << T << "u + threadIdx.x) * " << V << "u;\n";
+            body << "            if (k < " << lit(A, wide) << ") {\n";
+            body << "                #pragma unroll\n                for (int e = 0; e < " << V
+                 << "; ++e) { x[it][e] = __expf(x[it][e] - m); s = s + x[it][e]; }\n";
+            body << "            }\n        }\n";
+            block_reduce("s", false);
+            body << "        #pragma unroll\n        for (int it = 0; it < " << NI << "; ++it) {\n";
+            body << "            const " << I << " k = ((" << I << ")it * " << T << "u + threadIdx.x) * " << V << "u;\n";
+            body << "            if (k < " << lit(A, wide) << ") {\n";
+            if (V == 4)
+                body << "                pb_st4(out + " << orow << " + k, make_float4(x[it][0] / s, x[it][1] / s, x[it][2] / s, x[it][3] / s));\n";
+            else
+                body << "                out[" << orow << " + k] = x[it][0] / s;\n";
+            body << "            }\n        }\n";
+        } else {
+            // Rows too long for registers: max pass, sum pass, write pass.
+            body << "        float m = PB_NEG_FLT_MAX;\n";
+            body << "        for (" << I << " k = threadIdx.x * " << V << "u; k < " << lit(A, wide) << "; k += "
+                 << T * V << "u) {\n            float xv[" << V << "];\n";
+            emit_load("k", "xv", "            ");
+            body << "            for (int e = 0; e < " << V << "; ++e) m = m > xv[e] ? m : xv[e];\n        }\n";
+            block_reduce("m", true);
+            body << "        float s = 0.0f;\n";
+            body << "        for (" << I << " k = threadIdx.x * " << V << "u; k < " << lit(A, wide) << "; k += "
+                 << T * V << "u) {\n            float xv[" << V << "];\n";
+            emit_load("k", "xv", "            ");
+            body << "            for (int e = 0; e < " << V << "; ++e) s = s + __expf(xv[e] - m);\n        }\n";
+            block_reduce("s", false);
+            body << "        for (" << I << " k = threadIdx.x * " << V << "u; k < " << lit(A, wide) << "; k += "
+                 << T * V << "u) {\n            float xv[" << V << "];\n";
+            emit_load("k", "xv", "            ");
+            body << "            for (int e = 0; e < " << V << "; ++e) out[" << orow << " + k + e] = __expf(xv[e] - m) / s;\n        }\n";
+        }
+        body << "    }\n";
+        launch_spec l;
+        l.name = "pb_softmax_" + hex64(hash_string(src.str() + body.str())).substr(0, 8);
+        src << "extern \"C\" __global__ void __launch_bounds__(" << T << ") " << l.name << "(";
+        for (size_t i = 0; i < r.k.leaves.size(); ++i) src << "const float* __restrict__ in" << i << ", ";
+        src << "float* __restrict__ out) {\n" << body.str() << "}\n";
+        l.source = src.str();
+        const int64_t per_sm = 2048 / T;
+        l.grid = {static_cast<uint32_t>(std::min<int64_t>(rows, 148 * per_sm)), 1, 1};
+        l.block = {static_cast<uint32_t>(T), 1, 1};
+        l.schedule = "softmax row kernel T=" + std::to_string(T) + " V=" + std::to_string(V) +
+                     (in_registers ? " (row in registers, 1 read + 1 write)" : " (3-pass streaming)");
+        l.args = r.k.leaves;
+        kernel_arg o;
+        o.kind = arg_kind::temp;
+        o.index = out;
+        l.args.push_back(o);
+        finish_kernel(l);
+        p_.launches.push_back(std::move(l));
+        return out;
+    }
+
+    // ------------------------------------------------------------- GEMM --
+    int lowerer::emit_gemm(int id, int mm) {
+        const gnode& m = g_.nodes[static_cast<size_t>(mm)];
+        const gnode& root = g_.nodes[static_cast<size_t>(id)];
+        const int64_t M = m.shape[0], N = m.shape[1];
+        const int64_t K = g_.nodes[static_cast<size_t>(m.a)].shape[1];
+        // Epilogue over the output coordinates, accumulator at `mm`.
+        kernel k;
+        std::vector<box> boxes;
+        try {
+            boxes = build_boxes(k, id, root.shape, mm);
+        } catch (const not_fusable&) {
+            if (id != mm) return -1;
+            throw;
+        } catch (const not_affine&) {
+            return -1;
+        }
+        if (boxes.size() != 1) return -1;
+        const kernel_arg A = as_buffer(m.a);
+        const kernel_arg B = as_buffer(m.b);
+        if (const int t = emit_gemm_tc(id, boxes[0], k, A, B, M, N, K); t >= 0) return t;
+        return emit_gemm_simt(boxes[0], k, A, B, M, N, K);
+    }
+
+    int lowerer::emit_gemm_simt(const box& b, kernel& k, const kernel_arg& A, const kernel_arg& B,
+                                int64_t M, int64_t N, int64_t K) {
+        const int out = new_temp(static_cast<size_t>(M * N) * sizeof(float));
+        rank_ = 2;
+        const bool wide = M * N >= (int64_t{1} << 31) - 4096 || M * K >= (int64_t{1} << 31) - 4096 ||
+                          K * N >= (int64_t{1} << 31) - 4096;
+        const std::string I = wide ? "pb_u64" : "pb_u32";
+        std::vector<int> order;
+        std::ostringstream src;
+        src << kernel_prelude();
+        src << emit_expr_function(b, "0", order);
+        std::vector<std::string> cvar = {"r", "c"};
+        std::ostringstream body;
+        body << "    __shared__ float As[16][68];\n    __shared__ float Bs[16][68];\n";
+        body << "    const pb_u32 tx = threadIdx.x & 15u, ty = threadIdx.x >> 4;\n";
+        body << "    const " << I << " row0 = (" << I << ")blockIdx.y * 64u, col0 = (" << I << ")blockIdx.x * 64u;\n";
+        body << "    float acc[4][4];\n";
+        body << "    #pragma unroll\n    for (int i = 0; i < 4; ++i)\n        #pragma unroll\n        for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;\n";
+        body << "    for (" << I << " k0 = 0; k0 < " << lit(K, wide) << "; k0 += 16u) {\n";
+        body << "        #pragma unroll\n        for (int u = 0; u < 4; ++u) {\n";
+        body << "            const pb_u32 f = threadIdx.x + 256u * u;\n";
+        body << "            const pb_u32 ar = f >> 4, ak = f & 15u;\n";
+        body << "            As[ak][ar] = (row0 + ar < " << lit(M, wide) << " && k0 + ak < " << lit(K, wide)
+             << ") ? pb_ld(A + (row0 + ar) * " << lit(K, wide) << " + k0 + ak) : 0.0f;\n";
+        body << "            const pb_u32 bk = f >> 6, bc = f & 63u;\n";
+        body << "            Bs[bk][bc] = (k0 + bk < " << lit(K, wide) << " && col0 + bc < " << lit(N, wide)
+             << ") ? pb_ld(B + (k0 + bk) * " << lit(N, wide) << " + col0 + bc) : 0.0f;\n";
+        body << "        }\n        __syncthreads();\n";
+        body << "        const pb_u32 kmax = (" << lit(K, wide) << " - k0) < 16u ? (pb_u32)(" << lit(K, wide)
+             << " - k0) : 16u;\n";
+        body << "        for (pb_u32 kk = 0; kk < kmax; ++kk) {\n";
+        body << "            float a[4], bv[4];\n";
+        body << "            #pragma unroll\n            for (int i = 0; i < 4; ++i) { a[i] = As[kk][ty * 4u + i]; bv[i] = Bs[kk][tx * 4u + i]; }\n";
+        body << "            #pragma unroll\n            for (int i = 0; i < 4; ++i)\n                #pragma unroll\n                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], bv[j], acc[i][j]);\n";
+        body << "        }\n        __syncthreads();\n    }\n";
+        body << "    #pragma unroll\n    for (int i = 0; i < 4; ++i)\n        #pragma unroll\n        for (int j = 0; j < 4; ++j) {\n";
+        body << "            const " << I << " r = row0 + ty * 4u + i, c = col0 + tx * 4u + j;\n";
+        body << "            if (r < " << lit(M, wide) << " && c < " << lit(N, wide) << ") {\n";
+        for (size_t li = 0; li < order.size(); ++li) {
+            const vnode& v = b.nodes[static_cast<size_t>(order[li])];
+            body << "                const float x" << li << " = pb_ld(in" << v.buffer << " + " << address(v.map, cvar, wide, -1)
+                 << ");\n";
+        }
+        body << "                out[r * " << lit(N, wide) << " + c] = pb_e0(acc[i][j]";
+        for (size_t li = 0; li < order.size(); ++li) body << ", x" << li;
+        body << ");\n            }\n        }\n";
+        launch_spec l;
+        l.name = "pb_gemm_simt_" + hex64(hash_string(src.str() + body.str())).substr(0, 8);
+        src << "extern \"C\" __global__ void __launch_bounds__(256) " << l.name
+            << "(const float* __restrict__ A, const float* __restrict__ B, ";
+        for (size_t i = 0; i < k.leaves.size(); ++i) src << "const float* __restrict__ in" << i << ", ";
+        src << "float* __restrict__ out) {\n" << body.str() << "}\n";
+        l.source = src.str();
+        l.grid = {static_cast<uint32_t>((N + 63) / 64), static_cast<uint32_t>((M + 63) / 64), 1};
+        l.block = {256, 1, 1};
+        l.schedule = "gemm CUDA-core 64x64x16 tiles, k-ordered FMA chain, fused epilogue";
+        l.args.push_back(A);
+        l.args.push_back(B);
+        for (const kernel_arg& a : k.leaves) l.args.push_back(a);
+        kernel_arg o;
+        o.kind = arg_kind::temp;
+        o.index = out;
+        l.args.push_back(o);
+        finish_kernel(l);
+        p_.launches.push_back(std::move(l));
+        return out;
+    }
+
+    std::shared_ptr<plan> build_plan(const graph& g) {
+        auto p = std::make_shared<plan>();
+        lowerer low{g, *p};
+        p->result_temp = low.materialize(g.root);
+        p->out_shape = g.nodes[static_cast<size_t>(g.root)].shape;
+        return p;
+    }
+
+} // namespace porch::detail

@@ -1,0 +1,121 @@
+// Lowering internals shared by lower.cpp and the tensor-core GEMM emitter.
+#pragma once
+
+#include "plan.hpp"
+
+#include <map>
+#include <sstream>
+#include <string>
+#include <vector>
+
+namespace porch::detail {
+
+    // Integer affine map of the output (root) coordinates:
+    // value(c) = off + sum_d st[d] * c[d].
+    struct affine {
+        int64_t off = 0;
+        std::vector<int64_t> st;
+    };
+
+    // Where a node is evaluated: either as coordinates of the node's own
+    // shape (one affine map per dimension) or as a linear index into the
+    // node's contiguous layout.
+    struct position {
+        bool linear = false;
+        affine lin;
+        std::vector<affine> coords;
+    };
+
+    struct need_split {
+        int dim;
+        int64_t at;
+    };
+    struct not_affine {};
+    struct not_fusable {};
+
+    // Straight-line value graph of one output box.
+    struct vnode {
+        enum class op : uint8_t { load, scalar, acc, unary, binary } kind = op::scalar;
+        expr_kind ek = expr_kind::add;
+        int a = -1;
+        int b = -1;
+        int buffer = -1; // kernel leaf index
+        affine map;      // element index of the load
+        float scalar = 0.0F;
+    };
+
+    struct box {
+        std::vector<int64_t> lo;
+        std::vector<int64_t> hi;
+        std::vector<vnode> nodes;
+        int root = -1;
+    };
+
+    const char* kernel_prelude();
+
+    class lowerer {
+      public:
+        lowerer(const graph& g, plan& p);
+        int materialize(int id);
+
+        struct kernel {
+            std::vector<kernel_arg> leaves;
+            int leaf(arg_kind kind, int index);
+        };
+
+      private:
+        struct row_operand {
+            kernel k;
+            box b;
+            std::vector<index_t> shape;
+        };
+
+        int new_temp(size_t bytes);
+        bool match_softmax(int id, int& x, size_t& axis) const;
+        bool is_barrier(int id) const;
+        int match_gemm(int id) const;
+        kernel_arg as_buffer(int id);
+
+        static std::string pos_key(const position& p);
+        affine to_linear(const position& p, const std::vector<index_t>& shape) const;
+        std::vector<affine> to_coords(const position& p, const std::vector<index_t>& shape,
+                                      const box& b) const;
+        static int push(box& b, vnode v);
+        int build(kernel& k, box& b, int id, const position& pos, int acc_id,
+                  std::map<std::string, int>& memo);
+        std::vector<box> build_boxes(kernel& k, int root, const std::vector<index_t>& shape,
+                                     int acc_id);
+
+        std::string emit_expr_function(const box& b, const std::string& tag,
+                                       std::vector<int>& load_order) const;
+        bool needs_wide(const std::vector<box>& boxes, const std::vector<index_t>& shape) const;
+        std::string address(const affine& a, const std::vector<std::string>& cvar, bool wide,
+                            int skip_dim) const;
+        std::string emit_row_box(const box& b, int tag, const std::vector<index_t>& shape,
+                                 bool wide, int64_t& ctas, std::string& desc) const;
+        std::string emit_tile_box(const box& b, int tag, const std::vector<index_t>& shape,
+                                  bool wide, int p, int64_t& ctas, int& smem_tiles,
+                                  std::string& desc) const;
+        static void finish_kernel(launch_spec& l);
+
+        int emit_elementwise(int id);
+        std::string gen_value(kernel& k, int id, const std::string& idx,
+                              std::ostringstream& stmts, int& counter);
+        int emit_generic(int id);
+        row_operand row_prologue(int operand, size_t axis);
+        int emit_reduce(int id);
+        int emit_softmax(int id, int x);
+        int emit_gemm(int id, int mm);
+        int emit_gemm_simt(const box& b, kernel& k, const kernel_arg& A, const kernel_arg& B,
+                           int64_t M, int64_t N, int64_t K);
+        // tcgen05 3xTF32 path; returns -1 when the shape is not eligible.
+        int emit_gemm_tc(int id, const box& b, kernel& k, const kernel_arg& A,
+                         const kernel_arg& B, int64_t M, int64_t N, int64_t K);
+
+        const graph& g_;
+        plan& p_;
+        std::map<int, int> done_;
+        int rank_ = 0;
+    };
+
+} // namespace porch::detail

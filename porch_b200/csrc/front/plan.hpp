@@ -1,0 +1,93 @@
+// Canonical graphs, lowering plans and kernel launch descriptions.
+//
+// A porch expression tree is value-numbered into a `graph` (common
+// subexpressions merged, inputs numbered into slots by storage identity).
+// The graph's 64-bit structural hash keys a process-wide plan cache, so a
+// graph shape seen before skips lowering, code generation and NVRTC entirely
+// and costs one hash walk plus its launches.
+#pragma once
+
+#include "detail.hpp"
+
+#include <array>
+#include <map>
+#include <string>
+#include <vector>
+
+namespace porch::detail {
+
+    struct gnode {
+        expr_kind kind = expr_kind::scalar;
+        int a = -1;
+        int b = -1;
+        int slot = -1;
+        float scalar = 0.0F;
+        bool is_scalar = false;
+        std::vector<index_t> shape;     // inferred output shape
+        std::vector<index_t> p_shape;   // slice shape / reshape+broadcast target
+        std::vector<index_t> p_strides; // slice strides
+        index_t p_offset = 0;           // slice offset
+        size_t axis = 0;
+        bool keepdim = false;
+    };
+
+    struct graph {
+        std::vector<gnode> nodes;
+        int root = -1;
+        std::vector<std::shared_ptr<realized_storage>> slots;
+        std::vector<std::vector<index_t>> slot_shapes;
+        std::vector<int> uses; // number of parents per node
+        uint64_t hash = 0;
+        std::string key; // full structural key (verifies plan-cache hash hits)
+    };
+
+    graph canonicalize(const tensor_expr::node& root);
+
+    // ---------------------------------------------------------- launches --
+    enum class arg_kind : uint8_t {
+        slot,       // pointer to an input slot's device values
+        temp,       // pointer to a plan temporary
+        error_word, // pointer to the device's error block
+        u64,        // immediate
+    };
+
+    struct kernel_arg {
+        arg_kind kind = arg_kind::u64;
+        int index = 0;
+        uint64_t value = 0;
+    };
+
+    struct launch_spec {
+        std::string name;      // kernel entry point
+        std::string source;    // full NVRTC source
+        std::string schedule;  // one-line description for plan dumps
+        uint64_t image_key = 0;
+        std::array<uint32_t, 3> grid{1, 1, 1};
+        std::array<uint32_t, 3> block{256, 1, 1};
+        uint32_t smem = 0;
+        std::vector<kernel_arg> args;
+        // Resolved function handle per device (filled on first launch).
+        std::array<pbrt_function, 16> functions{};
+        std::mutex* resolve_mutex = nullptr;
+    };
+
+    struct plan {
+        std::vector<size_t> temp_bytes;
+        int result_temp = -1;
+        std::vector<launch_spec> launches;
+        std::vector<index_t> out_shape;
+        std::mutex resolve_mutex;
+    };
+
+    // Builds the plan for `g` (lowering + code generation + NVRTC compile).
+    std::shared_ptr<plan> build_plan(const graph& g);
+
+    // NVRTC options used for every generated kernel: sm_100a cubin, IEEE
+    // division and square root, no FMA contraction (bit-exact elementwise
+    // arithmetic against the host oracle), no flush-to-zero.
+    const std::vector<std::string>& kernel_options();
+
+    // Formats a float as an exact CUDA literal.
+    std::string float_literal(float v);
+
+} // namespace porch::detail
