@@ -265,6 +265,8 @@ def run_ours(args, rank, world, local, dist):
 
     api.profile_enable(True)
     api.profile_read()  # clear
+    api.host_profile_enable(True)
+    api.host_profile_read()  # clear
     barrier(dist)
     api.device_synchronize(device)
     launches0 = api.launch_count()
@@ -279,6 +281,8 @@ def run_ours(args, rank, world, local, dist):
     launches = api.launch_count() - launches0
     prof = api.profile_read()
     api.profile_enable(False)
+    host = api.host_profile_read()
+    api.host_profile_enable(False)
     barrier(dist)
     ms_rank = timer.ms / args.steps
     ms = max_over_ranks(dist, ms_rank)
@@ -360,6 +364,7 @@ def run_ours(args, rank, world, local, dist):
             "cpu_baseline": cpu,
             "clocks": clocks.summary(),
             "kernels": {k: {"launches": n, "ms": round(t, 4)} for k, (n, t) in prof.items()},
+            "host_us_per_materialize": {k: round(v, 2) for k, v in host.items()},
         }
         print(json.dumps(line), flush=True)
 

@@ -162,6 +162,11 @@ uint64_t pb_launch_count(void);
  * pbrt_profile_read for the text format. */
 int pb_profile_enable(int enable);
 int pb_profile_read(char* text, size_t capacity);
+/* Host-side phase timers of materialize (bind = inference, canonical graph
+ * and plan lookup; inputs = stream ordering and allocations; launch; wrap).
+ * Read returns "<phase>_us_per_call<TAB><value>" lines and resets. */
+int pb_host_profile_enable(int enable);
+int pb_host_profile_read(char* text, size_t capacity);
 /* Fills `values` (count floats) with seeded synthetic data: dist 0 = uniform
  * on [a, b), dist 1 = normal(mean a, stddev b). Deterministic for a given
  * (seed, count, dist, a, b), independent of thread count. Host side only. */

@@ -82,6 +82,8 @@ def _declare(L: ctypes.CDLL) -> None:
         "pb_launch_count": (c_uint64, []),
         "pb_profile_enable": (c_int, [c_int]),
         "pb_profile_read": (c_int, [c_char_p, c_size_t]),
+        "pb_host_profile_enable": (c_int, [c_int]),
+        "pb_host_profile_read": (c_int, [c_char_p, c_size_t]),
         "pb_fill_synthetic": (c_int, [c_void_p, c_size_t, c_uint64, c_int, c_double, c_double]),
         "pbrt_available": (c_int, []),
         "pbrt_device_count": (c_int, [P(c_int)]),

@@ -490,6 +490,20 @@ def profile_read() -> dict[str, tuple[int, float]]:
     return out
 
 
+def host_profile_enable(on: bool = True) -> None:
+    _check(lib().pb_host_profile_enable(int(on)))
+
+
+def host_profile_read() -> dict[str, float]:
+    buf = ctypes.create_string_buffer(4096)
+    _check(lib().pb_host_profile_read(buf, len(buf)))
+    out = {}
+    for line in buf.value.decode().splitlines():
+        k, v = line.split("\t")
+        out[k] = float(v)
+    return out
+
+
 class DeviceTimer:
     """CUDA events on this thread's porch stream of `device`."""
 

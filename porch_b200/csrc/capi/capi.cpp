@@ -462,6 +462,21 @@ int pb_device_synchronize(int device) {
 
 uint64_t pb_launch_count(void) { return pbrt_launch_count(); }
 
+int pb_host_profile_enable(int enable) {
+    return guarded([&] { porch::detail::host_profile_enable(enable != 0); });
+}
+
+int pb_host_profile_read(char* text, size_t capacity) {
+    return guarded([&] {
+        const std::string s = porch::detail::host_profile_read();
+        if (text != nullptr && capacity > 0) {
+            const size_t n = std::min(s.size(), capacity - 1);
+            std::memcpy(text, s.data(), n);
+            text[n] = '\0';
+        }
+    });
+}
+
 int pb_profile_enable(int enable) {
     return guarded([&] { porch::detail::check(pbrt_profile_enable(enable)); });
 }

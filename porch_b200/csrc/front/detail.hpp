@@ -154,6 +154,10 @@ namespace porch {
         index_t slice_offset = 0;
         size_t axis = 0;
         bool keepdim = false;
+        // Lowering bound to this exact root (canonical graph + plan), filled
+        // on its first materialisation so repeat realisations of the same
+        // expression skip inference, canonicalisation and plan lookup.
+        mutable std::shared_ptr<const void> bound;
     };
 
     struct expr_access {
@@ -208,6 +212,12 @@ namespace porch::detail {
     // Lower, compile and launch `root`; the result is a realised tensor on the
     // graph's device (src/tensor.cpp:1002-1066 is the reference's driver).
     tensor materialize_graph(const tensor_expr::node& root);
+
+    // Host-side phase timers of materialize (nanoseconds): enabled by
+    // host_profile_enable; read and reset by host_profile_read.
+    enum host_phase { phase_bind, phase_inputs, phase_launch, phase_wrap, phase_total, phase_count };
+    void host_profile_enable(bool on);
+    std::string host_profile_read();
 
     // Human-readable description of the plan chosen for `root` (kernels,
     // schedules and generated sources). Works on placeholder inputs without a

@@ -8,6 +8,8 @@
 // launches.
 #include "plan.hpp"
 
+#include <atomic>
+#include <chrono>
 #include <cstring>
 #include <sstream>
 #include <stdexcept>
@@ -221,23 +223,83 @@ namespace porch::detail {
 
     bool placeholder_mode() { return false; }
 
-    tensor materialize_graph(const tensor_expr::node& root) {
-        shape_info info = infer(root);
-        if (!info.has_input)
-            throw std::invalid_argument("tensor expression must reference at least one tensor");
-        if (info.scalar)
-            throw std::invalid_argument("scalar expression cannot materialize to a tensor");
+    namespace {
 
-        const size_t count = checked_numel(info.shape);
-        graph g = canonicalize(root);
-        int device = -1;
-        for (const auto& s : g.slots) {
-            if (s->placeholder)
-                throw std::runtime_error(
-                    "placeholder tensors can only be used to describe plans");
-            if (device < 0) device = s->device;
+        struct bound_graph {
+            graph g;
+            std::shared_ptr<plan> p;
+            shape_info info;
+            int device = 0;
+        };
+
+        struct host_profiler {
+            std::atomic<bool> on{false};
+            std::atomic<uint64_t> ns[phase_count]{};
+            std::atomic<uint64_t> calls{0};
+        };
+
+        host_profiler& hprof() {
+            static host_profiler* h = new host_profiler();
+            return *h;
         }
-        if (device < 0) device = 0;
+
+        uint64_t now_ns() {
+            return static_cast<uint64_t>(std::chrono::duration_cast<std::chrono::nanoseconds>(
+                                             std::chrono::steady_clock::now().time_since_epoch())
+                                             .count());
+        }
+
+        std::shared_ptr<const bound_graph> bind(const tensor_expr::node& root) {
+            auto cached = std::static_pointer_cast<const bound_graph>(std::atomic_load(&root.bound));
+            if (cached) return cached;
+            auto b = std::make_shared<bound_graph>();
+            b->info = infer(root);
+            if (!b->info.has_input)
+                throw std::invalid_argument("tensor expression must reference at least one tensor");
+            if (b->info.scalar)
+                throw std::invalid_argument("scalar expression cannot materialize to a tensor");
+            b->g = canonicalize(root);
+            int device = -1;
+            for (const auto& s : b->g.slots) {
+                if (s->placeholder)
+                    throw std::runtime_error("placeholder tensors can only be used to describe plans");
+                if (device < 0) device = s->device;
+            }
+            b->device = device < 0 ? 0 : device;
+            if (checked_numel(b->info.shape) != 0) b->p = lookup_plan(b->g);
+            std::shared_ptr<const void> erased = b;
+            std::atomic_store(&root.bound, erased);
+            return b;
+        }
+
+    } // namespace
+
+    void host_profile_enable(bool on) { hprof().on.store(on); }
+
+    std::string host_profile_read() {
+        host_profiler& h = hprof();
+        static const char* names[phase_count] = {"bind", "inputs", "launch", "wrap", "total"};
+        std::ostringstream os;
+        const uint64_t calls = h.calls.exchange(0);
+        os << "materialize_calls\t" << calls << "\n";
+        for (int i = 0; i < phase_count; ++i) {
+            const uint64_t v = h.ns[i].exchange(0);
+            os << names[i] << "_us_per_call\t" << (calls ? double(v) / 1000.0 / double(calls) : 0.0)
+               << "\n";
+        }
+        return os.str();
+    }
+
+    tensor materialize_graph(const tensor_expr::node& root) {
+        host_profiler& hp = hprof();
+        const bool timing = hp.on.load(std::memory_order_relaxed);
+        uint64_t t0 = timing ? now_ns() : 0, t1 = 0, t2 = 0, t3 = 0;
+
+        std::shared_ptr<const bound_graph> b = bind(root);
+        const graph& g = b->g;
+        const int device = b->device;
+        const size_t count = checked_numel(b->info.shape);
+        if (timing) t1 = now_ns();
 
         auto storage = std::make_shared<realized_storage>();
         storage->count = count;
@@ -247,11 +309,10 @@ namespace porch::detail {
             // Empty result: no launch (src/tensor.cpp:1023-1028).
             storage->device_values = allocate(device, 0, stream);
             storage->host_current = true;
-            return tensor_access::from_storage(std::move(info.shape), std::move(storage),
-                                               info.placement);
+            return tensor_access::from_storage(b->info.shape, std::move(storage),
+                                               b->info.placement);
         }
-
-        std::shared_ptr<plan> p = lookup_plan(g);
+        plan* p = b->p.get();
 
         for (const auto& s : g.slots) {
             const auto& st = cuda_jit::buffer_access::state(s->device_values);
@@ -265,10 +326,11 @@ namespace porch::detail {
         std::vector<cuda_jit::device_buffer> temps;
         temps.reserve(p->temp_bytes.size());
         for (size_t bytes : p->temp_bytes) temps.push_back(allocate(device, bytes, stream));
+        if (timing) t2 = now_ns();
 
         uint64_t error_word = 0;
-        std::vector<uint64_t> values;
-        std::vector<void*> params;
+        uint64_t values[64];
+        void* params[64];
         for (launch_spec& l : p->launches) {
             pbrt_function fn = nullptr;
             if (device < static_cast<int>(l.functions.size())) fn = l.functions[device];
@@ -279,8 +341,7 @@ namespace porch::detail {
                     check(pbrt_function_set_max_dynamic_smem(fn, static_cast<int>(l.smem)));
                 if (device < static_cast<int>(l.functions.size())) l.functions[device] = fn;
             }
-            values.assign(l.args.size(), 0);
-            params.assign(l.args.size(), nullptr);
+            if (l.args.size() > 64) throw std::runtime_error("kernel has too many arguments");
             for (size_t i = 0; i < l.args.size(); ++i) {
                 const kernel_arg& a = l.args[i];
                 switch (a.kind) {
@@ -305,13 +366,24 @@ namespace porch::detail {
                 params[i] = &values[i];
             }
             check(pbrt_launch(device, fn, l.grid.data(), l.block.data(), l.smem,
-                              stream->stream, params.data(), nullptr));
+                              stream->stream, params, nullptr));
         }
+        if (timing) t3 = now_ns();
 
         storage->device_values = temps[static_cast<size_t>(p->result_temp)];
         set_producer(*cuda_jit::buffer_access::state(storage->device_values), stream);
-        return tensor_access::from_storage(std::move(info.shape), std::move(storage),
-                                           info.placement);
+        tensor result = tensor_access::from_storage(b->info.shape, std::move(storage),
+                                                    b->info.placement);
+        if (timing) {
+            const uint64_t t4 = now_ns();
+            hp.ns[phase_bind] += t1 - t0;
+            hp.ns[phase_inputs] += t2 - t1;
+            hp.ns[phase_launch] += t3 - t2;
+            hp.ns[phase_wrap] += t4 - t3;
+            hp.ns[phase_total] += t4 - t0;
+            hp.calls += 1;
+        }
+        return result;
     }
 
     std::string describe_plan(const tensor_expr::node& root, bool with_source) {

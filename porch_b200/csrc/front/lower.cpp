@@ -44,7 +44,7 @@ namespace porch::detail {
         static const std::vector<std::string> options = {
             "--gpu-architecture=sm_100a", "-std=c++17", "--fmad=false",
             "--prec-div=true", "--prec-sqrt=true", "--ftz=false", "-lineinfo",
-            "-DPB_NVRTC=1"};
+            "--diag-suppress=177", "-DPB_NVRTC=1"};
         return options;
     }
 
@@ -1251,6 +1251,9 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
                 body << "    const " << I << " c" << d << " = t % " << lit(S[static_cast<size_t>(d)], wide) << "; t /= "
                      << lit(S[static_cast<size_t>(d)], wide) << ";\n";
             }
+            // Dimensions after the axis all have extent 1 here.
+            for (int d = static_cast<int>(ax) + 1; d < R; ++d)
+                body << "    const " << I << " c" << d << " = 0;\n";
             body << "    float acc = " << init << ";\n";
             body << "    for (" << I << " k = lane * " << V << "u; k < " << lit(A, wide) << "; k += " << 32 * V << "u) {\n";
             body << "        const " << I << " c" << ax << " = k;\n";

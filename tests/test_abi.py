@@ -109,10 +109,11 @@ def test_benchmark_plans(api):
     assert "softmax" in kernels["c5_mlp"][-1]
 
 
-@pytest.mark.parametrize("seed", range(60))
+@pytest.mark.parametrize("seed", list(range(120)) + list(range(2000, 2200)))
 def test_fuzz_plans_compile_for_sm100a(api, seed):
-    """Every lowering of a random program compiles with NVRTC for sm_100a."""
-    text, ins, _ = graphs.random_program(2000 + seed, integer_values=False)
+    """Every lowering of a random program compiles with NVRTC for sm_100a
+    (seeds 0..119 are the programs the GPU parity tests run)."""
+    text, ins, _ = graphs.random_program(seed, integer_values=seed % 2 == 0)
     tensors = [api.placeholder(list(a.shape)) for a in ins]
     orig = api.tensor
     try:
