@@ -156,6 +156,10 @@ int pb_timer_begin(int device, void** timer);
 int pb_timer_end(void* timer, float* milliseconds);
 /* Synchronise this thread's porch stream on `device`. */
 int pb_device_synchronize(int device);
+/* Returns every cached device block of `device` to the driver's pool
+ * (*released receives the bytes; may be NULL). Blocks freed by porch stay
+ * cached per stream for reuse without a driver call until then. */
+int pb_empty_cache(int device, size_t* released);
 /* Kernel launches issued by this library since process start. */
 uint64_t pb_launch_count(void);
 /* Per-launch kernel timing (events around each launch); see

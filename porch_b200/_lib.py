@@ -80,6 +80,7 @@ def _declare(L: ctypes.CDLL) -> None:
         "pb_timer_end": (c_int, [c_void_p, P(c_float)]),
         "pb_device_synchronize": (c_int, [c_int]),
         "pb_launch_count": (c_uint64, []),
+        "pb_empty_cache": (c_int, [c_int, P(c_size_t)]),
         "pb_profile_enable": (c_int, [c_int]),
         "pb_profile_read": (c_int, [c_char_p, c_size_t]),
         "pb_host_profile_enable": (c_int, [c_int]),

@@ -462,6 +462,13 @@ int pb_device_synchronize(int device) {
 
 uint64_t pb_launch_count(void) { return pbrt_launch_count(); }
 
+int pb_empty_cache(int device, size_t* released) {
+    return guarded([&] {
+        const size_t n = porch::detail::release_cached_blocks(device);
+        if (released) *released = n;
+    });
+}
+
 int pb_host_profile_enable(int enable) {
     return guarded([&] { porch::detail::host_profile_enable(enable != 0); });
 }

@@ -54,6 +54,7 @@ namespace porch::cuda_jit {
         int device = 0;
         uint64_t ptr = 0;
         size_t bytes = 0;
+        size_t capacity = 0; // allocator size class; 0 = not from the cache
         std::mutex mutex;
         std::shared_ptr<detail::stream_ref> producer;
         std::vector<std::shared_ptr<detail::stream_ref>> readers;
@@ -81,10 +82,15 @@ namespace porch::cuda_jit {
 
 namespace porch::detail {
 
-    // Allocates `bytes` on `device`, stream-ordered on `stream`.
+    // Allocates `bytes` on `device`, stream-ordered on `stream`, from the
+    // per-device caching allocator.
     cuda_jit::device_buffer allocate(
         int device, size_t bytes, const std::shared_ptr<stream_ref>& stream
     );
+    // Returns a block to the cache (called when its last owner drops it).
+    void recycle(int device, uint64_t ptr, size_t capacity, std::shared_ptr<stream_ref> stream);
+    // Gives every cached block of `device` back to the driver; returns bytes.
+    size_t release_cached_blocks(int device);
     // Makes `stream` wait for the buffer's producer when they differ, and
     // records `stream` as a reader so the eventual free is ordered after it.
     void order_read(

@@ -13,6 +13,7 @@
 #include <map>
 #include <sstream>
 #include <stdexcept>
+#include <unordered_map>
 
 namespace porch::detail {
 
@@ -65,6 +66,64 @@ namespace porch::detail {
         return out;
     }
 
+    // ------------------------------------------------- caching allocator --
+    // Freed blocks are kept per device in size classes together with the
+    // stream they were last used on; a request on that same stream reuses one
+    // with no driver call (stream order already makes it safe). Blocks seen by
+    // other streams go back to the driver's stream-ordered pool instead. On
+    // allocation failure every cached block of the device is returned to the
+    // driver and the request retried once.
+    namespace {
+        struct cached_block {
+            uint64_t ptr;
+            std::shared_ptr<stream_ref> stream;
+        };
+
+        struct device_cache {
+            std::mutex mutex;
+            std::unordered_map<size_t, std::vector<cached_block>> free;
+            size_t cached_bytes = 0;
+        };
+
+        struct block_cache {
+            std::mutex mutex;
+            std::vector<std::unique_ptr<device_cache>> devices;
+            device_cache& of(int device) {
+                std::scoped_lock lock{mutex};
+                if (devices.size() <= static_cast<size_t>(device))
+                    devices.resize(static_cast<size_t>(device) + 1);
+                auto& d = devices[static_cast<size_t>(device)];
+                if (!d) d = std::make_unique<device_cache>();
+                return *d;
+            }
+        };
+
+        block_cache& blocks() {
+            static block_cache* c = new block_cache(); // lives until exit
+            return *c;
+        }
+
+        size_t size_class(size_t bytes) {
+            if (bytes <= (size_t{1} << 20)) return (bytes + 511) & ~size_t{511};
+            return (bytes + (size_t{2} << 20) - 1) & ~((size_t{2} << 20) - 1);
+        }
+    } // namespace
+
+    size_t release_cached_blocks(int device) {
+        device_cache& dc = blocks().of(device);
+        std::unordered_map<size_t, std::vector<cached_block>> drop;
+        size_t bytes = 0;
+        {
+            std::scoped_lock lock{dc.mutex};
+            drop.swap(dc.free);
+            bytes = dc.cached_bytes;
+            dc.cached_bytes = 0;
+        }
+        for (auto& [size, list] : drop)
+            for (auto& b : list) (void)pbrt_mem_free_async(device, b.ptr, b.stream->stream);
+        return bytes;
+    }
+
     cuda_jit::device_buffer allocate(
         int device, size_t bytes, const std::shared_ptr<stream_ref>& stream
     ) {
@@ -72,10 +131,40 @@ namespace porch::detail {
         state->device = device;
         state->bytes = bytes;
         if (bytes != 0) {
-            check(pbrt_mem_alloc_async(device, bytes, stream->stream, &state->ptr));
+            const size_t cls = size_class(bytes);
+            state->capacity = cls;
+            device_cache& dc = blocks().of(device);
+            {
+                std::scoped_lock lock{dc.mutex};
+                auto it = dc.free.find(cls);
+                if (it != dc.free.end()) {
+                    auto& list = it->second;
+                    for (size_t i = list.size(); i > 0; --i) {
+                        if (list[i - 1].stream == stream) {
+                            state->ptr = list[i - 1].ptr;
+                            list.erase(list.begin() + static_cast<ptrdiff_t>(i - 1));
+                            dc.cached_bytes -= cls;
+                            break;
+                        }
+                    }
+                }
+            }
+            if (state->ptr == 0) {
+                int st = pbrt_mem_alloc_async(device, cls, stream->stream, &state->ptr);
+                if (st != PBRT_OK && release_cached_blocks(device) != 0)
+                    st = pbrt_mem_alloc_async(device, cls, stream->stream, &state->ptr);
+                check(st);
+            }
             state->producer = stream;
         }
         return cuda_jit::buffer_access::wrap(std::move(state));
+    }
+
+    void recycle(int device, uint64_t ptr, size_t capacity, std::shared_ptr<stream_ref> stream) {
+        device_cache& dc = blocks().of(device);
+        std::scoped_lock lock{dc.mutex};
+        dc.free[capacity].push_back({ptr, std::move(stream)});
+        dc.cached_bytes += capacity;
     }
 
     void order_read(
@@ -120,7 +209,14 @@ namespace porch::cuda_jit {
         try {
             std::shared_ptr<detail::stream_ref> free_stream =
                 producer != nullptr ? producer : detail::current_stream(device);
-            // Order the free after every reader on another stream.
+            bool foreign = false;
+            for (const auto& reader : readers) foreign = foreign || reader != free_stream;
+            if (!foreign && capacity != 0) {
+                // Only this stream ever touched it: keep it for reuse.
+                detail::recycle(device, ptr, capacity, std::move(free_stream));
+                return;
+            }
+            // Order the driver free after every reader on another stream.
             for (const auto& reader : readers) {
                 if (reader == free_stream) continue;
                 pbrt_event e = nullptr;
