@@ -257,11 +257,18 @@ def run_ours(args, rank, world, local, dist):
     def step(i):
         return api.materialize(graphs[i % n_sets])
 
+    def run_steps(n, outs):
+        # At most three results alive at once, in warm-up and timing alike,
+        # so the timed steps see the allocator state warm-up left behind.
+        for i in range(n):
+            outs.append(step(i))
+            if len(outs) > 2:
+                outs.pop(0)
+
     # Warm-up (first call lowers + compiles; later calls hit the plan cache).
-    for i in range(max(3, args.warmup)):
-        out = step(i)
+    outs = []
+    run_steps(max(3, args.warmup), outs)
     api.device_synchronize(device)
-    del out
 
     api.profile_enable(True)
     api.profile_read()  # clear
@@ -270,13 +277,9 @@ def run_ours(args, rank, world, local, dist):
     barrier(dist)
     api.device_synchronize(device)
     launches0 = api.launch_count()
-    outs = []
     with ClockSampler(device) as clocks:
         with api.DeviceTimer(device) as timer:
-            for i in range(args.steps):
-                outs.append(step(i))
-                if len(outs) > 2:
-                    outs.pop(0)
+            run_steps(args.steps, outs)
         api.device_synchronize(device)
     launches = api.launch_count() - launches0
     prof = api.profile_read()

@@ -221,7 +221,17 @@ namespace porch::detail {
 
     // Host-side phase timers of materialize (nanoseconds): enabled by
     // host_profile_enable; read and reset by host_profile_read.
-    enum host_phase { phase_bind, phase_inputs, phase_launch, phase_wrap, phase_total, phase_count };
+    enum host_phase {
+        phase_bind,
+        phase_stream,
+        phase_order,
+        phase_alloc,
+        phase_launch,
+        phase_wrap,
+        phase_total,
+        phase_count
+    };
+    void host_count(const char* what); // allocator hit/miss counters
     void host_profile_enable(bool on);
     std::string host_profile_read();
 

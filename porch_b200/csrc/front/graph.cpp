@@ -236,6 +236,8 @@ namespace porch::detail {
             std::atomic<bool> on{false};
             std::atomic<uint64_t> ns[phase_count]{};
             std::atomic<uint64_t> calls{0};
+            std::mutex counter_mutex;
+            std::map<std::string, uint64_t> counters;
         };
 
         host_profiler& hprof() {
@@ -276,12 +278,25 @@ namespace porch::detail {
 
     void host_profile_enable(bool on) { hprof().on.store(on); }
 
+    void host_count(const char* what) {
+        host_profiler& h = hprof();
+        if (!h.on.load(std::memory_order_relaxed)) return;
+        std::scoped_lock lock{h.counter_mutex};
+        ++h.counters[what];
+    }
+
     std::string host_profile_read() {
         host_profiler& h = hprof();
-        static const char* names[phase_count] = {"bind", "inputs", "launch", "wrap", "total"};
+        static const char* names[phase_count] = {"bind", "stream", "order", "alloc",
+                                                 "launch", "wrap", "total"};
         std::ostringstream os;
         const uint64_t calls = h.calls.exchange(0);
         os << "materialize_calls\t" << calls << "\n";
+        {
+            std::scoped_lock lock{h.counter_mutex};
+            for (const auto& [k, v] : h.counters) os << k << "\t" << v << "\n";
+            h.counters.clear();
+        }
         for (int i = 0; i < phase_count; ++i) {
             const uint64_t v = h.ns[i].exchange(0);
             os << names[i] << "_us_per_call\t" << (calls ? double(v) / 1000.0 / double(calls) : 0.0)
@@ -293,7 +308,7 @@ namespace porch::detail {
     tensor materialize_graph(const tensor_expr::node& root) {
         host_profiler& hp = hprof();
         const bool timing = hp.on.load(std::memory_order_relaxed);
-        uint64_t t0 = timing ? now_ns() : 0, t1 = 0, t2 = 0, t3 = 0;
+        uint64_t t0 = timing ? now_ns() : 0, t1 = 0, t2 = 0, t3 = 0, ta = 0, tb = 0;
 
         std::shared_ptr<const bound_graph> b = bind(root);
         const graph& g = b->g;
@@ -313,6 +328,7 @@ namespace porch::detail {
                                                b->info.placement);
         }
         plan* p = b->p.get();
+        if (timing) ta = now_ns();
 
         for (const auto& s : g.slots) {
             const auto& st = cuda_jit::buffer_access::state(s->device_values);
@@ -322,6 +338,7 @@ namespace porch::detail {
                 throw std::invalid_argument("tensor expression devices must match");
             order_read(*st, stream);
         }
+        if (timing) tb = now_ns();
 
         std::vector<cuda_jit::device_buffer> temps;
         temps.reserve(p->temp_bytes.size());
@@ -377,7 +394,9 @@ namespace porch::detail {
         if (timing) {
             const uint64_t t4 = now_ns();
             hp.ns[phase_bind] += t1 - t0;
-            hp.ns[phase_inputs] += t2 - t1;
+            hp.ns[phase_stream] += ta - t1;
+            hp.ns[phase_order] += tb - ta;
+            hp.ns[phase_alloc] += t2 - tb;
             hp.ns[phase_launch] += t3 - t2;
             hp.ns[phase_wrap] += t4 - t3;
             hp.ns[phase_total] += t4 - t0;

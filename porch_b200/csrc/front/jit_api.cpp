@@ -149,6 +149,7 @@ namespace porch::detail {
                     }
                 }
             }
+            host_count(state->ptr ? "alloc_cache_hit" : "alloc_cache_miss");
             if (state->ptr == 0) {
                 int st = pbrt_mem_alloc_async(device, cls, stream->stream, &state->ptr);
                 if (st != PBRT_OK && release_cached_blocks(device) != 0)
@@ -176,6 +177,7 @@ namespace porch::detail {
             std::scoped_lock lock{buffer.mutex};
             producer = buffer.producer;
             if (producer == nullptr || producer == stream) return;
+            host_count("order_read_cross_stream");
             bool known = false;
             for (const auto& r : buffer.readers) known = known || r == stream;
             if (!known) buffer.readers.push_back(stream);
