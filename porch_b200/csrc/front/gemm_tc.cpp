@@ -1,12 +1,395 @@
-// tcgen05 3xTF32 GEMM emitter (placeholder until the tensor-core path lands:
-// every GEMM currently takes the CUDA-core path).
+// tcgen05 / TMEM 3xTF32 GEMM with a fused elementwise epilogue (sm_100a).
+//
+// C[M,N] = epilogue(A[M,K] @ B[K,N], leaves...) in fp32 accuracy from
+// TF32 tensor-core products (Ootomo & Yokota, "Recovering single precision
+// accuracy from Tensor Cores while surpassing the FP32 theoretical peak
+// performance", 2022): x = hi + lo with hi = x truncated to TF32 (exact
+// split, so x - hi is exact in fp32) and lo = round-to-nearest TF32 of
+// x - hi; C ~= Ahi*Bhi + Ahi*Blo + Alo*Bhi (the lo*lo term is below fp32
+// resolution and dropped).
+//
+// Launches:
+//  1. pb_split_rows:      A [M,K]  -> Ahi, Alo [M,K]      (K-major as is)
+//  2. pb_split_transpose: B [K,N]  -> Bhi, Blo [N,K]      (to K-major)
+//  3. pb_gemm_tc:         one 128x256 output tile per CTA, 128 threads.
+//     warp 0 lane 0 issues TMA loads (128B swizzle, BK = 32 fp32) into a
+//     2-stage ring of {Ahi, Alo, Bhi, Blo} tiles (96 KB per stage); warp 1
+//     allocates 256 TMEM columns and its lane 0 issues tcgen05.mma
+//     (kind::tf32, M=128, N=256, K=8; 3 products x 4 k-steps per stage),
+//     committing each stage back to the producer and the last one to the
+//     epilogue barrier; then all four warps read the accumulator with
+//     tcgen05.ld (warp w owns TMEM lanes 32w..32w+31 = tile rows), apply the
+//     fused epilogue and store.
+// Every mbarrier wait is bounded (clock64 budget); on expiry the kernel
+// records a code in the device error word, stops issuing, waits (bounded)
+// for its own copies and MMAs in flight, frees its TMEM and returns.
+// No TMA multicast is used anywhere.
 #include "lower.hpp"
+
+#include <cstdlib>
+#include <sstream>
 
 namespace porch::detail {
 
-    int lowerer::emit_gemm_tc(int, const box&, kernel&, const kernel_arg&, const kernel_arg&,
-                              int64_t, int64_t, int64_t) {
-        return -1;
+    namespace {
+
+        constexpr int kBM = 128;
+        constexpr int kBN = 256;
+        constexpr int kBK = 32;
+
+        const char* gemm_device_source() {
+            return R"PB(
+#define PB_BM 128
+#define PB_BN 256
+#define PB_BK 32
+#define PB_STAGES 2
+#define PB_TILE_A_BYTES (PB_BM * PB_BK * 4)
+#define PB_TILE_B_BYTES (PB_BN * PB_BK * 4)
+#define PB_STAGE_BYTES (2 * PB_TILE_A_BYTES + 2 * PB_TILE_B_BYTES)
+#define PB_WAIT_CYCLES 4000000000ll
+
+struct __align__(64) pb_tmap { unsigned long long opaque[16]; };
+
+static __device__ __forceinline__ pb_u32 pb_smem(const void* p) {
+    return (pb_u32)__cvta_generic_to_shared(p);
+}
+
+static __device__ __forceinline__ void pb_mbar_init(pb_u32 bar, pb_u32 count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(bar), "r"(count) : "memory");
+}
+
+static __device__ __forceinline__ void pb_mbar_expect_tx(pb_u32 bar, pb_u32 bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(bar), "r"(bytes) : "memory");
+}
+
+static __device__ __forceinline__ pb_u32 pb_mbar_try(pb_u32 bar, pb_u32 parity) {
+    pb_u32 ok;
+    asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+                 : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+    return ok;
+}
+
+// Bounded wait: false when the budget ran out or another role aborted.
+static __device__ __forceinline__ bool pb_wait(pb_u32 bar, pb_u32 parity, volatile int* abort_flag,
+                                               int* err, int site) {
+    const long long start = clock64();
+    for (;;) {
+        if (pb_mbar_try(bar, parity)) return true;
+        if (*abort_flag) return false;
+        if (clock64() - start > PB_WAIT_CYCLES) {
+            *abort_flag = 1;
+            if (atomicCAS(err, 0, 0x7c00 + site) == 0) {
+                err[1] = site;
+                err[2] = (int)blockIdx.x;
+            }
+            return false;
+        }
+    }
+}
+
+static __device__ __forceinline__ void pb_tma_load(pb_u32 dst, const pb_tmap* map, pb_u32 bar, int x, int y) {
+    asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+                 :: "r"(dst), "l"((unsigned long long)map), "r"(bar), "r"(x), "r"(y) : "memory");
+}
+
+// tcgen05 shared-memory matrix descriptor: K-major, 128B swizzle, 8-row
+// groups 1024 B apart (SBO), start address in 16-byte units.
+static __device__ __forceinline__ pb_u64 pb_desc(pb_u32 addr) {
+    pb_u64 d = 0;
+    d |= (pb_u64)((addr & 0x3FFFFu) >> 4);
+    d |= (pb_u64)1 << 16;             // leading byte offset (unused for swizzled K-major)
+    d |= (pb_u64)(1024 >> 4) << 32;   // stride byte offset
+    d |= (pb_u64)1 << 46;             // fixed 0b001
+    d |= (pb_u64)2 << 61;             // 128-byte swizzle
+    return d;
+}
+
+// Instruction descriptor: D f32, A/B tf32, both K-major, N>>3, M>>4.
+#define PB_IDESC ((1u << 4) | (2u << 7) | (2u << 10) | ((pb_u32)(PB_BN >> 3) << 17) | ((pb_u32)(PB_BM >> 4) << 24))
+
+static __device__ __forceinline__ void pb_mma(pb_u32 tmem, pb_u64 a, pb_u64 b, pb_u32 accumulate) {
+    asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}\n"
+                 :: "r"(tmem), "l"(a), "l"(b), "r"(PB_IDESC), "r"(accumulate) : "memory");
+}
+
+static __device__ __forceinline__ void pb_commit(pb_u32 bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" :: "r"(bar) : "memory");
+}
+
+static __device__ __forceinline__ float pb_tf32_rn(float x) {
+    pb_u32 r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return __uint_as_float(r);
+}
+
+#define PB_TMEM_LD32(taddr, v)                                                                   \
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15," \
+                 "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"       \
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), \
+                   "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), \
+                   "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), \
+                   "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), \
+                   "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])                              \
+                 : "r"(taddr))
+)PB";
+        }
+
+        std::string hex8(const std::string& s) {
+            uint64_t h = 0xcbf29ce484222325ULL;
+            for (unsigned char c : s) {
+                h ^= c;
+                h *= 0x100000001b3ULL;
+            }
+            char b[20];
+            std::snprintf(b, sizeof b, "%08x", static_cast<unsigned>(h >> 32));
+            return b;
+        }
+
+        bool tensor_cores_disabled() {
+            const char* v = std::getenv("PORCH_B200_GEMM");
+            return v != nullptr && std::string{v} == "simt";
+        }
+
+    } // namespace
+
+    int lowerer::emit_gemm_tc(int id, const box& b, kernel& k, const kernel_arg& A,
+                              const kernel_arg& B, int64_t M, int64_t N, int64_t K) {
+        (void)id;
+        if (tensor_cores_disabled()) return -1;
+        if (M % kBM != 0 || N % kBN != 0 || K % 64 != 0) return -1;
+        if (M * N * K < (int64_t{1} << 27)) return -1;
+        if (M > (int64_t{1} << 30) || N > (int64_t{1} << 30) || K > (int64_t{1} << 30)) return -1;
+        rank_ = 2;
+
+        const int a_hi = new_temp(static_cast<size_t>(M * K) * 4);
+        const int a_lo = new_temp(static_cast<size_t>(M * K) * 4);
+        const int b_hi = new_temp(static_cast<size_t>(N * K) * 4);
+        const int b_lo = new_temp(static_cast<size_t>(N * K) * 4);
+        const int out = new_temp(static_cast<size_t>(M * N) * 4);
+        auto temp_arg = [](int t) {
+            kernel_arg a;
+            a.kind = arg_kind::temp;
+            a.index = t;
+            return a;
+        };
+
+        // ---- 1. split A rows (contiguous, float4) --------------------------
+        {
+            const int64_t n4 = M * K / 4;
+            std::ostringstream src;
+            src << kernel_prelude() << gemm_device_source();
+            src << "extern \"C\" __global__ void __launch_bounds__(256) pb_split_rows(const float* __restrict__ x, "
+                   "float* __restrict__ hi, float* __restrict__ lo) {\n"
+                << "    for (pb_u64 i = (pb_u64)blockIdx.x * 256u + threadIdx.x; i < " << n4
+                << "ull; i += (pb_u64)gridDim.x * 256u) {\n"
+                << "        const float4 v = pb_ld4(x + 4 * i);\n"
+                << "        float4 h, l;\n"
+                << "        h.x = __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u); l.x = pb_tf32_rn(v.x - h.x);\n"
+                << "        h.y = __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u); l.y = pb_tf32_rn(v.y - h.y);\n"
+                << "        h.z = __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u); l.z = pb_tf32_rn(v.z - h.z);\n"
+                << "        h.w = __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u); l.w = pb_tf32_rn(v.w - h.w);\n"
+                << "        pb_st4(hi + 4 * i, h);\n        pb_st4(lo + 4 * i, l);\n    }\n}\n";
+            launch_spec l;
+            l.name = "pb_split_rows";
+            l.source = src.str();
+            l.schedule = "3xTF32 split of A (hi = trunc, lo = rn(x - hi))";
+            l.grid = {static_cast<uint32_t>(std::min<int64_t>((n4 + 255) / 256, 148 * 16)), 1, 1};
+            l.args = {A, temp_arg(a_hi), temp_arg(a_lo)};
+            finish_kernel(l);
+            p_.launches.push_back(std::move(l));
+        }
+        // ---- 2. split + transpose B (64x64 tiles through shared memory) -----
+        {
+            std::ostringstream src;
+            src << kernel_prelude() << gemm_device_source();
+            src << "extern \"C\" __global__ void __launch_bounds__(256) pb_split_transpose(const float* __restrict__ x, "
+                   "float* __restrict__ hi, float* __restrict__ lo) {\n"
+                << "    __shared__ float t[64][65];\n"
+                << "    const pb_u64 k0 = (pb_u64)blockIdx.y * 64u, n0 = (pb_u64)blockIdx.x * 64u;\n"
+                << "    #pragma unroll\n    for (int u = 0; u < 16; ++u) {\n"
+                << "        const pb_u32 r = threadIdx.x / 64u + 4u * u, c = threadIdx.x % 64u;\n"
+                << "        t[r][c] = pb_ld(x + (k0 + r) * " << N << "ull + n0 + c);\n    }\n"
+                << "    __syncthreads();\n"
+                << "    #pragma unroll\n    for (int u = 0; u < 16; ++u) {\n"
+                << "        const pb_u32 r = threadIdx.x / 64u + 4u * u, c = threadIdx.x % 64u;\n"
+                << "        const float v = t[c][r];\n"
+                << "        const float h = __uint_as_float(__float_as_uint(v) & 0xFFFFE000u);\n"
+                << "        const pb_u64 o = (n0 + r) * " << K << "ull + k0 + c;\n"
+                << "        hi[o] = h;\n        lo[o] = pb_tf32_rn(v - h);\n    }\n}\n";
+            launch_spec l;
+            l.name = "pb_split_transpose";
+            l.source = src.str();
+            l.schedule = "3xTF32 split of B with transpose to K-major";
+            l.grid = {static_cast<uint32_t>(N / 64), static_cast<uint32_t>(K / 64), 1};
+            l.args = {B, temp_arg(b_hi), temp_arg(b_lo)};
+            finish_kernel(l);
+            p_.launches.push_back(std::move(l));
+        }
+        // ---- 3. tcgen05 GEMM + epilogue -------------------------------------
+        std::vector<int> order;
+        const std::string efn = emit_expr_function(b, "0", order);
+        const int64_t tiles_m = M / kBM, tiles_n = N / kBN;
+        const int64_t num_kb = K / kBK;
+        const int group_m = 16;
+        std::ostringstream src;
+        src << kernel_prelude() << gemm_device_source() << efn;
+        std::ostringstream body;
+        body << "    extern __shared__ float4 pb_dyn_smem[];\n"
+             << "    __shared__ __align__(8) unsigned long long full_bar[PB_STAGES], empty_bar[PB_STAGES], acc_bar;\n"
+             << "    __shared__ pb_u32 tmem_slot;\n"
+             << "    __shared__ int abort_flag;\n"
+             << "    __shared__ int issued, consumed;\n"
+             << "    const pb_u32 warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;\n"
+             << "    const pb_u32 base = (pb_smem(pb_dyn_smem) + 1023u) & ~1023u;\n"
+             // Tile order: groups of " << group_m << " M-tiles sweep N (L2 reuse of A and B).
+             << "    const pb_u32 tiles_m = " << tiles_m << "u, tiles_n = " << tiles_n << "u;\n"
+             << "    const pb_u32 per_group = " << group_m << "u * tiles_n;\n"
+             << "    const pb_u32 g = blockIdx.x / per_group, first_m = g * " << group_m << "u;\n"
+             << "    const pb_u32 gm = (tiles_m - first_m) < " << group_m << "u ? (tiles_m - first_m) : " << group_m << "u;\n"
+             << "    const pb_u32 tm = first_m + (blockIdx.x % per_group) % gm;\n"
+             << "    const pb_u32 tn = (blockIdx.x % per_group) / gm;\n"
+             << "    const int m0 = (int)(tm * PB_BM), n0 = (int)(tn * PB_BN);\n"
+             << "    if (threadIdx.x == 0) {\n"
+             << "        abort_flag = 0;\n"
+             << "        issued = 0;\n"
+             << "        consumed = 0;\n"
+             << "        for (int s = 0; s < PB_STAGES; ++s) { pb_mbar_init(pb_smem(&full_bar[s]), 1); pb_mbar_init(pb_smem(&empty_bar[s]), 1); }\n"
+             << "        pb_mbar_init(pb_smem(&acc_bar), 1);\n"
+             << "        asm volatile(\"fence.mbarrier_init.release.cluster;\" ::: \"memory\");\n"
+             << "    }\n"
+             << "    if (warp == 1) {\n"
+             << "        asm volatile(\"tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;\" :: \"r\"(pb_smem(&tmem_slot)) : \"memory\");\n"
+             << "        asm volatile(\"tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\" ::: \"memory\");\n"
+             << "    }\n"
+             << "    asm volatile(\"tcgen05.fence::before_thread_sync;\" ::: \"memory\");\n"
+             << "    __syncthreads();\n"
+             << "    asm volatile(\"tcgen05.fence::after_thread_sync;\" ::: \"memory\");\n"
+             << "    const pb_u32 tmem = tmem_slot;\n"
+             << "    const int num_kb = " << num_kb << ";\n"
+             << "    if (warp == 0 && lane == 0) {\n"
+             // producer
+             << "        for (int kb = 0; kb < num_kb; ++kb) {\n"
+             << "            const int s = kb % PB_STAGES;\n"
+             << "            const pb_u32 phase = (pb_u32)(kb / PB_STAGES) & 1u;\n"
+             << "            if (!pb_wait(pb_smem(&empty_bar[s]), phase ^ 1u, &abort_flag, err, 1)) break;\n"
+             << "            const pb_u32 st = base + (pb_u32)s * PB_STAGE_BYTES;\n"
+             << "            const pb_u32 fb = pb_smem(&full_bar[s]);\n"
+             << "            pb_mbar_expect_tx(fb, PB_STAGE_BYTES);\n"
+             << "            pb_tma_load(st, &tm_ahi, fb, kb * PB_BK, m0);\n"
+             << "            pb_tma_load(st + PB_TILE_A_BYTES, &tm_alo, fb, kb * PB_BK, m0);\n"
+             << "            pb_tma_load(st + 2 * PB_TILE_A_BYTES, &tm_bhi, fb, kb * PB_BK, n0);\n"
+             << "            pb_tma_load(st + 2 * PB_TILE_A_BYTES + PB_TILE_B_BYTES, &tm_blo, fb, kb * PB_BK, n0);\n"
+             << "            issued = kb + 1;\n"
+             << "        }\n"
+             << "    } else if (warp == 1 && lane == 0) {\n"
+             // MMA issuer
+             << "        for (int kb = 0; kb < num_kb; ++kb) {\n"
+             << "            const int s = kb % PB_STAGES;\n"
+             << "            const pb_u32 phase = (pb_u32)(kb / PB_STAGES) & 1u;\n"
+             << "            if (!pb_wait(pb_smem(&full_bar[s]), phase, &abort_flag, err, 2)) break;\n"
+             << "            consumed = kb + 1;\n"
+             << "            asm volatile(\"tcgen05.fence::after_thread_sync;\" ::: \"memory\");\n"
+             << "            const pb_u32 st = base + (pb_u32)s * PB_STAGE_BYTES;\n"
+             << "            #pragma unroll\n"
+             << "            for (int kk = 0; kk < PB_BK / 8; ++kk) {\n"
+             << "                const pb_u64 ahi = pb_desc(st + kk * 32);\n"
+             << "                const pb_u64 alo = pb_desc(st + PB_TILE_A_BYTES + kk * 32);\n"
+             << "                const pb_u64 bhi = pb_desc(st + 2 * PB_TILE_A_BYTES + kk * 32);\n"
+             << "                const pb_u64 blo = pb_desc(st + 2 * PB_TILE_A_BYTES + PB_TILE_B_BYTES + kk * 32);\n"
+             << "                pb_mma(tmem, ahi, bhi, (kb | kk) != 0);\n"
+             << "                pb_mma(tmem, ahi, blo, 1u);\n"
+             << "                pb_mma(tmem, alo, bhi, 1u);\n"
+             << "            }\n"
+             << "            pb_commit(pb_smem(&empty_bar[s]));\n"
+             << "        }\n"
+             // Whether or not the loop finished, tell the epilogue once every
+             // MMA issued so far has completed.
+             << "        pb_commit(pb_smem(&acc_bar));\n"
+             << "    }\n"
+             << "    __syncwarp();\n"
+             // epilogue: all four warps
+             << "    const bool acc_ok = pb_wait(pb_smem(&acc_bar), 0u, &abort_flag, err, 3) && !abort_flag;\n"
+             << "    asm volatile(\"tcgen05.fence::after_thread_sync;\" ::: \"memory\");\n"
+             << "    if (acc_ok) {\n"
+             << "        const int r = m0 + (int)(warp * 32u + lane);\n"
+             << "        for (int c = 0; c < PB_BN / 32; ++c) {\n"
+             << "            pb_u32 v[32];\n"
+             << "            PB_TMEM_LD32(tmem + ((warp * 32u) << 16) + (pb_u32)(c * 32), v);\n"
+             << "            asm volatile(\"tcgen05.wait::ld.sync.aligned;\" ::: \"memory\");\n"
+             << "            const int cbase = n0 + c * 32;\n"
+             << "            float* orow = out + (pb_u64)r * " << N << "ull + cbase;\n"
+             << "            #pragma unroll\n"
+             << "            for (int j = 0; j < 32; j += 4) {\n"
+             << "                float y[4];\n"
+             << "                #pragma unroll\n"
+             << "                for (int e = 0; e < 4; ++e) {\n"
+             << "                    const pb_u64 rr = (pb_u64)r, cc = (pb_u64)(cbase + j + e);\n"
+             << "                    (void)rr; (void)cc;\n";
+        std::vector<std::string> cvar = {"rr", "cc"};
+        for (size_t li = 0; li < order.size(); ++li) {
+            const vnode& v = b.nodes[static_cast<size_t>(order[li])];
+            body << "                    const float x" << li << " = pb_ld(in" << v.buffer << " + "
+                 << address(v.map, cvar, true, -1) << ");\n";
+        }
+        body << "                    y[e] = pb_e0(__uint_as_float(v[j + e])";
+        for (size_t li = 0; li < order.size(); ++li) body << ", x" << li;
+        body << ");\n"
+             << "                }\n"
+             << "                pb_st4(orow + j, make_float4(y[0], y[1], y[2], y[3]));\n"
+             << "            }\n"
+             << "        }\n"
+             << "    }\n"
+             // Teardown after an abort: wait (bounded, ignoring the abort
+             // flag) for the MMAs issued so far and for every TMA copy issued
+             // but not consumed, so nothing writes freed TMEM or shared memory.
+             << "    __syncthreads();\n"
+             << "    if (abort_flag && threadIdx.x == 0) {\n"
+             << "        int dummy = 0;\n"
+             << "        volatile int never = 0;\n"
+             << "        (void)pb_wait(pb_smem(&acc_bar), 0u, &never, &dummy, 4);\n"
+             << "        for (int kb = consumed; kb < issued; ++kb) {\n"
+             << "            (void)pb_wait(pb_smem(&full_bar[kb % PB_STAGES]), (pb_u32)(kb / PB_STAGES) & 1u, &never, &dummy, 5);\n"
+             << "        }\n"
+             << "    }\n"
+             << "    asm volatile(\"tcgen05.fence::before_thread_sync;\" ::: \"memory\");\n"
+             << "    __syncthreads();\n"
+             << "    if (warp == 1) {\n"
+             << "        asm volatile(\"tcgen05.fence::after_thread_sync;\" ::: \"memory\");\n"
+             << "        asm volatile(\"tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;\" :: \"r\"(tmem) : \"memory\");\n"
+             << "    }\n";
+        launch_spec l;
+        l.name = "pb_gemm_tc_" + hex8(src.str() + body.str());
+        src << "extern \"C\" __global__ void __launch_bounds__(128, 1) " << l.name
+            << "(const __grid_constant__ pb_tmap tm_ahi, const __grid_constant__ pb_tmap tm_alo, "
+               "const __grid_constant__ pb_tmap tm_bhi, const __grid_constant__ pb_tmap tm_blo, ";
+        for (size_t i = 0; i < k.leaves.size(); ++i) src << "const float* __restrict__ in" << i << ", ";
+        src << "float* __restrict__ out, int* __restrict__ err) {\n" << body.str() << "}\n";
+        l.source = src.str();
+        l.schedule = "gemm tcgen05 3xTF32 128x256x32, 2-stage TMA ring (no multicast), TMEM accumulator, "
+                     "fused epilogue, grouped tile order";
+        l.grid = {static_cast<uint32_t>(tiles_m * tiles_n), 1, 1};
+        l.block = {128, 1, 1};
+        l.smem = 2 * (2 * kBM * kBK * 4 + 2 * kBN * kBK * 4) + 1024;
+        auto tmap_arg = [&](int temp, int64_t rows, int box_rows) {
+            kernel_arg a;
+            a.kind = arg_kind::tmap;
+            a.index = temp;
+            a.value = static_cast<uint64_t>(rows);
+            a.cols = K;
+            a.box_rows = box_rows;
+            a.box_cols = kBK;
+            return a;
+        };
+        l.args = {tmap_arg(a_hi, M, kBM), tmap_arg(a_lo, M, kBM), tmap_arg(b_hi, N, kBN),
+                  tmap_arg(b_lo, N, kBN)};
+        for (const kernel_arg& a : k.leaves) l.args.push_back(a);
+        l.args.push_back(temp_arg(out));
+        kernel_arg e;
+        e.kind = arg_kind::error_word;
+        l.args.push_back(e);
+        finish_kernel(l);
+        p_.launches.push_back(std::move(l));
+        return out;
     }
 
 } // namespace porch::detail

@@ -348,6 +348,11 @@ namespace porch::detail {
         uint64_t error_word = 0;
         uint64_t values[64];
         void* params[64];
+        struct alignas(64) tensor_map_storage {
+            unsigned char bytes[128];
+        };
+        tensor_map_storage maps[8];
+        int nmaps = 0;
         for (launch_spec& l : p->launches) {
             pbrt_function fn = nullptr;
             if (device < static_cast<int>(l.functions.size())) fn = l.functions[device];
@@ -379,6 +384,23 @@ namespace porch::detail {
                     case arg_kind::u64:
                         values[i] = a.value;
                         break;
+                    case arg_kind::tmap: {
+                        if (nmaps >= 8) throw std::runtime_error("too many tensor maps");
+                        const uint64_t base =
+                            cuda_jit::buffer_access::state(temps[static_cast<size_t>(a.index)])->ptr;
+                        const uint64_t dims[2] = {static_cast<uint64_t>(a.cols), a.value};
+                        const uint64_t strides[1] = {static_cast<uint64_t>(a.cols) * 4u};
+                        const uint32_t box[2] = {static_cast<uint32_t>(a.box_cols),
+                                                 static_cast<uint32_t>(a.box_rows)};
+                        const uint32_t estride[2] = {1, 1};
+                        // fp32, no interleave, 128-byte swizzle, 256-byte L2
+                        // promotion, zero fill.
+                        check(pbrt_tensor_map_encode_tiled(maps[nmaps].bytes, 7, 2, base, dims,
+                                                           strides, box, estride, 0, 3, 3, 0));
+                        params[i] = maps[nmaps].bytes;
+                        ++nmaps;
+                        continue;
+                    }
                 }
                 params[i] = &values[i];
             }

@@ -49,12 +49,17 @@ namespace porch::detail {
         temp,       // pointer to a plan temporary
         error_word, // pointer to the device's error block
         u64,        // immediate
+        tmap,       // TMA tensor map (128 bytes) over a temp: `value` rows x
+                    // `cols` fp32, box `box_rows` x `box_cols`, 128B swizzle
     };
 
     struct kernel_arg {
         arg_kind kind = arg_kind::u64;
         int index = 0;
         uint64_t value = 0;
+        int64_t cols = 0;
+        int box_rows = 0;
+        int box_cols = 0;
     };
 
     struct launch_spec {

@@ -252,6 +252,7 @@ struct environment {
     bool cuda_ok = false;
     bool nvrtc_ok = false;
     bool initialized = false;
+    std::atomic<bool> ready{false}; // initialised successfully
     int init_status = PBRT_OK;
     std::string init_error;
     int device_count = 0;
@@ -303,6 +304,7 @@ environment& env_raw() {
 int ensure_init(environment*& out) {
     environment& env = env_raw();
     out = &env;
+    if (env.ready.load(std::memory_order_acquire)) return PBRT_OK;
     std::scoped_lock lock{env.device_mutex};
     if (env.initialized) {
         if (env.init_status != PBRT_OK) tl_error = env.init_error;
@@ -330,6 +332,7 @@ int ensure_init(environment*& out) {
     env.device_count = count;
     env.devices.resize(static_cast<size_t>(count));
     env.init_status = PBRT_OK;
+    env.ready.store(true, std::memory_order_release);
     return PBRT_OK;
 }
 
@@ -1111,13 +1114,14 @@ int pbrt_error_word(int device, uint64_t* pointer) {
     int s = use_device(device, env);
     if (s != PBRT_OK) return s;
     device_state& d = env->devices[static_cast<size_t>(device)];
-    std::scoped_lock lock{env->device_mutex};
+    // A dedicated mutex: the helpers called below take device_mutex.
+    static std::mutex* error_mutex = new std::mutex();
+    std::scoped_lock lock{*error_mutex};
     if (d.error_block == 0) {
-        CUstream st = nullptr;
         pbrt_stream ps = nullptr;
         s = pbrt_stream_current(device, &ps);
         if (s != PBRT_OK) return s;
-        st = reinterpret_cast<CUstream>(ps);
+        CUstream st = reinterpret_cast<CUstream>(ps);
         CUdeviceptr p = 0;
         s = check(*env, env->cu.cuMemAllocAsync(&p, 64, st), "cuMemAllocAsync");
         if (s != PBRT_OK) return s;

@@ -165,3 +165,38 @@ def test_matmul_epilogue_against_fp64(gpu, m, k, n):
     got = api.materialize(api.relu(api.matmul(A, B) + api.broadcast_to(Bi, [m, n]))).cpu()
     ref = np.maximum(a.astype(np.float64) @ b.astype(np.float64) + bias, 0.0)
     assert matmul_error(got, ref, k) <= 1e-5
+
+
+TC_SHAPES = [(512, 512, 512), (256, 1024, 640), (1024, 768, 512), (384, 512, 1024)]
+
+
+@pytest.mark.parametrize("m,k,n", TC_SHAPES)
+def test_tcgen05_3xtf32_matmul(gpu, m, k, n):
+    """Shapes eligible for the tcgen05 path (M%128, N%256, K%64): the plan
+    must use it, and the result must hold fp32 accuracy: within the
+    normalised 1e-5 bound, and within 4x the error of an fp32 FMA chain
+    (a plain one-pass TF32 product is ~1000x worse and fails this)."""
+    api = gpu
+    rng = np.random.default_rng(m + 3 * k + 7 * n)
+    a = rng.uniform(-1, 1, (m, k)).astype(np.float32)
+    b = rng.uniform(-1, 1, (k, n)).astype(np.float32)
+    bias = rng.uniform(-0.1, 0.1, n).astype(np.float32)
+    A, B, Bi = api.tensor([m, k], a), api.tensor([k, n], b), api.tensor([n], bias)
+    expr = api.relu(api.matmul(A, B) + api.broadcast_to(Bi, [m, n]))
+    assert "tcgen05" in api.describe(expr)
+    got = api.materialize(expr).cpu()
+    ref = np.maximum(a.astype(np.float64) @ b.astype(np.float64) + bias, 0.0)
+    err = matmul_error(got, ref, k)
+    assert err <= 1e-5, err
+    fp32 = np.maximum((a @ b) + bias, 0.0)  # numpy fp32 (blocked) for scale
+    assert err <= 4 * max(matmul_error(fp32, ref, k), 2 ** -24), (err, matmul_error(fp32, ref, k))
+
+
+def test_matmul_c4_full_size_sampled_rows(gpu):
+    api = gpu
+    a, b, bias = _config_inputs(api, "c4_matmul", [[8192, 8192], [8192, 8192], [8192]])
+    A, B, Bi = api.tensor([8192, 8192], a), api.tensor([8192, 8192], b), api.tensor([8192], bias)
+    got = api.materialize(api.relu(api.matmul(A, B) + api.broadcast_to(Bi, [8192, 8192]))).cpu()
+    rows = np.linspace(0, 8191, 64).astype(int)
+    ref = np.maximum(a[rows].astype(np.float64) @ b.astype(np.float64) + bias, 0.0)
+    assert matmul_error(got[rows], ref, 8192) <= 1e-5
