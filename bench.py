@@ -423,7 +423,36 @@ def run_reference(args, rank, world, dist):
     print(json.dumps(line), flush=True)
 
 
+def measure_tf32_peak() -> None:
+    """cuBLAS TF32 GEMM throughput (torch.matmul, fp32 inputs with TF32
+    allowed), 8192^3, best of 10 after warm-up: the tensor-pipe ceiling for
+    one TF32 product. A 3xTF32 kernel's fp32-equivalent ceiling is a third."""
+    import torch
+
+    torch.backends.cuda.matmul.allow_tf32 = True
+    n = 8192
+    a = torch.randn(n, n, device="cuda")
+    b = torch.randn(n, n, device="cuda")
+    for _ in range(3):
+        a @ b
+    torch.cuda.synchronize()
+    best = 1e9
+    for _ in range(10):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        a @ b
+        e.record()
+        e.synchronize()
+        best = min(best, s.elapsed_time(e))
+    tf = 2 * n ** 3 / (best * 1e-3) / 1e12
+    print(json.dumps({"tf32_tflops": round(tf, 1), "ms": round(best, 4),
+                      "how": "torch.matmul fp32 8192^3 allow_tf32, best of 10"}))
+
+
 def main():
+    if "--measure-tf32-peak" in sys.argv:
+        measure_tf32_peak()
+        return
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)

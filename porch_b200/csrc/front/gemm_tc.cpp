@@ -3,10 +3,10 @@
 // C[M,N] = epilogue(A[M,K] @ B[K,N], leaves...) in fp32 accuracy from
 // TF32 tensor-core products (Ootomo & Yokota, "Recovering single precision
 // accuracy from Tensor Cores while surpassing the FP32 theoretical peak
-// performance", 2022): x = hi + lo with hi = x truncated to TF32 (exact
-// split, so x - hi is exact in fp32) and lo = round-to-nearest TF32 of
-// x - hi; C ~= Ahi*Bhi + Ahi*Blo + Alo*Bhi (the lo*lo term is below fp32
-// resolution and dropped).
+// performance", 2022): x = hi + lo with hi = x rounded to nearest TF32
+// (x - hi is then exact in fp32, |x - hi| <= 2^-11 |x|) and lo = x - hi
+// rounded to nearest TF32; C ~= Ahi*Bhi + Ahi*Blo + Alo*Bhi (the lo*lo term,
+// ~2^-22 relative, is dropped).
 //
 // Launches:
 //  1. pb_split_rows:      A [M,K]  -> Ahi, Alo [M,K]      (K-major as is)
@@ -122,6 +122,13 @@ static __device__ __forceinline__ float pb_tf32_rn(float x) {
     return __uint_as_float(r);
 }
 
+// hi = x rounded to TF32 (truncated instead where rounding would overflow);
+// x - hi is then exact in fp32 and |x - hi| <= 2^-11 |x|.
+static __device__ __forceinline__ float pb_tf32_hi(float x) {
+    const float r = pb_tf32_rn(x);
+    return isinf(r) && !isinf(x) ? __uint_as_float(__float_as_uint(x) & 0xFFFFE000u) : r;
+}
+
 #define PB_TMEM_LD32(taddr, v)                                                                   \
     asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15," \
                  "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"       \
@@ -184,15 +191,15 @@ static __device__ __forceinline__ float pb_tf32_rn(float x) {
                 << "ull; i += (pb_u64)gridDim.x * 256u) {\n"
                 << "        const float4 v = pb_ld4(x + 4 * i);\n"
                 << "        float4 h, l;\n"
-                << "        h.x = __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u); l.x = pb_tf32_rn(v.x - h.x);\n"
-                << "        h.y = __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u); l.y = pb_tf32_rn(v.y - h.y);\n"
-                << "        h.z = __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u); l.z = pb_tf32_rn(v.z - h.z);\n"
-                << "        h.w = __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u); l.w = pb_tf32_rn(v.w - h.w);\n"
+                << "        h.x = pb_tf32_hi(v.x); l.x = pb_tf32_rn(v.x - h.x);\n"
+                << "        h.y = pb_tf32_hi(v.y); l.y = pb_tf32_rn(v.y - h.y);\n"
+                << "        h.z = pb_tf32_hi(v.z); l.z = pb_tf32_rn(v.z - h.z);\n"
+                << "        h.w = pb_tf32_hi(v.w); l.w = pb_tf32_rn(v.w - h.w);\n"
                 << "        pb_st4(hi + 4 * i, h);\n        pb_st4(lo + 4 * i, l);\n    }\n}\n";
             launch_spec l;
             l.name = "pb_split_rows";
             l.source = src.str();
-            l.schedule = "3xTF32 split of A (hi = trunc, lo = rn(x - hi))";
+            l.schedule = "3xTF32 split of A (hi = rn(x), lo = rn(x - hi))";
             l.grid = {static_cast<uint32_t>(std::min<int64_t>((n4 + 255) / 256, 148 * 16)), 1, 1};
             l.args = {A, temp_arg(a_hi), temp_arg(a_lo)};
             finish_kernel(l);
@@ -213,7 +220,7 @@ static __device__ __forceinline__ float pb_tf32_rn(float x) {
                 << "    #pragma unroll\n    for (int u = 0; u < 16; ++u) {\n"
                 << "        const pb_u32 r = threadIdx.x / 64u + 4u * u, c = threadIdx.x % 64u;\n"
                 << "        const float v = t[c][r];\n"
-                << "        const float h = __uint_as_float(__float_as_uint(v) & 0xFFFFE000u);\n"
+                << "        const float h = pb_tf32_hi(v);\n"
                 << "        const pb_u64 o = (n0 + r) * " << K << "ull + k0 + c;\n"
                 << "        hi[o] = h;\n        lo[o] = pb_tf32_rn(v - h);\n    }\n}\n";
             launch_spec l;
