@@ -14,8 +14,11 @@
 //  3. pb_gemm_tc:         one 128x256 output tile per CTA, 128 threads.
 //     warp 0 lane 0 issues TMA loads (128B swizzle, BK = 32 fp32) into a
 //     2-stage ring of {Ahi, Alo, Bhi, Blo} tiles (96 KB per stage); warp 1
-//     allocates 256 TMEM columns and its lane 0 issues tcgen05.mma
-//     (kind::tf32, M=128, N=256, K=8; 3 products x 4 k-steps per stage),
+//     allocates 512 TMEM columns and its lane 0 issues tcgen05.mma
+//     (kind::tf32, M=128, N=256, K=8; 3 products x 4 k-steps per stage):
+//     Ahi*Bhi accumulates in columns 0..255 and the small Ahi*Blo + Alo*Bhi
+//     terms in columns 256..511, so the large accumulator is rounded once per
+//     k-step instead of three times; the epilogue adds the two,
 //     committing each stage back to the producer and the last one to the
 //     epilogue barrier; then all four warps read the accumulator with
 //     tcgen05.ld (warp w owns TMEM lanes 32w..32w+31 = tile rows), apply the
@@ -265,7 +268,7 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
              << "        asm volatile(\"fence.mbarrier_init.release.cluster;\" ::: \"memory\");\n"
              << "    }\n"
              << "    if (warp == 1) {\n"
-             << "        asm volatile(\"tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;\" :: \"r\"(pb_smem(&tmem_slot)) : \"memory\");\n"
+             << "        asm volatile(\"tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;\" :: \"r\"(pb_smem(&tmem_slot)) : \"memory\");\n"
              << "        asm volatile(\"tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\" ::: \"memory\");\n"
              << "    }\n"
              << "    asm volatile(\"tcgen05.fence::before_thread_sync;\" ::: \"memory\");\n"
@@ -304,8 +307,8 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
              << "                const pb_u64 bhi = pb_desc(st + 2 * PB_TILE_A_BYTES + kk * 32);\n"
              << "                const pb_u64 blo = pb_desc(st + 2 * PB_TILE_A_BYTES + PB_TILE_B_BYTES + kk * 32);\n"
              << "                pb_mma(tmem, ahi, bhi, (kb | kk) != 0);\n"
-             << "                pb_mma(tmem, ahi, blo, 1u);\n"
-             << "                pb_mma(tmem, alo, bhi, 1u);\n"
+             << "                pb_mma(tmem + PB_BN, ahi, blo, (kb | kk) != 0);\n"
+             << "                pb_mma(tmem + PB_BN, alo, bhi, 1u);\n"
              << "            }\n"
              << "            pb_commit(pb_smem(&empty_bar[s]));\n"
              << "        }\n"
@@ -320,8 +323,9 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
              << "    if (acc_ok) {\n"
              << "        const int r = m0 + (int)(warp * 32u + lane);\n"
              << "        for (int c = 0; c < PB_BN / 32; ++c) {\n"
-             << "            pb_u32 v[32];\n"
+             << "            pb_u32 v[32], w[32];\n"
              << "            PB_TMEM_LD32(tmem + ((warp * 32u) << 16) + (pb_u32)(c * 32), v);\n"
+             << "            PB_TMEM_LD32(tmem + ((warp * 32u) << 16) + (pb_u32)(PB_BN + c * 32), w);\n"
              << "            asm volatile(\"tcgen05.wait::ld.sync.aligned;\" ::: \"memory\");\n"
              << "            const int cbase = n0 + c * 32;\n"
              << "            float* orow = out + (pb_u64)r * " << N << "ull + cbase;\n"
@@ -338,7 +342,7 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
             body << "                    const float x" << li << " = pb_ld(in" << v.buffer << " + "
                  << address(v.map, cvar, true, -1) << ");\n";
         }
-        body << "                    y[e] = pb_e0(__uint_as_float(v[j + e])";
+        body << "                    y[e] = pb_e0(__uint_as_float(v[j + e]) + __uint_as_float(w[j + e])";
         for (size_t li = 0; li < order.size(); ++li) body << ", x" << li;
         body << ");\n"
              << "                }\n"
@@ -362,7 +366,7 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
              << "    __syncthreads();\n"
              << "    if (warp == 1) {\n"
              << "        asm volatile(\"tcgen05.fence::after_thread_sync;\" ::: \"memory\");\n"
-             << "        asm volatile(\"tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;\" :: \"r\"(tmem) : \"memory\");\n"
+             << "        asm volatile(\"tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;\" :: \"r\"(tmem) : \"memory\");\n"
              << "    }\n";
         launch_spec l;
         l.name = "pb_gemm_tc_" + hex8(src.str() + body.str());
