@@ -29,7 +29,10 @@ ROOT = ORACLE.parent
 BUILD = ORACLE / "_build"
 REF_OUT = ORACLE / "_ref"
 REFERENCE = Path(os.environ.get("PORCH_REFERENCE", "/root/reference"))
-CXX = os.environ.get("CXX", "g++")
+# The system g++ links the C++ runtime dynamically; a toolchain wrapper that
+# embeds a private static copy would give this library its own exported
+# libstdc++ and clash with other C++ code in the process.
+CXX = os.environ.get("PORCH_B200_CXX", "/usr/bin/g++" if os.path.exists("/usr/bin/g++") else "g++")
 SYNTH = ROOT / "porch_b200" / "csrc" / "synth.cpp"
 PB_LIB_DIR = ROOT / "porch_b200" / "lib"
 

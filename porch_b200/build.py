@@ -33,7 +33,10 @@ OBJ_DIR = ROOT / "_build" / "obj"
 LIBRARY = LIB_DIR / "libporch_b200.so"
 
 CUDA_HOME = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
-CXX = os.environ.get("CXX", "g++")
+# The system g++ links the C++ runtime dynamically; a toolchain wrapper that
+# embeds a private static copy would give this library its own exported
+# libstdc++ and clash with other C++ code in the process.
+CXX = os.environ.get("PORCH_B200_CXX", "/usr/bin/g++" if os.path.exists("/usr/bin/g++") else "g++")
 CXXFLAGS = [
     "-std=c++20",
     "-O2",
