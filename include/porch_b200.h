@@ -177,6 +177,23 @@ int pb_host_profile_read(char* text, size_t capacity);
 int pb_fill_synthetic(float* values, size_t count, uint64_t seed, int dist,
                       double a, double b);
 
+/* ---- matmul without allocation ------------------------------------------ */
+/* C = A @ B in fp32 (3xTF32 on tcgen05), on raw device pointers, allocating
+ * nothing. No counterpart in the reference: it is for callers that must not
+ * let a library allocate device memory (a custom arena or allocator hook
+ * owns the device, or an allocation would synchronise or fail where they
+ * call). A, B, C are row-major device arrays on the current device:
+ * A [M,K], B [K,N], C [M,N]; M % 128 == 0, N % 256 == 0, K % 64 == 0.
+ * The split operands live in a fixed 64 MiB device array that every GPU
+ * loading this library holds until exit; calls needing more than that
+ * (2 * (M*K + N*K) floats) are rejected with PB_ERR_INVALID_ARGUMENT.
+ * All calls share the array, so calls that overlap on the GPU race. The first
+ * call on each device sets that device up (symbol address, kernel limits);
+ * make it outside any stream capture. The call enqueues on `stream`
+ * (a cudaStream_t, NULL for the default stream) and waits for the result. */
+int pb_matmul_3xtf32_noalloc(const float* a, const float* b, float* c,
+                             int64_t m, int64_t n, int64_t k, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

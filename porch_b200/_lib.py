@@ -86,6 +86,8 @@ def _declare(L: ctypes.CDLL) -> None:
         "pb_host_profile_enable": (c_int, [c_int]),
         "pb_host_profile_read": (c_int, [c_char_p, c_size_t]),
         "pb_fill_synthetic": (c_int, [c_void_p, c_size_t, c_uint64, c_int, c_double, c_double]),
+        "pb_matmul_3xtf32_noalloc": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64,
+                                             c_void_p]),
         "pbrt_available": (c_int, []),
         "pbrt_device_count": (c_int, [P(c_int)]),
         "pbrt_last_error": (c_char_p, []),

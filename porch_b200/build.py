@@ -52,8 +52,13 @@ CXXFLAGS = [
 ]
 
 
+NVCC = os.environ.get("NVCC", str(CUDA_HOME / "bin" / "nvcc"))
+NVCCFLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo", "-O3", "-std=c++17",
+             "--fmad=false", "-Xcompiler", "-fPIC", f"-I{ROOT / 'include'}"]
+
+
 def sources() -> list[Path]:
-    return sorted(p for p in CSRC.rglob("*.cpp"))
+    return sorted(p for p in CSRC.rglob("*.cpp")) + sorted(p for p in CSRC.rglob("*.cu"))
 
 
 def headers() -> list[Path]:
@@ -65,7 +70,10 @@ def _compile(src: Path) -> Path:
     rel = src.relative_to(CSRC)
     obj = OBJ_DIR / rel.with_suffix(".o")
     obj.parent.mkdir(parents=True, exist_ok=True)
-    cmd = [CXX, *CXXFLAGS, "-c", str(src), "-o", str(obj)]
+    if src.suffix == ".cu":
+        cmd = [NVCC, *NVCCFLAGS, "-c", str(src), "-o", str(obj)]
+    else:
+        cmd = [CXX, *CXXFLAGS, "-c", str(src), "-o", str(obj)]
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
         raise RuntimeError(f"compile failed: {' '.join(cmd)}\n{res.stderr}")
@@ -81,8 +89,11 @@ def build(force: bool = False) -> Path:
     with concurrent.futures.ThreadPoolExecutor(max_workers=os.cpu_count() or 4) as ex:
         objs = list(ex.map(_compile, srcs))
     tmp = LIBRARY.with_suffix(".so.tmp")
-    cmd = [CXX, "-shared", "-o", str(tmp), *map(str, objs), "-ldl", "-lpthread",
-           "-Wl,--no-undefined"]
+    # The CUDA runtime is linked statically for the one nvcc-compiled entry
+    # point (pb_matmul_3xtf32_noalloc); everything else reaches the driver
+    # through dlopen.
+    cmd = [CXX, "-shared", "-o", str(tmp), *map(str, objs), f"-L{CUDA_HOME / 'lib64'}",
+           "-lcudart_static", "-lrt", "-ldl", "-lpthread", "-Wl,--no-undefined"]
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
         raise RuntimeError(f"link failed: {' '.join(cmd)}\n{res.stderr}")

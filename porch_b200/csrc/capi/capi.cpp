@@ -60,6 +60,12 @@ namespace {
 
 } // namespace
 
+namespace porch::detail {
+    // Lets other translation units of the C-ABI (the no-allocation matmul)
+    // report through pb_last_error().
+    void set_last_error(const std::string& message) { tl_error = message; }
+} // namespace porch::detail
+
 extern "C" {
 
 const char* pb_last_error(void) { return tl_error.c_str(); }
