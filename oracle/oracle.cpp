@@ -685,9 +685,11 @@ int oracle_shape(const char* program, const float* const* inputs, const int64_t*
         for (size_t i = 0; i < n_inputs; ++i) {
             auto a = std::make_shared<array>();
             a->shape.assign(shapes[i], shapes[i] + ranks[i]);
+            // Values are needed when the program materialises an intermediate.
+            if (inputs != nullptr && inputs[i] != nullptr)
+                a->values.assign(inputs[i], inputs[i] + numel(a->shape));
             ins.push_back(a);
         }
-        (void)inputs;
         evaluator ev;
         bool mat = false;
         node_ptr root = run_program(program, ins, ev, mat);

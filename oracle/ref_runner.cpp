@@ -26,6 +26,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <deque>
 #include <fstream>
 #include <iostream>
 #include <map>
@@ -87,7 +88,10 @@ namespace {
     }
 
     porch::tensor run_program(const std::string& program, const std::vector<porch::tensor>& inputs) {
-        std::vector<value> vals;
+        // A deque keeps element addresses stable: the reference's expression
+        // nodes hold raw `const tensor*` pointers to the tensors stored here
+        // (src/tensor.cpp:50), so they must never move.
+        std::deque<value> vals;
         std::stringstream lines(program);
         std::string line;
         size_t last = 0;
