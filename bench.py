@@ -10,7 +10,10 @@ Multi-GPU (python -m torch.distributed.run ... bench.py --gpus N): the
 default graph does not shard, so every rank realises its own replica on its
 own GPU (weak scaling, no data-path collective); torch.distributed (gloo)
 carries only the barrier and the max-over-ranks timing. Row-shardable
-workloads (c3a/c3b/c5) split their rows across ranks (strong scaling).
+workloads (c3a/c3b/c5) split their rows across ranks in contiguous blocks
+(strong scaling): each rank realises its block on its own GPU; c5's output P
+is then gathered whole on every rank with one ncclAllGather over NVLink per
+step (porch_b200 Communicator.allgather_rows), inside the timed region.
 
 --impl reference runs the reference's own implementation of the path
 (oracle/_ref/ref_runner: AkhilSamavedam/porch compiled from its sources,
@@ -52,6 +55,8 @@ CONFIGS = {
                 ([4096], "uniform", -0.1, 0.1)], 4 * 16384 * 4096 * 16384, "tensor"),
 }
 ROW_SHARDED = {"c3a_softmax", "c3b_relu_logistic", "c5_mlp"}
+# Row-sharded workloads whose output a consumer needs whole (gathered by NCCL).
+GATHERED = {"c5_mlp"}
 KEYS = {
     "c1_elementwise": ["a", "b"], "c2_view": ["x", "bias", "y"], "c3a_softmax": ["x"],
     "c3b_relu_logistic": ["x"], "c4_matmul": ["a", "b", "bias"],
@@ -110,9 +115,23 @@ class ClockSampler:
             self._t.join(timeout=2)
         return False
 
-    def summary(self) -> dict | None:
+    def mark(self) -> int:
+        return len(self.lines)
+
+    def hold_load(self, work, count: int, since: int | None = None, limit_s: float = 5.0) -> None:
+        """Runs `work` (the benchmark's own steps) until `count` samples have
+        arrived after `since`, so that a timed region shorter than the
+        sampling period is bracketed by samples taken under the same load."""
+        if self.proc is None:
+            return
+        base = self.mark() if since is None else since
+        t0 = time.perf_counter()
+        while self.mark() < base + count and time.perf_counter() - t0 < limit_s:
+            work()
+
+    def summary(self, lo: int = 0, hi: int | None = None) -> dict | None:
         rows = []
-        for ln in self.lines:
+        for ln in self.lines[lo:hi]:
             parts = [p.strip() for p in ln.split(",")]
             if len(parts) < 9:
                 continue
@@ -130,7 +149,9 @@ class ClockSampler:
                     reasons.add(n)
         loaded = [r[0] for r in rows]
         return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": max(r[1] for r in rows),
-                "reasons": sorted(reasons), "samples": len(rows)}
+                "reasons": sorted(reasons), "samples": len(rows),
+                "window": "samples from the last one before to the first one after the timed "
+                          "region, the same steps running throughout"}
 
 
 def dist_setup(n_gpus: int):
@@ -142,7 +163,7 @@ def dist_setup(n_gpus: int):
 
         import torch.distributed as dist
 
-        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=180))
         return rank, world, local, dist
     return 0, 1, 0, None
 
@@ -171,8 +192,8 @@ def make_host_inputs(api, workload: str, rank: int, world: int):
         api.fill_synthetic(arr, SEED + i, dist_name, a, b)
         arr = arr.reshape(shape)
         if workload in ROW_SHARDED and world > 1 and i == 0:
-            rows = shape[0] // world
-            arr = np.ascontiguousarray(arr[rank * rows:(rank + 1) * rows])
+            begin, end = api.row_block(shape[0], rank, world)
+            arr = np.ascontiguousarray(arr[begin:end])
         arrays.append(arr)
     return arrays
 
@@ -254,14 +275,27 @@ def run_ours(args, rank, world, local, dist):
         sets.append({k: api.tensor(list(a.shape), a, device=device) for k, a in zip(keys, arrays)})
     graphs = [api.config_graph(workload, t) for t in sets]
 
-    def step(i):
-        return api.materialize(graphs[i % n_sets])
+    # Config 5 gathers its output P whole on every rank (one ncclAllGather
+    # over NVLink per step); configs 3a/3b keep their row blocks where they
+    # are, since no consumer of the benchmark needs them whole.
+    comm = None
+    total_rows = CONFIGS[workload][0][0][0][0]
+    if workload in GATHERED and world > 1:
+        uid = [api.comm_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        comm = api.Communicator(world, uid[0], rank, device, timeout_s=120.0)
 
-    def run_steps(n, outs):
+    def step(i, gather=True):
+        out = api.materialize(graphs[i % n_sets])
+        if comm is not None and gather:
+            out = comm.allgather_rows(out, total_rows)
+        return out
+
+    def run_steps(n, outs, gather=True):
         # At most three results alive at once, in warm-up and timing alike,
         # so the timed steps see the allocator state warm-up left behind.
         for i in range(n):
-            outs.append(step(i))
+            outs.append(step(i, gather))
             if len(outs) > 2:
                 outs.pop(0)
 
@@ -270,22 +304,31 @@ def run_ours(args, rank, world, local, dist):
     run_steps(max(3, args.warmup), outs)
     api.device_synchronize(device)
 
-    api.profile_enable(True)
-    api.profile_read()  # clear
-    api.host_profile_enable(True)
-    api.host_profile_read()  # clear
-    barrier(dist)
-    api.device_synchronize(device)
-    launches0 = api.launch_count()
+    def load():
+        # Runs a rank-dependent number of times: no collective inside.
+        run_steps(4, outs, gather=False)
+        api.device_synchronize(device)
+
     with ClockSampler(device) as clocks:
+        clocks.hold_load(load, 2)
+        api.profile_enable(True)
+        api.profile_read()  # clear
+        api.host_profile_enable(True)
+        api.host_profile_read()  # clear
+        barrier(dist)
+        api.device_synchronize(device)
+        launches0 = api.launch_count()
+        lo = clocks.mark()
         with api.DeviceTimer(device) as timer:
             run_steps(args.steps, outs)
         api.device_synchronize(device)
-    launches = api.launch_count() - launches0
-    prof = api.profile_read()
-    api.profile_enable(False)
-    host = api.host_profile_read()
-    api.host_profile_enable(False)
+        launches = api.launch_count() - launches0
+        prof = api.profile_read()
+        api.profile_enable(False)
+        host = api.host_profile_read()
+        api.host_profile_enable(False)
+        clocks.hold_load(load, 1, since=clocks.mark())
+        clock_summary = clocks.summary(max(0, lo - 1), clocks.mark())
     barrier(dist)
     ms_rank = timer.ms / args.steps
     ms = max_over_ranks(dist, ms_rank)
@@ -318,7 +361,7 @@ def run_ours(args, rank, world, local, dist):
     pinned = [api.PinnedBuffer(a.size) for a in arrays]
     for pb, a in zip(pinned, arrays):
         pb.array[:] = a.reshape(-1)
-    out_count = int(np.prod(api.materialize(graphs[0]).shape()))
+    out_count = int(np.prod(step(0).shape()))
     out_buf = api.PinnedBuffer(out_count)
     h2d = sum(a.size * 4 for a in arrays)
     d2h = out_count * 4
@@ -327,6 +370,8 @@ def run_ours(args, rank, world, local, dist):
         ts = {k: api.tensor_from_pointer(list(a.shape), pb.address, a.size, device=device)
               for k, a, pb in zip(keys, arrays, pinned)}
         t = api.materialize(api.config_graph(workload, ts))
+        if comm is not None:
+            t = comm.allgather_rows(t, total_rows)
         t.cpu(out_buf.array)
 
     e2e_steps = max(1, min(args.steps, 10))
@@ -348,6 +393,9 @@ def run_ours(args, rank, world, local, dist):
         except Exception as exc:  # the baseline must not sink the bench line
             cpu = {"error": str(exc)}
 
+    if comm is not None:
+        outs.clear()
+        comm.close()
     if rank == 0:
         line = {
             "metric": CONFIG_METRIC[workload], "value": round(value, 3), "unit": unit,
@@ -358,14 +406,16 @@ def run_ours(args, rank, world, local, dist):
             "config": {"workload": workload, "shapes": {k: s for k, (s, *_) in zip(keys, specs)},
                        "parallelism": (f"row-shard x{world}" if workload in ROW_SHARDED and world > 1
                                        else (f"replicas x{world}" if world > 1 else "single GPU")),
-                       "l2": f"inputs rotated over {n_sets} device-resident sets, each larger than L2"},
+                       "l2": f"inputs rotated over {n_sets} device-resident sets, each larger than L2",
+                       "collective": (f"ncclAllGather of the output rows ({total_rows} rows whole on every "
+                                      "rank) inside every step" if comm is not None else None)},
             "e2e": {"value": round(e2e_value, 3), "unit": unit, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4),
                     "path": "pb_tensor_create from pinned host -> pb_materialize -> pb_tensor_read"},
             "gpu_launches": launches,
             "roofline": roofline,
             "cpu_baseline": cpu,
-            "clocks": clocks.summary(),
+            "clocks": clock_summary,
             "kernels": {k: {"launches": n, "ms": round(t, 4)} for k, (n, t) in prof.items()},
             "host_us_per_materialize": {k: round(v, 2) for k, v in host.items()},
         }

@@ -177,6 +177,36 @@ int pb_host_profile_read(char* text, size_t capacity);
 int pb_fill_synthetic(float* values, size_t count, uint64_t seed, int dist,
                       double a, double b);
 
+/* ---- row sharding across GPUs (one process per GPU) --------------------- */
+/* No counterpart in the reference, which runs on one device only
+ * (src/backend.cpp, src/cuda_jit.cpp:437-528). A graph whose rows are
+ * independent is realised per row block on each rank's GPU; these calls move
+ * data only where a consumer needs the whole tensor. */
+typedef struct pb_comm_s pb_comm;
+/* 128-byte NCCL unique id, made on one rank and passed to the others. */
+int pb_comm_unique_id(char id[128]);
+/* Joins rank `rank` of `nranks` on `device`; every host-side wait of this
+ * communicator (init included) gives up after timeout_s seconds, aborting
+ * the communicator and returning PB_ERR_RUNTIME. */
+int pb_comm_init(int nranks, const char id[128], int rank, int device, double timeout_s,
+                 pb_comm** out);
+int pb_comm_info(const pb_comm* comm, int* rank, int* nranks, int* device);
+/* Bound (seconds) on this communicator's host-side waits from now on. */
+int pb_comm_set_timeout(pb_comm* comm, double timeout_s);
+/* Aborts outstanding work; later calls on the communicator fail. */
+int pb_comm_abort(pb_comm* comm);
+int pb_comm_release(pb_comm* comm);
+/* Rows [*begin, *end) of a `rows`-row tensor owned by `rank` of `nranks`:
+ * contiguous blocks, the first rows % nranks ranks holding one extra row. */
+int pb_row_block(int64_t rows, int rank, int nranks, int64_t* begin, int64_t* end);
+/* Every rank passes its row block `shard` (realised first if lazy; its row
+ * count must be pb_row_block's for this rank) and receives the whole
+ * [total_rows, ...] tensor, row blocks concatenated in rank order, on its own
+ * device: one ncclAllGather for equal blocks, grouped Send/Recv otherwise.
+ * Returns once the gather has completed on the device. */
+int pb_allgather_rows(pb_comm* comm, const pb_tensor* shard, int64_t total_rows,
+                      pb_tensor** out);
+
 /* ---- matmul without allocation ------------------------------------------ */
 /* C = A @ B in fp32 (3xTF32 on tcgen05), on raw device pointers, allocating
  * nothing. No counterpart in the reference: it is for callers that must not

@@ -165,7 +165,14 @@ int pbrt_nccl_init_all(int count, const int* devices, pbrt_comm* comms);
 int pbrt_nccl_init_rank(int nranks, const char id[128], int rank, int device,
                         double timeout_s, pbrt_comm* comm);
 int pbrt_nccl_group_start(void);
+/* Ends a group. On non-blocking communicators the group's operations may
+ * still be enqueueing when this returns: call pbrt_nccl_settle on every
+ * communicator of the group before ordering other work behind them. */
 int pbrt_nccl_group_end(void);
+/* Waits (bounded by the communicator's timeout, aborting it on expiry or on
+ * an asynchronous error) until the communicator's pending host-side enqueue
+ * has finished. Collectives issued outside a group settle by themselves. */
+int pbrt_nccl_settle(pbrt_comm comm);
 int pbrt_nccl_allgather_f32(pbrt_comm comm, uint64_t send, uint64_t recv,
                             size_t count_per_rank, pbrt_stream stream);
 int pbrt_nccl_send_f32(pbrt_comm comm, uint64_t send, size_t count, int peer,
@@ -177,6 +184,8 @@ int pbrt_nccl_recv_f32(pbrt_comm comm, uint64_t recv, size_t count, int peer,
 int pbrt_nccl_wait(pbrt_comm comm, int device, pbrt_stream stream,
                    double timeout_s);
 int pbrt_nccl_abort(pbrt_comm comm);
+/* Bound (seconds) on the communicator's host-side waits from now on. */
+int pbrt_nccl_set_timeout(pbrt_comm comm, double timeout_s);
 int pbrt_nccl_destroy(pbrt_comm comm);
 
 #ifdef __cplusplus

@@ -88,6 +88,14 @@ def _declare(L: ctypes.CDLL) -> None:
         "pb_fill_synthetic": (c_int, [c_void_p, c_size_t, c_uint64, c_int, c_double, c_double]),
         "pb_matmul_3xtf32_noalloc": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64,
                                              c_void_p]),
+        "pb_comm_unique_id": (c_int, [c_char_p]),
+        "pb_comm_init": (c_int, [c_int, c_char_p, c_int, c_int, c_double, P(c_void_p)]),
+        "pb_comm_info": (c_int, [c_void_p, P(c_int), P(c_int), P(c_int)]),
+        "pb_comm_abort": (c_int, [c_void_p]),
+        "pb_comm_set_timeout": (c_int, [c_void_p, c_double]),
+        "pb_comm_release": (c_int, [c_void_p]),
+        "pb_row_block": (c_int, [c_int64, c_int, c_int, P(c_int64), P(c_int64)]),
+        "pb_allgather_rows": (c_int, [c_void_p, c_void_p, c_int64, P(c_void_p)]),
         "pbrt_available": (c_int, []),
         "pbrt_device_count": (c_int, [P(c_int)]),
         "pbrt_last_error": (c_char_p, []),

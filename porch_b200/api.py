@@ -71,6 +71,20 @@ def is_available() -> bool:
     return lib().pb_is_available() == 1
 
 
+def device_count() -> int:
+    """CUDA devices visible to this process (0 without a driver)."""
+    if not is_available():
+        return 0
+    n = c_int(0)
+    _check_rt(lib().pbrt_device_count(byref(n)))
+    return n.value
+
+
+def _check_rt(status: int) -> None:
+    if status != 0:
+        raise RuntimeError(lib().pbrt_last_error().decode(errors="replace"))
+
+
 def backend_name() -> str:
     return lib().pb_backend_name().decode()
 
@@ -548,6 +562,62 @@ class PinnedBuffer:
     def __del__(self):
         try:
             self.free()
+        except Exception:
+            pass
+
+
+# ----------------------------------------------------------- row sharding --
+def row_block(rows: int, rank: int, nranks: int) -> tuple[int, int]:
+    """Rows [begin, end) of `rows` owned by `rank` of `nranks` (contiguous
+    blocks; the first rows % nranks ranks hold one extra row)."""
+    b, e = c_int64(), c_int64()
+    _check(lib().pb_row_block(int(rows), int(rank), int(nranks), byref(b), byref(e)))
+    return b.value, e.value
+
+
+def comm_unique_id() -> bytes:
+    """A fresh 128-byte NCCL unique id (make on one rank, send to the rest)."""
+    buf = ctypes.create_string_buffer(128)
+    _check(lib().pb_comm_unique_id(buf))
+    return buf.raw
+
+
+class Communicator:
+    """One rank of a one-process-per-GPU communicator (NCCL over NVLink)."""
+
+    def __init__(self, nranks: int, unique_id: bytes, rank: int, device: int, timeout_s: float = 60.0):
+        if len(unique_id) != 128:
+            raise InvalidArgument("unique id must be 128 bytes")
+        self._h = c_void_p()
+        _check(lib().pb_comm_init(int(nranks), unique_id, int(rank), int(device), float(timeout_s),
+                                  byref(self._h)))
+
+    def info(self) -> tuple[int, int, int]:
+        r, n, d = c_int(), c_int(), c_int()
+        _check(lib().pb_comm_info(self._h, byref(r), byref(n), byref(d)))
+        return r.value, n.value, d.value
+
+    def allgather_rows(self, shard, total_rows: int) -> Tensor:
+        """Whole [total_rows, ...] tensor from every rank's row block."""
+        t = shard if isinstance(shard, Tensor) else materialize(shard)
+        out = c_void_p()
+        _check(lib().pb_allgather_rows(self._h, t._h, int(total_rows), byref(out)))
+        return Tensor(out.value)
+
+    def set_timeout(self, timeout_s: float) -> None:
+        _check(lib().pb_comm_set_timeout(self._h, float(timeout_s)))
+
+    def abort(self) -> None:
+        _check(lib().pb_comm_abort(self._h))
+
+    def close(self) -> None:
+        if self._h.value:
+            _check(lib().pb_comm_release(self._h))
+            self._h = c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
         except Exception:
             pass
 

@@ -7,6 +7,7 @@
 
 #include <cmath>
 #include <cstring>
+#include <memory>
 #include <stdexcept>
 #include <string>
 #include <vector>
@@ -17,6 +18,10 @@ struct pb_tensor_s {
 
 struct pb_expr_s {
     porch::tensor_expr value;
+};
+
+struct pb_comm_s {
+    std::unique_ptr<porch::detail::communicator> value;
 };
 
 namespace {
@@ -487,6 +492,72 @@ int pb_host_profile_read(char* text, size_t capacity) {
             std::memcpy(text, s.data(), n);
             text[n] = '\0';
         }
+    });
+}
+
+int pb_comm_unique_id(char id[128]) {
+    return guarded([&] {
+        require(id, "id");
+        porch::detail::check(pbrt_nccl_unique_id(id));
+    });
+}
+
+int pb_comm_init(int nranks, const char id[128], int rank, int device, double timeout_s,
+                 pb_comm** out) {
+    return guarded([&] {
+        require(id, "id");
+        require(out, "out");
+        *out = nullptr;
+        auto c = porch::detail::make_communicator(nranks, id, rank, device, timeout_s);
+        *out = new pb_comm_s{std::move(c)};
+    });
+}
+
+int pb_comm_info(const pb_comm* comm, int* rank, int* nranks, int* device) {
+    return guarded([&] {
+        require(comm, "communicator");
+        if (rank) *rank = comm->value->rank;
+        if (nranks) *nranks = comm->value->nranks;
+        if (device) *device = comm->value->device;
+    });
+}
+
+int pb_comm_set_timeout(pb_comm* comm, double timeout_s) {
+    return guarded([&] {
+        require(comm, "communicator");
+        if (!(timeout_s > 0.0)) throw std::invalid_argument("timeout must be positive");
+        porch::detail::check(pbrt_nccl_set_timeout(comm->value->comm, timeout_s));
+        comm->value->timeout_s = timeout_s;
+    });
+}
+
+int pb_comm_abort(pb_comm* comm) {
+    return guarded([&] {
+        require(comm, "communicator");
+        porch::detail::abort_communicator(*comm->value);
+    });
+}
+
+int pb_comm_release(pb_comm* comm) {
+    return guarded([&] { delete comm; });
+}
+
+int pb_row_block(int64_t rows, int rank, int nranks, int64_t* begin, int64_t* end) {
+    return guarded([&] {
+        const auto [b, e] = porch::detail::row_block(rows, rank, nranks);
+        if (begin) *begin = b;
+        if (end) *end = e;
+    });
+}
+
+int pb_allgather_rows(pb_comm* comm, const pb_tensor* shard, int64_t total_rows,
+                      pb_tensor** out) {
+    return guarded([&] {
+        require(comm, "communicator");
+        require(shard, "shard");
+        require(out, "out");
+        *out = nullptr;
+        *out = wrap(porch::detail::allgather_rows(*comm->value, shard->value, total_rows));
     });
 }
 

@@ -9,6 +9,7 @@
 #include <memory>
 #include <mutex>
 #include <string>
+#include <utility>
 #include <vector>
 
 namespace porch::detail {
@@ -234,6 +235,31 @@ namespace porch::detail {
     void host_count(const char* what); // allocator hit/miss counters
     void host_profile_enable(bool on);
     std::string host_profile_read();
+
+    // ---------------------------------------------------- row sharding --
+    // One rank of a one-process-per-GPU communicator (NCCL over NVLink).
+    struct communicator {
+        pbrt_comm comm = nullptr;
+        int rank = 0;
+        int nranks = 1;
+        int device = 0;
+        double timeout_s = 60.0; // bound on every host-side wait
+        bool aborted = false;
+        communicator() = default;
+        communicator(const communicator&) = delete;
+        communicator& operator=(const communicator&) = delete;
+        ~communicator();
+    };
+    std::unique_ptr<communicator> make_communicator(
+        int nranks, const char id[128], int rank, int device, double timeout_s
+    );
+    void abort_communicator(communicator& c);
+    // Rows [begin, end) of `rows` owned by `rank` of `nranks` (contiguous
+    // blocks, the first rows % nranks ranks one row longer).
+    std::pair<index_t, index_t> row_block(index_t rows, int rank, int nranks);
+    // Every rank passes its realised row block; every rank receives the whole
+    // [total_rows, ...] tensor (row blocks concatenated in rank order).
+    tensor allgather_rows(communicator& c, const tensor& shard, index_t total_rows);
 
     // Human-readable description of the plan chosen for `root` (kernels,
     // schedules and generated sources). Works on placeholder inputs without a

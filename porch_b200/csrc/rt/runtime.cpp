@@ -156,6 +156,7 @@ struct nvrtc_api {
                                                ncclUniqueId, int,            \
                                                ncclConfig_t*))               \
     X(ncclCommDestroy, ncclResult_t (*)(ncclComm_t))                         \
+    X(ncclCommFinalize, ncclResult_t (*)(ncclComm_t))                        \
     X(ncclCommAbort, ncclResult_t (*)(ncclComm_t))                           \
     X(ncclCommGetAsyncError, ncclResult_t (*)(ncclComm_t, ncclResult_t*))    \
     X(ncclGroupStart, ncclResult_t (*)())                                    \
@@ -533,7 +534,45 @@ struct comm_handle {
     ncclComm_t comm = nullptr;
     int device = 0;
     bool aborted = false;
+    double timeout_s = 60.0; // bound on every host-side wait for this communicator
 };
+
+// Group nesting of the calling thread: inside a group NCCL only records the
+// operations, so there is nothing to settle until the outermost group end.
+thread_local int nccl_group_depth = 0;
+
+// A non-blocking communicator may return ncclInProgress while the operation
+// is still being enqueued on the host; nothing recorded on the stream after
+// it is ordered behind it until the state leaves ncclInProgress. Polls that
+// state with the communicator's deadline, aborting it on error or timeout.
+int settle(comm_handle* h, const char* operation) {
+    nccl_env& n = nccl();
+    const auto deadline = std::chrono::steady_clock::now() +
+                          std::chrono::duration<double>(h->timeout_s);
+    for (;;) {
+        ncclResult_t state = ncclSuccess;
+        const ncclResult_t r = n.api.ncclCommGetAsyncError(h->comm, &state);
+        if (r != ncclSuccess) state = r;
+        if (state == ncclSuccess) return PBRT_OK;
+        if (state != ncclInProgress) {
+            (void)n.api.ncclCommAbort(h->comm);
+            h->aborted = true;
+            return nccl_check(state, operation);
+        }
+        if (std::chrono::steady_clock::now() > deadline) {
+            (void)n.api.ncclCommAbort(h->comm);
+            h->aborted = true;
+            return fail(PBRT_ERR_NCCL, std::string{operation} +
+                                           " did not complete its enqueue in time; communicator aborted");
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+}
+
+int after_call(comm_handle* h, ncclResult_t r, const char* operation) {
+    if (r == ncclInProgress) return nccl_group_depth > 0 ? PBRT_OK : settle(h, operation);
+    return nccl_check(r, operation);
+}
 
 }  // namespace
 
@@ -1252,7 +1291,7 @@ int pbrt_nccl_init_all(int count, const int* devices, pbrt_comm* comms) {
     int s = nccl_check(n.api.ncclCommInitAll(raw.data(), count, devices), "ncclCommInitAll");
     if (s != PBRT_OK) return s;
     for (int i = 0; i < count; ++i) {
-        auto* h = new comm_handle{raw[static_cast<size_t>(i)], devices[i], false};
+        auto* h = new comm_handle{raw[static_cast<size_t>(i)], devices[i], false, 60.0};
         comms[i] = reinterpret_cast<pbrt_comm>(h);
     }
     return PBRT_OK;
@@ -1293,22 +1332,33 @@ int pbrt_nccl_init_rank(int nranks, const char id[128], int rank, int device,
         }
         std::this_thread::sleep_for(std::chrono::milliseconds(1));
     }
-    *comm = reinterpret_cast<pbrt_comm>(new comm_handle{raw, device, false});
+    *comm = reinterpret_cast<pbrt_comm>(new comm_handle{raw, device, false, timeout_s});
     return PBRT_OK;
 }
 
 int pbrt_nccl_group_start(void) {
     nccl_env& n = nccl();
     if (!n.ok) return fail(PBRT_ERR_UNAVAILABLE, "libnccl.so.2 not found");
-    return nccl_check(n.api.ncclGroupStart(), "ncclGroupStart");
+    const int s = nccl_check(n.api.ncclGroupStart(), "ncclGroupStart");
+    if (s == PBRT_OK) ++nccl_group_depth;
+    return s;
 }
 
 int pbrt_nccl_group_end(void) {
     nccl_env& n = nccl();
     if (!n.ok) return fail(PBRT_ERR_UNAVAILABLE, "libnccl.so.2 not found");
     ncclResult_t r = n.api.ncclGroupEnd();
-    if (r == ncclInProgress) return PBRT_OK;  // non-blocking communicators
+    if (nccl_group_depth > 0) --nccl_group_depth;
+    if (r == ncclInProgress) return PBRT_OK;  // settled per communicator by pbrt_nccl_settle
     return nccl_check(r, "ncclGroupEnd");
+}
+
+int pbrt_nccl_settle(pbrt_comm comm) {
+    nccl_env& n = nccl();
+    if (!n.ok) return fail(PBRT_ERR_UNAVAILABLE, "libnccl.so.2 not found");
+    auto* h = reinterpret_cast<comm_handle*>(comm);
+    if (h == nullptr || h->aborted) return fail(PBRT_ERR_NCCL, "NCCL communicator is not usable");
+    return settle(h, "NCCL group");
 }
 
 int pbrt_nccl_allgather_f32(pbrt_comm comm, uint64_t send, uint64_t recv,
@@ -1325,8 +1375,7 @@ int pbrt_nccl_allgather_f32(pbrt_comm comm, uint64_t send, uint64_t recv,
                                          reinterpret_cast<void*>(recv), count_per_rank,
                                          ncclFloat32, h->comm,
                                          reinterpret_cast<cudaStream_t>(stream));
-    if (r == ncclInProgress) return PBRT_OK;
-    return nccl_check(r, "ncclAllGather");
+    return after_call(h, r, "ncclAllGather");
 }
 
 int pbrt_nccl_send_f32(pbrt_comm comm, uint64_t send, size_t count, int peer,
@@ -1341,8 +1390,7 @@ int pbrt_nccl_send_f32(pbrt_comm comm, uint64_t send, size_t count, int peer,
     if (s != PBRT_OK) return s;
     ncclResult_t r = n.api.ncclSend(reinterpret_cast<const void*>(send), count, ncclFloat32,
                                     peer, h->comm, reinterpret_cast<cudaStream_t>(stream));
-    if (r == ncclInProgress) return PBRT_OK;
-    return nccl_check(r, "ncclSend");
+    return after_call(h, r, "ncclSend");
 }
 
 int pbrt_nccl_recv_f32(pbrt_comm comm, uint64_t recv, size_t count, int peer,
@@ -1357,8 +1405,7 @@ int pbrt_nccl_recv_f32(pbrt_comm comm, uint64_t recv, size_t count, int peer,
     if (s != PBRT_OK) return s;
     ncclResult_t r = n.api.ncclRecv(reinterpret_cast<void*>(recv), count, ncclFloat32, peer,
                                     h->comm, reinterpret_cast<cudaStream_t>(stream));
-    if (r == ncclInProgress) return PBRT_OK;
-    return nccl_check(r, "ncclRecv");
+    return after_call(h, r, "ncclRecv");
 }
 
 int pbrt_nccl_wait(pbrt_comm comm, int device, pbrt_stream stream, double timeout_s) {
@@ -1410,6 +1457,14 @@ int pbrt_nccl_wait(pbrt_comm comm, int device, pbrt_stream stream, double timeou
     return status;
 }
 
+int pbrt_nccl_set_timeout(pbrt_comm comm, double timeout_s) {
+    auto* h = reinterpret_cast<comm_handle*>(comm);
+    if (h == nullptr) return fail(PBRT_ERR_INVALID, "communicator is null");
+    if (!(timeout_s > 0.0)) return fail(PBRT_ERR_INVALID, "timeout must be positive");
+    h->timeout_s = timeout_s;
+    return PBRT_OK;
+}
+
 int pbrt_nccl_abort(pbrt_comm comm) {
     nccl_env& n = nccl();
     auto* h = reinterpret_cast<comm_handle*>(comm);
@@ -1424,7 +1479,14 @@ int pbrt_nccl_destroy(pbrt_comm comm) {
     auto* h = reinterpret_cast<comm_handle*>(comm);
     if (h == nullptr) return PBRT_OK;
     int s = PBRT_OK;
-    if (!h->aborted && n.ok) s = nccl_check(n.api.ncclCommDestroy(h->comm), "ncclCommDestroy");
+    if (!h->aborted && n.ok) {
+        // Non-blocking communicators finalise first (flushing outstanding
+        // work), bounded by the communicator's deadline, then are destroyed.
+        ncclResult_t r = n.api.ncclCommFinalize(h->comm);
+        s = r == ncclInProgress ? settle(h, "ncclCommFinalize") : nccl_check(r, "ncclCommFinalize");
+        if (!h->aborted)
+            s = s != PBRT_OK ? s : nccl_check(n.api.ncclCommDestroy(h->comm), "ncclCommDestroy");
+    }
     delete h;
     return s;
 }
