@@ -347,14 +347,22 @@ def run_ours(args, rank, world, local, dist):
         per_launch_ms = k_ms / k_launches
         per_launch_work = work_rank / max(1, k_launches // args.steps)
         achieved = per_launch_work / (per_launch_ms * 1e-3) / scale
-        peak = pk["hbm_gbs"] if bound == "hbm" else pk["bf16_tflops"]
+        if bound == "hbm":
+            peak, basis = pk["hbm_gbs"], f"hbm_gbs ({pk['source']}): STREAM-style copy"
+        else:
+            # fp32 work on the 3xTF32 path: TF32 MMAs run at half the bf16
+            # rate and each fp32 product costs three of them (hi*hi, hi*lo,
+            # lo*hi), so the tensor-pipe ceiling in useful fp32 flop/s is
+            # the measured bf16 figure / 6.
+            peak = round(pk["bf16_tflops"] / 6.0, 2)
+            basis = f"bf16_tflops ({pk['source']}) / 6: TF32 = bf16 / 2, three TF32 MMAs per fp32 product"
         traffic = None
         tfile = ROOT / "profiles" / "ncu_traffic.json"
         if tfile.exists():
             traffic = json.loads(tfile.read_text()).get(workload)
         roofline = {"bound": bound, "achieved": round(achieved, 2), "peak": peak,
                     "unit": unit, "frac": round(achieved / peak, 4), "traffic": traffic,
-                    "peak_source": pk["source"], "kernel": fam,
+                    "peak_source": pk["source"], "peak_basis": basis, "kernel": fam,
                     "kernel_ms": round(per_launch_ms, 5)}
 
     # End to end through the C-ABI with host buffers in pinned memory.
@@ -366,14 +374,15 @@ def run_ours(args, rank, world, local, dist):
     h2d = sum(a.size * 4 for a in arrays)
     d2h = out_count * 4
 
-    def e2e_step():
+    def e2e_step(out=out_buf):
         ts = {k: api.tensor_from_pointer(list(a.shape), pb.address, a.size, device=device)
               for k, a, pb in zip(keys, arrays, pinned)}
         t = api.materialize(api.config_graph(workload, ts))
         if comm is not None:
             t = comm.allgather_rows(t, total_rows)
-        t.cpu(out_buf.array)
+        t.cpu(out.array)
 
+    bw = api.copy_bandwidth(device)
     e2e_steps = max(1, min(args.steps, 10))
     for _ in range(2):
         e2e_step()
@@ -385,6 +394,49 @@ def run_ours(args, rank, world, local, dist):
     e2e_ms_rank = (time.perf_counter() - t0) * 1e3 / e2e_steps
     e2e_ms = max_over_ranks(dist, e2e_ms_rank)
     e2e_value = total_work / (e2e_ms * 1e-3) / scale
+
+    # The same steps from two host threads (each has its own stream, so one
+    # step's host->device copies overlap the other's device->host read).
+    # Skipped when a step holds a collective: threads would interleave the
+    # ranks' collectives in different orders.
+    e2e_threads = None
+    if comm is None:
+        n_threads = 2
+        per_thread = max(1, e2e_steps // n_threads)
+        t_bufs = [api.PinnedBuffer(out_count) for _ in range(n_threads)]
+        errors = []
+
+        start = threading.Barrier(n_threads + 1)
+        done = threading.Barrier(n_threads + 1)
+
+        def worker(j):
+            # Streams and allocator caches are per thread: warm this thread's
+            # own before the timed steps.
+            try:
+                for _ in range(2):
+                    e2e_step(t_bufs[j])
+            except Exception as exc:  # reported, not raised, from a thread
+                errors.append(repr(exc))
+            start.wait()
+            try:
+                for _ in range(per_thread):
+                    e2e_step(t_bufs[j])
+            except Exception as exc:
+                errors.append(repr(exc))
+            done.wait()
+
+        threads = [threading.Thread(target=worker, args=(j,)) for j in range(n_threads)]
+        for th in threads:
+            th.start()
+        barrier(dist)
+        start.wait()
+        t0 = time.perf_counter()
+        done.wait()
+        thr_ms = max_over_ranks(dist, (time.perf_counter() - t0) * 1e3 / (per_thread * n_threads))
+        for th in threads:
+            th.join()
+        e2e_threads = {"threads": n_threads, "value": round(total_work / (thr_ms * 1e-3) / scale, 3),
+                       "unit": unit, "ms_per_step": round(thr_ms, 4), "errors": errors or None}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -411,6 +463,11 @@ def run_ours(args, rank, world, local, dist):
                                       "rank) inside every step" if comm is not None else None)},
             "e2e": {"value": round(e2e_value, 3), "unit": unit, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4),
+                    "copy_bound": {"h2d_gbs": round(bw["h2d_gbs"], 2), "d2h_gbs": round(bw["d2h_gbs"], 2),
+                                   "ms": round((h2d / bw["h2d_gbs"] + d2h / bw["d2h_gbs"]) / 1e6, 4),
+                                   "frac": round((h2d / bw["h2d_gbs"] + d2h / bw["d2h_gbs"]) / 1e6 / e2e_ms, 4),
+                                   "how": "pinned 256 MiB H2D and D2H copies timed alone (best of 3)"},
+                    "two_threads": e2e_threads,
                     "path": "pb_tensor_create from pinned host -> pb_materialize -> pb_tensor_read"},
             "gpu_launches": launches,
             "roofline": roofline,

@@ -117,6 +117,10 @@ int pbrt_register_image(const void* image, size_t size, uint64_t* key);
 int pbrt_get_function(int device, uint64_t key, const char* name,
                   pbrt_function* function);
 int pbrt_function_set_max_dynamic_smem(pbrt_function function, int bytes);
+/* CTAs of `function` that fit on one SM of `device` at this block size and
+ * dynamic shared memory (registers, shared memory and thread limits). */
+int pbrt_occupancy(int device, pbrt_function function, int block_threads, size_t dynamic_smem,
+                   int* blocks_per_sm);
 int pbrt_function_attribute(pbrt_function function, int attribute,
                             int* value);
 /* grid/block are 3-vectors; cluster may be NULL (no cluster attribute). */

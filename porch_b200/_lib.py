@@ -101,6 +101,17 @@ def _declare(L: ctypes.CDLL) -> None:
         "pbrt_last_error": (c_char_p, []),
         "pbrt_fault_inject": (c_int, [c_char_p]),
         "pbrt_launch_count": (c_uint64, []),
+        "pbrt_stream_current": (c_int, [c_int, P(c_void_p)]),
+        "pbrt_stream_synchronize": (c_int, [c_int, c_void_p]),
+        "pbrt_mem_alloc_async": (c_int, [c_int, c_size_t, c_void_p, P(c_uint64)]),
+        "pbrt_mem_free_async": (c_int, [c_int, c_uint64, c_void_p]),
+        "pbrt_memcpy_h2d_async": (c_int, [c_int, c_uint64, c_void_p, c_size_t, c_void_p]),
+        "pbrt_memcpy_d2h_async": (c_int, [c_int, c_void_p, c_uint64, c_size_t, c_void_p]),
+        "pbrt_event_create": (c_int, [c_int, c_int, P(c_void_p)]),
+        "pbrt_event_destroy": (c_int, [c_int, c_void_p]),
+        "pbrt_event_record": (c_int, [c_int, c_void_p, c_void_p]),
+        "pbrt_event_synchronize": (c_int, [c_int, c_void_p]),
+        "pbrt_event_elapsed_ms": (c_int, [c_void_p, c_void_p, P(c_float)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)

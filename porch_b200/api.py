@@ -566,6 +566,45 @@ class PinnedBuffer:
             pass
 
 
+def copy_bandwidth(device: int = 0, nbytes: int = 256 << 20, reps: int = 3) -> dict[str, float]:
+    """Page-locked host <-> device copy rates in GB/s (best of `reps`, CUDA
+    events on this thread's stream): the transfer bound of an end-to-end
+    step whose inputs start in host memory and whose result ends there."""
+    L = lib()
+    stream = c_void_p()
+    _check_rt(L.pbrt_stream_current(int(device), byref(stream)))
+    dptr = c_uint64()
+    _check_rt(L.pbrt_mem_alloc_async(int(device), int(nbytes), stream, byref(dptr)))
+    host = PinnedBuffer(int(nbytes) // 4)
+    ev = [c_void_p(), c_void_p()]
+    for e in ev:
+        _check_rt(L.pbrt_event_create(int(device), 1, byref(e)))
+    out = {}
+    try:
+        copies = {
+            "h2d": lambda: L.pbrt_memcpy_h2d_async(int(device), dptr.value, host.address, int(nbytes), stream),
+            "d2h": lambda: L.pbrt_memcpy_d2h_async(int(device), host.address, dptr.value, int(nbytes), stream),
+        }
+        for name, copy in copies.items():
+            best = float("inf")
+            for _ in range(_builtins.max(1, reps)):
+                _check_rt(L.pbrt_event_record(int(device), ev[0], stream))
+                _check_rt(copy())
+                _check_rt(L.pbrt_event_record(int(device), ev[1], stream))
+                _check_rt(L.pbrt_event_synchronize(int(device), ev[1]))
+                ms = c_float()
+                _check_rt(L.pbrt_event_elapsed_ms(ev[0], ev[1], byref(ms)))
+                best = _builtins.min(best, ms.value)
+            out[name + "_gbs"] = nbytes / (best * 1e-3) / 1e9
+    finally:
+        for e in ev:
+            L.pbrt_event_destroy(int(device), e)
+        L.pbrt_mem_free_async(int(device), dptr.value, stream)
+        L.pbrt_stream_synchronize(int(device), stream)
+        host.free()
+    return out
+
+
 # ----------------------------------------------------------- row sharding --
 def row_block(rows: int, rank: int, nranks: int) -> tuple[int, int]:
     """Rows [begin, end) of `rows` owned by `rank` of `nranks` (contiguous

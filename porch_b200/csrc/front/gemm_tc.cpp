@@ -12,10 +12,13 @@
 //  1. pb_split_rows:      A [M,K]  -> Ahi, Alo [M,K]      (K-major as is)
 //  2. pb_split_transpose: B [K,N]  -> Bhi, Blo [N,K]      (to K-major)
 //  3. pb_gemm_tc:         one 128x256 output tile per CTA, 128 threads.
-//     warp 0 lane 0 issues TMA loads (128B swizzle, BK = 32 fp32) into a
-//     2-stage ring of {Ahi, Alo, Bhi, Blo} tiles (96 KB per stage); warp 1
+//     warp 0 lane 0 issues TMA loads (64B swizzle, BK = 16 fp32 = one 64-byte
+//     swizzle row) into a 4-stage ring of {Ahi, Alo, Bhi, Blo} tiles (48 KB
+//     per stage, 192 KB in all: three stages are in flight while the MMAs
+//     read the fourth, about 1.8 us of tensor work, enough to cover TMA
+//     latency from L2 or HBM); warp 1
 //     allocates 512 TMEM columns and its lane 0 issues tcgen05.mma
-//     (kind::tf32, M=128, N=256, K=8; 3 products x 4 k-steps per stage):
+//     (kind::tf32, M=128, N=256, K=8; 3 products x 2 k-steps per stage):
 //     Ahi*Bhi accumulates in columns 0..255 and the small Ahi*Blo + Alo*Bhi
 //     terms in columns 256..511, so the large accumulator is rounded once per
 //     k-step instead of three times; the epilogue adds the two,
@@ -38,14 +41,15 @@ namespace porch::detail {
 
         constexpr int kBM = 128;
         constexpr int kBN = 256;
-        constexpr int kBK = 32;
+        constexpr int kBK = 16;
+        constexpr int kStages = 4;
 
         const char* gemm_device_source() {
             return R"PB(
 #define PB_BM 128
 #define PB_BN 256
-#define PB_BK 32
-#define PB_STAGES 2
+#define PB_BK 16
+#define PB_STAGES 4
 #define PB_TILE_A_BYTES (PB_BM * PB_BK * 4)
 #define PB_TILE_B_BYTES (PB_BN * PB_BK * 4)
 #define PB_STAGE_BYTES (2 * PB_TILE_A_BYTES + 2 * PB_TILE_B_BYTES)
@@ -95,15 +99,17 @@ static __device__ __forceinline__ void pb_tma_load(pb_u32 dst, const pb_tmap* ma
                  :: "r"(dst), "l"((unsigned long long)map), "r"(bar), "r"(x), "r"(y) : "memory");
 }
 
-// tcgen05 shared-memory matrix descriptor: K-major, 128B swizzle, 8-row
-// groups 1024 B apart (SBO), start address in 16-byte units.
+// tcgen05 shared-memory matrix descriptor: K-major, 64B swizzle (one
+// 64-byte row = 16 fp32 of K per tile row), 8-row groups 8 x 64 = 512 B
+// apart (SBO), start address in 16-byte units. Tiles start on 1024-byte
+// boundaries, so the swizzle phase (base offset field) is 0.
 static __device__ __forceinline__ pb_u64 pb_desc(pb_u32 addr) {
     pb_u64 d = 0;
     d |= (pb_u64)((addr & 0x3FFFFu) >> 4);
     d |= (pb_u64)1 << 16;             // leading byte offset (unused for swizzled K-major)
-    d |= (pb_u64)(1024 >> 4) << 32;   // stride byte offset
+    d |= (pb_u64)(512 >> 4) << 32;    // stride byte offset
     d |= (pb_u64)1 << 46;             // fixed 0b001
-    d |= (pb_u64)2 << 61;             // 128-byte swizzle
+    d |= (pb_u64)4 << 61;             // 64-byte swizzle
     return d;
 }
 
@@ -376,11 +382,11 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
         for (size_t i = 0; i < k.leaves.size(); ++i) src << "const float* __restrict__ in" << i << ", ";
         src << "float* __restrict__ out, int* __restrict__ err) {\n" << body.str() << "}\n";
         l.source = src.str();
-        l.schedule = "gemm tcgen05 3xTF32 128x256x32, 2-stage TMA ring (no multicast), TMEM accumulator, "
-                     "fused epilogue, grouped tile order";
+        l.schedule = "gemm tcgen05 3xTF32 128x256x16, 4-stage TMA ring (64B swizzle, no multicast), "
+                     "TMEM accumulator, fused epilogue, grouped tile order";
         l.grid = {static_cast<uint32_t>(tiles_m * tiles_n), 1, 1};
         l.block = {128, 1, 1};
-        l.smem = 2 * (2 * kBM * kBK * 4 + 2 * kBN * kBK * 4) + 1024;
+        l.smem = kStages * (2 * kBM * kBK * 4 + 2 * kBN * kBK * 4) + 1024;
         auto tmap_arg = [&](int temp, int64_t rows, int box_rows) {
             kernel_arg a;
             a.kind = arg_kind::tmap;
@@ -389,6 +395,7 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
             a.cols = K;
             a.box_rows = box_rows;
             a.box_cols = kBK;
+            a.swizzle = 2; // 64B: the box's 16-fp32 inner extent is one swizzle row
             return a;
         };
         l.args = {tmap_arg(a_hi, M, kBM), tmap_arg(a_lo, M, kBM), tmap_arg(b_hi, N, kBN),

@@ -361,7 +361,19 @@ namespace porch::detail {
                 check(pbrt_get_function(device, l.image_key, l.name.c_str(), &fn));
                 if (l.smem > 48 * 1024)
                     check(pbrt_function_set_max_dynamic_smem(fn, static_cast<int>(l.smem)));
-                if (device < static_cast<int>(l.functions.size())) l.functions[device] = fn;
+                uint32_t pgrid = 0;
+                if (l.persistent_units > 0) {
+                    int per_sm = 0, sms = 0;
+                    check(pbrt_occupancy(device, fn, static_cast<int>(l.block[0] * l.block[1] * l.block[2]),
+                                         l.smem, &per_sm));
+                    check(pbrt_device_attribute(device, 16 /* multiprocessor count */, &sms));
+                    const int64_t fit = std::max<int64_t>(1, int64_t{per_sm} * sms);
+                    pgrid = static_cast<uint32_t>(std::min<int64_t>(l.persistent_units, fit));
+                }
+                if (device < static_cast<int>(l.functions.size())) {
+                    l.persistent_grid[device] = pgrid;
+                    l.functions[device] = fn;
+                }
             }
             if (l.args.size() > 64) throw std::runtime_error("kernel has too many arguments");
             for (size_t i = 0; i < l.args.size(); ++i) {
@@ -393,10 +405,10 @@ namespace porch::detail {
                         const uint32_t box[2] = {static_cast<uint32_t>(a.box_cols),
                                                  static_cast<uint32_t>(a.box_rows)};
                         const uint32_t estride[2] = {1, 1};
-                        // fp32, no interleave, 128-byte swizzle, 256-byte L2
-                        // promotion, zero fill.
+                        // fp32, no interleave, the kernel's swizzle, 256-byte
+                        // L2 promotion, zero fill.
                         check(pbrt_tensor_map_encode_tiled(maps[nmaps].bytes, 7, 2, base, dims,
-                                                           strides, box, estride, 0, 3, 3, 0));
+                                                           strides, box, estride, 0, a.swizzle, 3, 0));
                         params[i] = maps[nmaps].bytes;
                         ++nmaps;
                         continue;
@@ -404,7 +416,11 @@ namespace porch::detail {
                 }
                 params[i] = &values[i];
             }
-            check(pbrt_launch(device, fn, l.grid.data(), l.block.data(), l.smem,
+            std::array<uint32_t, 3> grid = l.grid;
+            if (l.persistent_units > 0 && device < static_cast<int>(l.persistent_grid.size()) &&
+                l.persistent_grid[device] != 0)
+                grid[0] = l.persistent_grid[device];
+            check(pbrt_launch(device, fn, grid.data(), l.block.data(), l.smem,
                               stream->stream, params, nullptr));
         }
         if (timing) t3 = now_ns();

@@ -1366,13 +1366,19 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
         for (int d = 0; d < R; ++d) cvar[static_cast<size_t>(d)] = "c" + std::to_string(d);
         const char* comps[4] = {"x", "y", "z", "w"};
         std::ostringstream body;
-        body << "    __shared__ float red[32];\n";
+        // Separate partial arrays for the max and the sum: each reduction
+        // then needs one barrier (the other reduction's barrier orders a
+        // row's reads before the next row's writes).
+        body << "    __shared__ float red_m[32], red_s[32];\n";
         body << "    const pb_u32 warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;\n";
-        body << "    for (" << I << " row = blockIdx.x; row < " << lit(rows, wide) << "; row += gridDim.x) {\n";
-        body << "        " << I << " t = row;\n";
-        for (int d = static_cast<int>(ax) - 1; d >= 0; --d)
-            body << "        const " << I << " c" << d << " = t % " << lit(S[static_cast<size_t>(d)], wide) << "; t /= "
-                 << lit(S[static_cast<size_t>(d)], wide) << ";\n";
+        // Declares the row coordinates c0..c(ax-1) of row `r` in a scope.
+        auto emit_row_coords = [&](const std::string& r, const std::string& indent) {
+            body << indent << I << " t = " << r << ";\n";
+            for (int d = static_cast<int>(ax) - 1; d >= 0; --d)
+                body << indent << "const " << I << " c" << d << " = t % " << lit(S[static_cast<size_t>(d)], wide)
+                     << "; t /= " << lit(S[static_cast<size_t>(d)], wide) << ";\n";
+            body << indent << "(void)t;\n";
+        };
         // Loads the operand value vector at column k into float xv[V].
         auto emit_load = [&](const std::string& k, const std::string& dst, const std::string& indent) {
             body << indent << "{\n" << indent << "    const " << I << " c" << ax << " = " << k << ";\n";
@@ -1405,25 +1411,41 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
             body << "        #pragma unroll\n        for (int o = 16; o > 0; o >>= 1) { const float v = __shfl_xor_sync(0xffffffffu, "
                  << var << ", o); " << comb << " }\n";
             if (T > 32) {
-                body << "        if (lane == 0) red[warp] = " << var << ";\n        __syncthreads();\n";
-                body << "        if (warp == 0) {\n            " << var << " = lane < " << T / 32 << "u ? red[lane] : "
-                     << (is_max ? "PB_NEG_FLT_MAX" : "0.0f") << ";\n";
-                body << "            #pragma unroll\n            for (int o = 16; o > 0; o >>= 1) { const float v = __shfl_xor_sync(0xffffffffu, "
-                     << var << ", o); " << comb << " }\n";
-                body << "            if (lane == 0) red[0] = " << var << ";\n        }\n";
-                body << "        __syncthreads();\n        " << var << " = red[0];\n        __syncthreads();\n";
+                // Every thread combines the warps' partials in the same order,
+                // so all hold the same value.
+                const std::string red = is_max ? "red_m" : "red_s";
+                body << "        if (lane == 0) " << red << "[warp] = " << var << ";\n        __syncthreads();\n";
+                body << "        " << var << " = " << red << "[0];\n";
+                body << "        #pragma unroll\n        for (int w = 1; w < " << T / 32 << "; ++w) { const float v = "
+                     << red << "[w]; " << comb << " }\n";
             }
         };
         const std::string orow = "row * " + lit(A, wide);
         if (in_registers) {
+            // Software pipeline over the CTA's rows: the next row's loads are
+            // issued before this row's reductions, so HBM stays busy while
+            // the block waits at its barriers.
+            auto emit_row_loads = [&](const std::string& r, const std::string& dst, const std::string& indent) {
+                body << indent << "{\n";
+                emit_row_coords(r, indent + "    ");
+                body << indent << "    #pragma unroll\n" << indent << "    for (int it = 0; it < " << NI << "; ++it) {\n";
+                body << indent << "        const " << I << " k = ((" << I << ")it * " << T << "u + threadIdx.x) * " << V
+                     << "u;\n";
+                body << indent << "        if (k < " << lit(A, wide) << ") ";
+                emit_load("k", dst + "[it]", indent + "        ");
+                body << indent << "        else { ";
+                for (int e = 0; e < V; ++e) body << dst << "[it][" << e << "] = PB_NEG_FLT_MAX; ";
+                body << "}\n" << indent << "    }\n" << indent << "}\n";
+            };
+            body << "    float xn[" << NI << "][" << V << "];\n";
+            body << "    if (blockIdx.x < " << lit(rows, wide) << ")\n";
+            emit_row_loads("blockIdx.x", "xn", "    ");
+            body << "    for (" << I << " row = blockIdx.x; row < " << lit(rows, wide) << "; row += gridDim.x) {\n";
             body << "        float x[" << NI << "][" << V << "];\n";
-            body << "        #pragma unroll\n        for (int it = 0; it < " << NI << "; ++it) {\n";
-            body << "            const " << I << " k = ((" << I << ")it * " << T << "u + threadIdx.x) * " << V << "u;\n";
-            body << "            if (k < " << lit(A, wide) << ") ";
-            emit_load("k", "x[it]", "            ");
-            body << "            else { ";
-            for (int e = 0; e < V; ++e) body << "x[it][" << e << "] = PB_NEG_FLT_MAX; ";
-            body << "}\n        }\n";
+            body << "        #pragma unroll\n        for (int it = 0; it < " << NI << "; ++it)\n";
+            body << "            #pragma unroll\n            for (int e = 0; e < " << V << "; ++e) x[it][e] = xn[it][e];\n";
+            body << "        if (row + gridDim.x < " << lit(rows, wide) << ")\n";
+            emit_row_loads("row + gridDim.x", "xn", "        ");
             body << "        float m = PB_NEG_FLT_MAX;\n";
             body << "        #pragma unroll\n        for (int it = 0; it < " << NI << "; ++it)\n";
             body << "            #pragma unroll\n            for (int e = 0; e < " << V
@@ -1447,6 +1469,8 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
             body << "            }\n        }\n";
         } else {
             // Rows too long for registers: max pass, sum pass, write pass.
+            body << "    for (" << I << " row = blockIdx.x; row < " << lit(rows, wide) << "; row += gridDim.x) {\n";
+            emit_row_coords("row", "        ");
             body << "        float m = PB_NEG_FLT_MAX;\n";
             body << "        for (" << I << " k = threadIdx.x * " << V << "u; k < " << lit(A, wide) << "; k += "
                  << T * V << "u) {\n            float xv[" << V << "];\n";
@@ -1473,9 +1497,11 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
         l.source = src.str();
         const int64_t per_sm = 2048 / T;
         l.grid = {static_cast<uint32_t>(std::min<int64_t>(rows, 148 * per_sm)), 1, 1};
+        l.persistent_units = rows; // grid = CTAs resident at once, fixed at first launch
         l.block = {static_cast<uint32_t>(T), 1, 1};
         l.schedule = "softmax row kernel T=" + std::to_string(T) + " V=" + std::to_string(V) +
-                     (in_registers ? " (row in registers, 1 read + 1 write)" : " (3-pass streaming)");
+                     (in_registers ? " (row in registers, next row prefetched, 1 read + 1 write)"
+                                   : " (3-pass streaming)");
         l.args = r.k.leaves;
         kernel_arg o;
         o.kind = arg_kind::temp;

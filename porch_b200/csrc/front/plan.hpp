@@ -60,6 +60,7 @@ namespace porch::detail {
         int64_t cols = 0;
         int box_rows = 0;
         int box_cols = 0;
+        int swizzle = 3; // CUtensorMapSwizzle: 1 = 32B, 2 = 64B, 3 = 128B
     };
 
     struct launch_spec {
@@ -71,6 +72,12 @@ namespace porch::detail {
         std::array<uint32_t, 3> block{256, 1, 1};
         uint32_t smem = 0;
         std::vector<kernel_arg> args;
+        // Persistent kernels loop over `persistent_units` work units with a
+        // grid-stride loop; their grid is fixed on first launch per device to
+        // exactly the CTAs that fit at once (SMs x occupancy), so no CTA waits
+        // for a second wave. 0 = launch `grid` as given.
+        int64_t persistent_units = 0;
+        std::array<uint32_t, 16> persistent_grid{};
         // Resolved function handle per device (filled on first launch).
         std::array<pbrt_function, 16> functions{};
         std::mutex* resolve_mutex = nullptr;

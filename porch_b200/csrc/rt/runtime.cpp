@@ -111,6 +111,8 @@ dl_handle open_first(std::initializer_list<const char*> names) {
       CUresult (*)(CUfunction, CUfunction_attribute, int))                   \
     X(cuFuncGetAttribute,                                                    \
       CUresult (*)(int*, CUfunction_attribute, CUfunction))                  \
+    X(cuOccupancyMaxActiveBlocksPerMultiprocessor,                           \
+      CUresult (*)(int*, CUfunction, int, size_t))                           \
     X(cuLaunchKernelEx, CUresult (*)(const CUlaunchConfig*, CUfunction,      \
                                      void**, void**))                        \
     X(cuTensorMapEncodeTiled,                                                \
@@ -1066,6 +1068,20 @@ int pbrt_function_attribute(pbrt_function function, int attribute, int* value) {
                                             static_cast<CUfunction_attribute>(attribute),
                                             reinterpret_cast<CUfunction>(function)),
                  "cuFuncGetAttribute");
+}
+
+int pbrt_occupancy(int device, pbrt_function function, int block_threads, size_t dynamic_smem,
+                   int* blocks_per_sm) {
+    if (function == nullptr || blocks_per_sm == nullptr || block_threads <= 0)
+        return fail(PBRT_ERR_INVALID, "invalid occupancy query");
+    environment* env = nullptr;
+    int s = use_device(device, env);
+    if (s != PBRT_OK) return s;
+    return check(*env,
+                 env->cu.cuOccupancyMaxActiveBlocksPerMultiprocessor(
+                     blocks_per_sm, reinterpret_cast<CUfunction>(function), block_threads,
+                     dynamic_smem),
+                 "cuOccupancyMaxActiveBlocksPerMultiprocessor");
 }
 
 int pbrt_launch(int device, pbrt_function function, const uint32_t* grid,

@@ -1,0 +1,56 @@
+"""Realises one benchmark graph a few times, for a profiler to capture.
+
+    python -m porch_b200.profile_case c3a_softmax --rows 16384 --steps 3
+
+Builds the named configuration's graph (porch_b200.api.config_graph) on
+seeded synthetic inputs whose leading dimension is cut to --rows (0 keeps
+the benchmark's full shape), realises it --steps times on --device and
+synchronises. Nothing is timed here: under ncu the per-launch figures come
+from the profiler; without it the run only checks that the case exits 0.
+"""
+
+from __future__ import annotations
+
+import argparse
+
+import numpy as np
+
+from porch_b200 import api
+
+DISTRIBUTIONS = {
+    "c1_elementwise": [("uniform", -1, 1), ("uniform", -1, 1)],
+    "c2_view": [("normal", 0, 1), ("uniform", -0.5, 0.5), ("normal", 0, 1)],
+    "c3a_softmax": [("normal", 0, 2)],
+    "c3b_relu_logistic": [("normal", 0, 2)],
+    "c4_matmul": [("uniform", -1 / 90.50966799187808, 1 / 90.50966799187808)] * 2 + [("uniform", -0.1, 0.1)],
+    "c5_mlp": [("normal", 0, 1), ("normal", 0, 1 / 64), ("uniform", -0.1, 0.1), ("normal", 0, 1 / 128),
+               ("uniform", -0.1, 0.1)],
+}
+# Inputs whose leading dimension is the graph's row axis (cut by --rows).
+ROW_INPUTS = {"c3a_softmax": {"x"}, "c3b_relu_logistic": {"x"}, "c4_matmul": {"a"}, "c5_mlp": {"x"}}
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("workload", choices=sorted(api.CONFIG_SHAPES))
+    ap.add_argument("--rows", type=int, default=0)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--device", type=int, default=0)
+    args = ap.parse_args()
+    shapes = api.CONFIG_SHAPES[args.workload]
+    tensors = {}
+    for i, ((key, shape), (dist, a, b)) in enumerate(zip(shapes.items(), DISTRIBUTIONS[args.workload])):
+        shape = list(shape)
+        if args.rows and key in ROW_INPUTS.get(args.workload, ()):
+            shape[0] = args.rows
+        arr = np.empty(int(np.prod(shape)), dtype=np.float32)
+        api.fill_synthetic(arr, 20261201 + i, dist, a, b)
+        tensors[key] = api.tensor(shape, arr, device=args.device)
+    graph = api.config_graph(args.workload, tensors)
+    outs = [api.materialize(graph) for _ in range(max(1, args.steps))]
+    api.device_synchronize(args.device)
+    print(f"{args.workload}: {len(outs)} realisations of shape {outs[-1].shape()}")
+
+
+if __name__ == "__main__":
+    main()
