@@ -11,7 +11,7 @@
 // Launches:
 //  1. pb_split_rows:      A [M,K]  -> Ahi, Alo [M,K]      (K-major as is)
 //  2. pb_split_transpose: B [K,N]  -> Bhi, Blo [N,K]      (to K-major)
-//  3. pb_gemm_tc:         one 128x256 output tile per CTA, 128 threads.
+//  3. pb_gemm_tc:         one 128x256 output tile per CTA, 256 threads.
 //     warp 0 lane 0 issues TMA loads (64B swizzle, BK = 16 fp32 = one 64-byte
 //     swizzle row) into a 4-stage ring of {Ahi, Alo, Bhi, Blo} tiles (48 KB
 //     per stage, 192 KB in all: three stages are in flight while the MMAs
@@ -23,9 +23,9 @@
 //     terms in columns 256..511, so the large accumulator is rounded once per
 //     k-step instead of three times; the epilogue adds the two,
 //     committing each stage back to the producer and the last one to the
-//     epilogue barrier; then all four warps read the accumulator with
-//     tcgen05.ld (warp w owns TMEM lanes 32w..32w+31 = tile rows), apply the
-//     fused epilogue and store.
+//     epilogue barrier; then all eight warps read the accumulators with
+//     tcgen05.ld (warp w owns TMEM lanes 32(w%4)..+31 = tile rows, and
+//     column half w/4), apply the fused epilogue and store.
 // Every mbarrier wait is bounded (clock64 budget); on expiry the kernel
 // records a code in the device error word, stops issuing, waits (bounded)
 // for its own copies and MMAs in flight, frees its TMEM and returns.
@@ -323,30 +323,68 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
              << "        pb_commit(pb_smem(&acc_bar));\n"
              << "    }\n"
              << "    __syncwarp();\n"
-             // epilogue: all four warps
-             << "    const bool acc_ok = pb_wait(pb_smem(&acc_bar), 0u, &abort_flag, err, 3) && !abort_flag;\n"
+             // epilogue: all eight warps. Warp w reads TMEM lanes
+             // 32*(w%4).. (its tile rows; tcgen05.ld lets warps w and w+4
+             // share a lane quadrant) and columns half w/4 of the tile.
+             << "    const bool acc_ok = __all_sync(0xffffffffu, pb_wait(pb_smem(&acc_bar), 0u, &abort_flag, err, 3) && !abort_flag);\n"
              << "    asm volatile(\"tcgen05.fence::after_thread_sync;\" ::: \"memory\");\n"
              << "    if (acc_ok) {\n"
-             << "        const int r = m0 + (int)(warp * 32u + lane);\n"
-             << "        for (int c = 0; c < PB_BN / 32; ++c) {\n"
-             << "            pb_u32 v[32], w[32];\n"
-             << "            PB_TMEM_LD32(tmem + ((warp * 32u) << 16) + (pb_u32)(c * 32), v);\n"
-             << "            PB_TMEM_LD32(tmem + ((warp * 32u) << 16) + (pb_u32)(PB_BN + c * 32), w);\n"
-             << "            asm volatile(\"tcgen05.wait::ld.sync.aligned;\" ::: \"memory\");\n"
-             << "            const int cbase = n0 + c * 32;\n"
-             << "            float* orow = out + (pb_u64)r * " << N << "ull + cbase;\n"
-             << "            #pragma unroll\n"
-             << "            for (int j = 0; j < 32; j += 4) {\n"
-             << "                float y[4];\n"
-             << "                #pragma unroll\n"
-             << "                for (int e = 0; e < 4; ++e) {\n"
-             << "                    const pb_u64 rr = (pb_u64)r, cc = (pb_u64)(cbase + j + e);\n"
-             << "                    (void)rr; (void)cc;\n";
-        std::vector<std::string> cvar = {"rr", "cc"};
+             << "        const pb_u32 quad = warp & 3u, half = warp >> 2;\n"
+             << "        const int r = m0 + (int)(quad * 32u + lane);\n"
+             << "        const pb_u64 rr = (pb_u64)r;\n"
+             << "        (void)rr;\n";
+        // Leaf loads by column stride: 1 and 16-byte aligned -> float4 per
+        // 4 columns; 0 -> one load per row, hoisted out of the column loops;
+        // otherwise one scalar per element.
+        std::vector<int> leaf_mode(order.size());
         for (size_t li = 0; li < order.size(); ++li) {
             const vnode& v = b.nodes[static_cast<size_t>(order[li])];
-            body << "                    const float x" << li << " = pb_ld(in" << v.buffer << " + "
+            const int64_t sr = v.map.st[0], sc = v.map.st[1];
+            if (sc == 0) {
+                leaf_mode[li] = 0;
+                std::vector<std::string> cv = {"rr", "0"};
+                body << "        const float h" << li << " = pb_ld(in" << v.buffer << " + "
+                     << address(v.map, cv, true, 1) << ");\n";
+            } else if (sc == 1 && v.map.off % 4 == 0 && sr % 4 == 0) {
+                leaf_mode[li] = 1;
+            } else {
+                leaf_mode[li] = 2;
+            }
+        }
+        body << "        for (int c = (int)half * (PB_BN / 64); c < ((int)half + 1) * (PB_BN / 64); ++c) {\n"
+             << "            pb_u32 v[32], w[32];\n"
+             << "            PB_TMEM_LD32(tmem + ((quad * 32u) << 16) + (pb_u32)(c * 32), v);\n"
+             << "            PB_TMEM_LD32(tmem + ((quad * 32u) << 16) + (pb_u32)(PB_BN + c * 32), w);\n"
+             << "            asm volatile(\"tcgen05.wait::ld.sync.aligned;\" ::: \"memory\");\n"
+             << "            const int cbase = n0 + c * 32;\n"
+             << "            float* orow = out + rr * " << N << "ull + cbase;\n"
+             << "            #pragma unroll\n"
+             << "            for (int j = 0; j < 32; j += 4) {\n"
+             << "                const pb_u64 cc = (pb_u64)(cbase + j);\n"
+             << "                (void)cc;\n";
+        std::vector<std::string> cvar = {"rr", "cc"};
+        for (size_t li = 0; li < order.size(); ++li) {
+            if (leaf_mode[li] != 1) continue;
+            const vnode& v = b.nodes[static_cast<size_t>(order[li])];
+            body << "                const float4 q" << li << " = pb_ld4(in" << v.buffer << " + "
                  << address(v.map, cvar, true, -1) << ");\n";
+        }
+        body << "                float y[4];\n"
+             << "                #pragma unroll\n"
+             << "                for (int e = 0; e < 4; ++e) {\n"
+             << "                    const pb_u64 ce = cc + (pb_u64)e;\n"
+             << "                    (void)ce;\n";
+        std::vector<std::string> evar = {"rr", "ce"};
+        for (size_t li = 0; li < order.size(); ++li) {
+            const vnode& v = b.nodes[static_cast<size_t>(order[li])];
+            if (leaf_mode[li] == 0)
+                body << "                    const float x" << li << " = h" << li << ";\n";
+            else if (leaf_mode[li] == 1)
+                body << "                    const float x" << li << " = e == 0 ? q" << li << ".x : e == 1 ? q" << li
+                     << ".y : e == 2 ? q" << li << ".z : q" << li << ".w;\n";
+            else
+                body << "                    const float x" << li << " = pb_ld(in" << v.buffer << " + "
+                     << address(v.map, evar, true, -1) << ");\n";
         }
         body << "                    y[e] = pb_e0(__uint_as_float(v[j + e]) + __uint_as_float(w[j + e])";
         for (size_t li = 0; li < order.size(); ++li) body << ", x" << li;
@@ -376,7 +414,7 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
              << "    }\n";
         launch_spec l;
         l.name = "pb_gemm_tc_" + hex8(src.str() + body.str());
-        src << "extern \"C\" __global__ void __launch_bounds__(128, 1) " << l.name
+        src << "extern \"C\" __global__ void __launch_bounds__(256, 1) " << l.name
             << "(const __grid_constant__ pb_tmap tm_ahi, const __grid_constant__ pb_tmap tm_alo, "
                "const __grid_constant__ pb_tmap tm_bhi, const __grid_constant__ pb_tmap tm_blo, ";
         for (size_t i = 0; i < k.leaves.size(); ++i) src << "const float* __restrict__ in" << i << ", ";
@@ -385,7 +423,7 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
         l.schedule = "gemm tcgen05 3xTF32 128x256x16, 4-stage TMA ring (64B swizzle, no multicast), "
                      "TMEM accumulator, fused epilogue, grouped tile order";
         l.grid = {static_cast<uint32_t>(tiles_m * tiles_n), 1, 1};
-        l.block = {128, 1, 1};
+        l.block = {256, 1, 1};
         l.smem = kStages * (2 * kBM * kBK * 4 + 2 * kBN * kBK * 4) + 1024;
         auto tmap_arg = [&](int temp, int64_t rows, int box_rows) {
             kernel_arg a;
