@@ -206,6 +206,17 @@ int pb_row_block(int64_t rows, int rank, int nranks, int64_t* begin, int64_t* en
  * Returns once the gather has completed on the device. */
 int pb_allgather_rows(pb_comm* comm, const pb_tensor* shard, int64_t total_rows,
                       pb_tensor** out);
+/* The same gather enqueued on the communicator's own stream, returning at
+ * once: it waits (on the device) for the shard's producer, and whatever
+ * later reads the result waits for the gather the same way, so the gather
+ * overlaps compute enqueued after it. pb_comm_wait is the bounded
+ * completion check (it aborts the communicator on timeout or error); call it
+ * before reading results on the host if a peer may fail. */
+int pb_allgather_rows_async(pb_comm* comm, const pb_tensor* shard, int64_t total_rows,
+                            pb_tensor** out);
+/* Waits, bounded by the communicator's timeout, until every asynchronous
+ * gather issued so far has completed. */
+int pb_comm_wait(pb_comm* comm);
 
 /* ---- matmul without allocation ------------------------------------------ */
 /* C = A @ B in fp32 (3xTF32 on tcgen05), on raw device pointers, allocating

@@ -76,6 +76,8 @@ int pbrt_event_create(int device, int enable_timing, pbrt_event* event);
 int pbrt_event_destroy(int device, pbrt_event event);
 int pbrt_event_record(int device, pbrt_event event, pbrt_stream stream);
 int pbrt_event_synchronize(int device, pbrt_event event);
+/* *done = 1 when every operation before the event has completed, else 0. */
+int pbrt_event_query(int device, pbrt_event event, int* done);
 int pbrt_event_elapsed_ms(pbrt_event start, pbrt_event end, float* ms);
 int pbrt_stream_wait_event(int device, pbrt_stream stream, pbrt_event event);
 

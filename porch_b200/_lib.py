@@ -96,6 +96,8 @@ def _declare(L: ctypes.CDLL) -> None:
         "pb_comm_release": (c_int, [c_void_p]),
         "pb_row_block": (c_int, [c_int64, c_int, c_int, P(c_int64), P(c_int64)]),
         "pb_allgather_rows": (c_int, [c_void_p, c_void_p, c_int64, P(c_void_p)]),
+        "pb_allgather_rows_async": (c_int, [c_void_p, c_void_p, c_int64, P(c_void_p)]),
+        "pb_comm_wait": (c_int, [c_void_p]),
         "pbrt_available": (c_int, []),
         "pbrt_device_count": (c_int, [P(c_int)]),
         "pbrt_last_error": (c_char_p, []),

@@ -636,12 +636,19 @@ class Communicator:
         _check(lib().pb_comm_info(self._h, byref(r), byref(n), byref(d)))
         return r.value, n.value, d.value
 
-    def allgather_rows(self, shard, total_rows: int) -> Tensor:
-        """Whole [total_rows, ...] tensor from every rank's row block."""
+    def allgather_rows(self, shard, total_rows: int, wait: bool = True) -> Tensor:
+        """Whole [total_rows, ...] tensor from every rank's row block.
+        wait=False enqueues the gather on the communicator's stream and
+        returns at once (see wait())."""
         t = shard if isinstance(shard, Tensor) else materialize(shard)
         out = c_void_p()
-        _check(lib().pb_allgather_rows(self._h, t._h, int(total_rows), byref(out)))
+        fn = lib().pb_allgather_rows if wait else lib().pb_allgather_rows_async
+        _check(fn(self._h, t._h, int(total_rows), byref(out)))
         return Tensor(out.value)
+
+    def wait(self) -> None:
+        """Bounded wait for every asynchronous gather issued so far."""
+        _check(lib().pb_comm_wait(self._h))
 
     def set_timeout(self, timeout_s: float) -> None:
         _check(lib().pb_comm_set_timeout(self._h, float(timeout_s)))

@@ -561,6 +561,24 @@ int pb_allgather_rows(pb_comm* comm, const pb_tensor* shard, int64_t total_rows,
     });
 }
 
+int pb_allgather_rows_async(pb_comm* comm, const pb_tensor* shard, int64_t total_rows,
+                            pb_tensor** out) {
+    return guarded([&] {
+        require(comm, "communicator");
+        require(shard, "shard");
+        require(out, "out");
+        *out = nullptr;
+        *out = wrap(porch::detail::allgather_rows(*comm->value, shard->value, total_rows, true));
+    });
+}
+
+int pb_comm_wait(pb_comm* comm) {
+    return guarded([&] {
+        require(comm, "communicator");
+        porch::detail::wait_communicator(*comm->value);
+    });
+}
+
 int pb_profile_enable(int enable) {
     return guarded([&] { porch::detail::check(pbrt_profile_enable(enable)); });
 }

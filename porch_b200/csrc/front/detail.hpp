@@ -90,6 +90,10 @@ namespace porch::detail {
     );
     // Returns a block to the cache (called when its last owner drops it).
     void recycle(int device, uint64_t ptr, size_t capacity, std::shared_ptr<stream_ref> stream);
+    // Returns a block to `stream`'s free list once every (device, event) in
+    // `events` -- recorded behind reads on other streams -- has completed.
+    void defer_recycle(int device, uint64_t ptr, size_t capacity, std::shared_ptr<stream_ref> stream,
+                       std::vector<std::pair<int, pbrt_event>> events);
     // Gives every cached block of `device` back to the driver; returns bytes.
     size_t release_cached_blocks(int device);
     // Makes `stream` wait for the buffer's producer when they differ, and
@@ -245,6 +249,9 @@ namespace porch::detail {
         int device = 0;
         double timeout_s = 60.0; // bound on every host-side wait
         bool aborted = false;
+        // Stream of the asynchronous gathers (created on first use), so a
+        // gather overlaps the compute that the caller enqueues next.
+        std::shared_ptr<stream_ref> stream;
         communicator() = default;
         communicator(const communicator&) = delete;
         communicator& operator=(const communicator&) = delete;
@@ -259,7 +266,14 @@ namespace porch::detail {
     std::pair<index_t, index_t> row_block(index_t rows, int rank, int nranks);
     // Every rank passes its realised row block; every rank receives the whole
     // [total_rows, ...] tensor (row blocks concatenated in rank order).
-    tensor allgather_rows(communicator& c, const tensor& shard, index_t total_rows);
+    // Synchronous: on the caller's stream, returns after a bounded wait for
+    // completion. Asynchronous: on the communicator's own stream, ordered
+    // after the shard's producer by an event; the result's readers order
+    // after it the same way; wait_communicator() is the bounded completion
+    // (and failure) check.
+    tensor allgather_rows(communicator& c, const tensor& shard, index_t total_rows,
+                          bool asynchronous = false);
+    void wait_communicator(communicator& c);
 
     // Human-readable description of the plan chosen for `root` (kernels,
     // schedules and generated sources). Works on placeholder inputs without a

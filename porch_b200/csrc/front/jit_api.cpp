@@ -68,22 +68,59 @@ namespace porch::detail {
 
     // ------------------------------------------------- caching allocator --
     // Freed blocks are kept per device in size classes together with the
-    // stream they were last used on; a request on that same stream reuses one
-    // with no driver call (stream order already makes it safe). Blocks seen by
-    // other streams go back to the driver's stream-ordered pool instead. On
-    // allocation failure every cached block of the device is returned to the
-    // driver and the request retried once.
+    // stream that produced them; a request on that same stream reuses one
+    // with no driver call (stream order already makes it safe). A block also
+    // read on other streams waits in a pending list with an event recorded
+    // on each of those readers, and joins its producer stream's free list
+    // once every event has completed: no stream is ever made to wait for
+    // another, so a reader (a gather on a communicator's stream) overlaps
+    // the producer's next work. On allocation failure every cached block of
+    // the device (pending ones after their readers finish) is returned to
+    // the driver and the request retried once.
     namespace {
         struct cached_block {
             uint64_t ptr;
             std::shared_ptr<stream_ref> stream;
         };
 
+        struct pending_block {
+            uint64_t ptr;
+            size_t capacity;
+            std::shared_ptr<stream_ref> stream;
+            std::vector<std::pair<int, pbrt_event>> events; // (device, event) per foreign reader
+        };
+
         struct device_cache {
             std::mutex mutex;
             std::unordered_map<size_t, std::vector<cached_block>> free;
+            std::vector<pending_block> pending;
             size_t cached_bytes = 0;
         };
+
+        // Moves pending blocks whose readers have all finished to the free
+        // lists. Caller holds dc.mutex.
+        void reap_locked(device_cache& dc) {
+            for (size_t i = 0; i < dc.pending.size();) {
+                pending_block& p = dc.pending[i];
+                bool done = true;
+                for (const auto& [dev, ev] : p.events) {
+                    int d = 0;
+                    if (pbrt_event_query(dev, ev, &d) != PBRT_OK || d == 0) {
+                        done = false;
+                        break;
+                    }
+                }
+                if (!done) {
+                    ++i;
+                    continue;
+                }
+                for (const auto& [dev, ev] : p.events) (void)pbrt_event_destroy(dev, ev);
+                dc.free[p.capacity].push_back({p.ptr, std::move(p.stream)});
+                dc.cached_bytes += p.capacity;
+                dc.pending[i] = std::move(dc.pending.back());
+                dc.pending.pop_back();
+            }
+        }
 
         struct block_cache {
             std::mutex mutex;
@@ -112,16 +149,33 @@ namespace porch::detail {
     size_t release_cached_blocks(int device) {
         device_cache& dc = blocks().of(device);
         std::unordered_map<size_t, std::vector<cached_block>> drop;
+        std::vector<pending_block> waiting;
         size_t bytes = 0;
         {
             std::scoped_lock lock{dc.mutex};
             drop.swap(dc.free);
+            waiting.swap(dc.pending);
             bytes = dc.cached_bytes;
             dc.cached_bytes = 0;
         }
         for (auto& [size, list] : drop)
             for (auto& b : list) (void)pbrt_mem_free_async(device, b.ptr, b.stream->stream);
+        for (auto& p : waiting) {
+            for (const auto& [dev, ev] : p.events) {
+                (void)pbrt_event_synchronize(dev, ev);
+                (void)pbrt_event_destroy(dev, ev);
+            }
+            (void)pbrt_mem_free_async(device, p.ptr, p.stream->stream);
+            bytes += p.capacity;
+        }
         return bytes;
+    }
+
+    void defer_recycle(int device, uint64_t ptr, size_t capacity, std::shared_ptr<stream_ref> stream,
+                       std::vector<std::pair<int, pbrt_event>> events) {
+        device_cache& dc = blocks().of(device);
+        std::scoped_lock lock{dc.mutex};
+        dc.pending.push_back({ptr, capacity, std::move(stream), std::move(events)});
     }
 
     cuda_jit::device_buffer allocate(
@@ -136,6 +190,7 @@ namespace porch::detail {
             device_cache& dc = blocks().of(device);
             {
                 std::scoped_lock lock{dc.mutex};
+                if (!dc.pending.empty()) reap_locked(dc);
                 auto it = dc.free.find(cls);
                 if (it != dc.free.end()) {
                     auto& list = it->second;
@@ -218,15 +273,34 @@ namespace porch::cuda_jit {
                 detail::recycle(device, ptr, capacity, std::move(free_stream));
                 return;
             }
-            // Order the driver free after every reader on another stream.
+            // Read on other streams: an event behind each of those reads;
+            // the block rejoins the producer stream's free list once they
+            // have all completed (the producer's own later reads are ordered
+            // by its stream). Nothing waits now.
+            std::vector<std::pair<int, pbrt_event>> events;
+            bool ok = true;
             for (const auto& reader : readers) {
                 if (reader == free_stream) continue;
                 pbrt_event e = nullptr;
-                if (pbrt_event_create(reader->device, 0, &e) != PBRT_OK) continue;
-                (void)pbrt_event_record(reader->device, e, reader->stream);
-                (void)pbrt_stream_wait_event(free_stream->device, free_stream->stream, e);
-                (void)pbrt_event_destroy(reader->device, e);
+                if (pbrt_event_create(reader->device, 0, &e) != PBRT_OK) {
+                    ok = false;
+                    break;
+                }
+                events.emplace_back(reader->device, e);
+                if (pbrt_event_record(reader->device, e, reader->stream) != PBRT_OK) {
+                    ok = false;
+                    break;
+                }
             }
+            if (ok && capacity != 0) {
+                detail::defer_recycle(device, ptr, capacity, std::move(free_stream), std::move(events));
+                return;
+            }
+            // No events (or a block from outside the cache): drain the
+            // readers on the host, then a stream-ordered free.
+            for (const auto& [dev, ev] : events) (void)pbrt_event_destroy(dev, ev);
+            for (const auto& reader : readers)
+                if (reader != free_stream) (void)pbrt_stream_synchronize(reader->device, reader->stream);
             (void)pbrt_mem_free_async(device, ptr, free_stream->stream);
         } catch (...) {
         }

@@ -36,6 +36,7 @@ namespace porch::detail {
 
     communicator::~communicator() {
         if (comm != nullptr) (void)pbrt_nccl_destroy(comm);
+        comm = nullptr;
     }
 
     std::unique_ptr<communicator> make_communicator(
@@ -53,7 +54,8 @@ namespace porch::detail {
         return c;
     }
 
-    tensor allgather_rows(communicator& c, const tensor& shard, index_t total_rows) {
+    tensor allgather_rows(communicator& c, const tensor& shard, index_t total_rows,
+                          bool asynchronous) {
         if (c.comm == nullptr || c.aborted)
             throw std::runtime_error("communicator is not usable (aborted or destroyed)");
         if (shard.rank() == 0) throw std::invalid_argument("allgather_rows needs a tensor of rank >= 1");
@@ -73,7 +75,12 @@ namespace porch::detail {
         const size_t out_count = checked_numel(out_shape);
 
         auto storage_in = tensor_access::storage(shard); // realises a lazy shard
-        auto stream = current_stream(c.device);
+        if (asynchronous && c.stream == nullptr) {
+            pbrt_stream s = nullptr;
+            check(pbrt_stream_create(c.device, &s));
+            c.stream = std::make_shared<stream_ref>(c.device, s);
+        }
+        auto stream = asynchronous ? c.stream : current_stream(c.device);
         auto storage = std::make_shared<realized_storage>();
         storage->count = out_count;
         storage->device = c.device;
@@ -121,7 +128,7 @@ namespace porch::detail {
         // Bounded wait: a peer that never arrives (or an asynchronous NCCL
         // error) aborts the communicator and surfaces here as an exception,
         // instead of hanging a later synchronize.
-        if (status == PBRT_OK)
+        if (status == PBRT_OK && !asynchronous)
             status = pbrt_nccl_wait(c.comm, c.device, stream->stream, c.timeout_s);
         if (status != PBRT_OK) {
             abort_communicator(c);
@@ -130,6 +137,17 @@ namespace porch::detail {
         set_producer(out_state, stream);
         return tensor_access::from_storage(std::move(out_shape), std::move(storage),
                                            shard.placement());
+    }
+
+    void wait_communicator(communicator& c) {
+        if (c.comm == nullptr || c.aborted)
+            throw std::runtime_error("communicator is not usable (aborted or destroyed)");
+        if (c.stream == nullptr) return;
+        const int status = pbrt_nccl_wait(c.comm, c.device, c.stream->stream, c.timeout_s);
+        if (status != PBRT_OK) {
+            abort_communicator(c);
+            throw_status(status);
+        }
     }
 
     void abort_communicator(communicator& c) {

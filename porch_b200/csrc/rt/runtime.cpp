@@ -726,6 +726,20 @@ int pbrt_event_synchronize(int device, pbrt_event event) {
     return check(*env, env->cu.cuEventSynchronize(reinterpret_cast<CUevent>(event)),
                  "cuEventSynchronize");
 }
+int pbrt_event_query(int device, pbrt_event event, int* done) {
+    if (event == nullptr || done == nullptr) return fail(PBRT_ERR_INVALID, "invalid event query");
+    environment* env = nullptr;
+    int s = use_device(device, env);
+    if (s != PBRT_OK) return s;
+    const CUresult r = env->cu.cuEventQuery(reinterpret_cast<CUevent>(event));
+    if (r == CUDA_ERROR_NOT_READY) {
+        *done = 0;
+        return PBRT_OK;
+    }
+    *done = r == CUDA_SUCCESS ? 1 : 0;
+    return check(*env, r, "cuEventQuery");
+}
+
 
 int pbrt_event_elapsed_ms(pbrt_event start, pbrt_event end, float* ms) {
     environment* env = nullptr;

@@ -155,14 +155,21 @@ def gpu_allgather_worker(rank: int, world: int, port: int, q) -> None:
 
                 expr = graph(np.ascontiguousarray(mlp[0][b:e]), rank)
                 whole_expr = graph(mlp[0], 0) if rank == 0 else None
-            gathered = comm.allgather_rows(api.materialize(expr), rows)
+            shard = api.materialize(expr)
+            gathered = comm.allgather_rows(shard, rows)
             got = gathered.cpu().reshape(gathered.shape())
+            # The asynchronous gather, read back at once: the host read is
+            # ordered after it by events alone; then the bounded wait.
+            late = comm.allgather_rows(shard, rows, wait=False)
+            got_async = late.cpu().reshape(late.shape())
+            comm.wait()
+            same_async = np.array_equal(got.view(np.uint32), got_async.view(np.uint32))
             if rank == 0:
                 want = api.materialize(whole_expr).cpu().reshape(rows, -1)
                 same = np.array_equal(got.view(np.uint32), want.view(np.uint32))
-                details.append((name, bool(same)))
+                details.append((name, bool(same and same_async)))
             else:
-                details.append((name, got.shape[0] == rows))
+                details.append((name, got.shape[0] == rows and same_async))
         comm.close()
         dist.barrier()
         dist.destroy_process_group()
