@@ -1230,6 +1230,32 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
         std::ostringstream body;
         launch_spec l;
         std::string desc;
+        // The loop over the reduction axis of a strided reduction: eight
+        // independent loads (and prologues) per step, then combined in k
+        // order -- the same result as one at a time, with eight loads in
+        // flight per thread.
+        auto emit_strided_loop = [&](std::ostringstream& os, const std::string& from, const std::string& to) {
+            auto value_at = [&](const std::string& k, const std::string& dst, const std::string& ind) {
+                os << ind << "{\n" << ind << "    const " << I << " c" << ax << " = " << k << ";\n";
+                for (size_t li = 0; li < order.size(); ++li) {
+                    const vnode& v = r.b.nodes[static_cast<size_t>(order[li])];
+                    os << ind << "    const float x" << li << " = pb_ld(in" << v.buffer << " + "
+                       << address(v.map, cvar, wide, -1) << ");\n";
+                }
+                os << ind << "    " << dst << " = pb_e0(";
+                for (size_t li = 0; li < order.size(); ++li) os << (li ? ", " : "") << "x" << li;
+                os << ");\n" << ind << "}\n";
+            };
+            os << "    " << I << " k = " << from << ";\n";
+            os << "    for (; k + 8u <= " << to << "; k += 8u) {\n        float vv[8];\n";
+            os << "        #pragma unroll\n        for (int u = 0; u < 8; ++u)\n";
+            value_at("k + (" + I + ")u", "vv[u]", "        ");
+            os << "        #pragma unroll\n        for (int u = 0; u < 8; ++u) { const float v = vv[u]; "
+               << combine("acc", "v") << " }\n    }\n";
+            os << "    for (; k < " << to << "; ++k) {\n        float v;\n";
+            value_at("k", "v", "        ");
+            os << "        " << combine("acc", "v") << "\n    }\n";
+        };
         if (inner == 1) {
             // Row reduction: one warp per output row, 8 rows per CTA.
             bool vec = A % 4 == 0;
@@ -1289,7 +1315,89 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
             desc = "row reduction (warp per row) V=" + std::to_string(V);
         } else {
             // Strided reduction: one thread per output, coalesced across the
-            // inner dimensions.
+            // inner dimensions. When the outputs alone give too few CTAs to
+            // fill the GPU (sum(x, 0) on a tall x), the reduction axis is
+            // also split into row chunks: pass 1 writes one partial per
+            // (chunk, output), pass 2 combines the partials of each output in
+            // chunk order, so the result does not depend on scheduling.
+            const int64_t col_ctas = (outputs + 255) / 256;
+            const int64_t target = 148 * 8;
+            int64_t chunks = 1;
+            if (col_ctas * 2 < target && A >= 64)
+                chunks = std::min<int64_t>((target + col_ctas - 1) / col_ctas, A / 32);
+            if (chunks > 1) {
+                const int64_t per = (A + chunks - 1) / chunks;
+                chunks = (A + per - 1) / per;
+                const int partial = new_temp(static_cast<size_t>(chunks * outputs) * sizeof(float));
+                const bool pwide = wide || chunks * outputs >= (int64_t{1} << 31) - 4096;
+                const std::string PI = pwide ? "pb_u64" : "pb_u32";
+                std::ostringstream b1;
+                b1 << "    const " << I << " o = (" << I << ")blockIdx.x * 256u + threadIdx.x;\n";
+                b1 << "    if (o >= " << lit(outputs, wide) << ") return;\n";
+                b1 << "    " << I << " t = o;\n";
+                for (int d = R - 1; d >= 0; --d) {
+                    if (static_cast<size_t>(d) == ax) continue;
+                    b1 << "    const " << I << " c" << d << " = t % " << lit(S[static_cast<size_t>(d)], wide)
+                       << "; t /= " << lit(S[static_cast<size_t>(d)], wide) << ";\n";
+                }
+                b1 << "    const " << I << " k0 = (" << I << ")blockIdx.y * " << lit(per, wide) << ";\n";
+                b1 << "    const " << I << " k1 = k0 + " << lit(per, wide) << " < " << lit(A, wide) << " ? k0 + "
+                   << lit(per, wide) << " : " << lit(A, wide) << ";\n";
+                b1 << "    float acc = " << init << ";\n";
+                emit_strided_loop(b1, "k0", "k1");
+                b1 << "    part[(" << PI << ")blockIdx.y * " << lit(outputs, pwide) << " + (" << PI << ")o] = acc;\n";
+                launch_spec l1;
+                l1.name = "pb_reduce_part_" + hex64(hash_string(src.str() + b1.str())).substr(0, 8);
+                std::ostringstream s1;
+                s1 << src.str() << "extern \"C\" __global__ void __launch_bounds__(256) " << l1.name << "(";
+                for (size_t i = 0; i < r.k.leaves.size(); ++i) s1 << "const float* __restrict__ in" << i << ", ";
+                s1 << "float* __restrict__ part) {\n" << b1.str() << "}\n";
+                l1.source = s1.str();
+                l1.schedule = std::string(is_sum ? "sum " : "max ") + "strided reduction pass 1 (" +
+                              std::to_string(chunks) + " row chunks of " + std::to_string(per) + ")";
+                l1.grid = {static_cast<uint32_t>(col_ctas), static_cast<uint32_t>(chunks), 1};
+                l1.block = {256, 1, 1};
+                l1.args = r.k.leaves;
+                kernel_arg pa;
+                pa.kind = arg_kind::temp;
+                pa.index = partial;
+                l1.args.push_back(pa);
+                finish_kernel(l1);
+                p_.launches.push_back(std::move(l1));
+
+                std::ostringstream b2;
+                b2 << "    const " << PI << " o = (" << PI << ")blockIdx.x * 256u + threadIdx.x;\n";
+                b2 << "    if (o >= " << lit(outputs, pwide) << ") return;\n";
+                b2 << "    float acc = part[o];\n";
+                b2 << "    " << PI << " c = 1;\n";
+                b2 << "    for (; c + 8u <= " << lit(chunks, pwide) << "; c += 8u) {\n        float vv[8];\n";
+                b2 << "        #pragma unroll\n        for (int u = 0; u < 8; ++u) vv[u] = part[(c + (" << PI
+                   << ")u) * " << lit(outputs, pwide) << " + o];\n";
+                b2 << "        #pragma unroll\n        for (int u = 0; u < 8; ++u) { const float v = vv[u]; "
+                   << combine("acc", "v") << " }\n    }\n";
+                b2 << "    for (; c < " << lit(chunks, pwide) << "; ++c) {\n";
+                b2 << "        const float v = part[c * " << lit(outputs, pwide) << " + o]; " << combine("acc", "v")
+                   << "\n    }\n";
+                b2 << "    out[o] = acc;\n";
+                launch_spec l2;
+                l2.name = "pb_reduce_comb_" + hex64(hash_string(b2.str())).substr(0, 8);
+                std::ostringstream s2;
+                s2 << kernel_prelude() << "extern \"C\" __global__ void __launch_bounds__(256) " << l2.name
+                   << "(const float* __restrict__ part, float* __restrict__ out) {\n" << b2.str() << "}\n";
+                l2.source = s2.str();
+                l2.schedule = std::string(is_sum ? "sum " : "max ") + "strided reduction pass 2 (combine " +
+                              std::to_string(chunks) + " partials in order)";
+                l2.grid = {static_cast<uint32_t>(col_ctas), 1, 1};
+                l2.block = {256, 1, 1};
+                l2.args = {pa};
+                kernel_arg oa;
+                oa.kind = arg_kind::temp;
+                oa.index = out;
+                l2.args.push_back(oa);
+                finish_kernel(l2);
+                p_.launches.push_back(std::move(l2));
+                return out;
+            }
             body << "    const " << I << " o = (" << I << ")blockIdx.x * 256u + threadIdx.x;\n";
             body << "    if (o >= " << lit(outputs, wide) << ") return;\n";
             body << "    " << I << " t = o;\n";
@@ -1299,16 +1407,7 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
                      << lit(S[static_cast<size_t>(d)], wide) << ";\n";
             }
             body << "    float acc = " << init << ";\n";
-            body << "    for (" << I << " k = 0; k < " << lit(A, wide) << "; ++k) {\n";
-            body << "        const " << I << " c" << ax << " = k;\n";
-            for (size_t li = 0; li < order.size(); ++li) {
-                const vnode& v = r.b.nodes[static_cast<size_t>(order[li])];
-                body << "        const float x" << li << " = pb_ld(in" << v.buffer << " + "
-                     << address(v.map, cvar, wide, -1) << ");\n";
-            }
-            body << "        { const float v = pb_e0(";
-            for (size_t li = 0; li < order.size(); ++li) body << (li ? ", " : "") << "x" << li;
-            body << "); " << combine("acc", "v") << " }\n    }\n";
+            emit_strided_loop(body, "(" + I + ")0", lit(A, wide));
             body << "    out[o] = acc;\n";
             const int64_t ctas = (outputs + 255) / 256;
             l.grid = {static_cast<uint32_t>(ctas), 1, 1};

@@ -3,6 +3,11 @@
 - Elementwise / view / indexing graphs: bit-exact (NaNs compared as a class).
 - Reductions, softmax, exp-based graphs: relative error <= 1e-5 per element,
   i.e. |got - want| <= 1e-5 * max(|want|, 1e-30) + 1e-30.
+- Sums over many terms that can cancel (a reduction of signed values):
+  |got - want| <= 1e-5 * max(|want|, sum|x| / sqrt(n)) per output, i.e.
+  relative to the sum's own scale (sqrt(n) times the typical term), since a
+  sum that cancels to near zero has no fp32 evaluation order that meets a
+  bound relative to its tiny result.
 - fp32 matmul: per element |C - C64| / (max(|C64|, rms(C64)) * sqrt(K)) <= 1e-5
   against an fp64 reference C64 (the 1e-5 "relative, normalised by sqrt(K)"
   criterion); plus a sharper check in the matmul tests that the error stays
@@ -43,6 +48,19 @@ def assert_relative(got: np.ndarray, want: np.ndarray, tol: float = REL_TOL, wha
         i = int(np.flatnonzero(bad)[0])
         raise AssertionError(f"{what}: {int(bad.sum())} of {got.size} exceed rel {tol}; first at {i}: "
                              f"got {got[i]!r} want {want[i]!r} rel {err[i] / max(abs(want[i]), 1e-30):.3e}")
+
+
+def assert_sum_close(got: np.ndarray, want: np.ndarray, abs_sum: np.ndarray, n: int,
+                     tol: float = REL_TOL, what: str = "") -> None:
+    got = np.asarray(got, dtype=np.float64).reshape(-1)
+    want = np.asarray(want, dtype=np.float64).reshape(-1)
+    scale = np.maximum(np.abs(want), np.asarray(abs_sum, dtype=np.float64).reshape(-1) / np.sqrt(max(n, 1)))
+    err = np.abs(got - want)
+    bad = err > tol * scale + 1e-30
+    if bad.any():
+        i = int(np.flatnonzero(bad)[0])
+        raise AssertionError(f"{what}: {int(bad.sum())} of {got.size} exceed {tol} of the sum's scale; "
+                             f"first at {i}: got {got[i]!r} want {want[i]!r} scale {scale[i]:.4g}")
 
 
 def matmul_error(got: np.ndarray, want64: np.ndarray, k: int) -> float:
