@@ -281,6 +281,10 @@ def run_ours(args, rank, world, local, dist):
     comm = None
     total_rows = CONFIGS[workload][0][0][0][0]
     if workload in GATHERED and world > 1:
+        # NVLink multicast (NVLS) is left off unless the caller asks for it:
+        # the gather is a plain all-gather, and a rank that dies while bound
+        # to a multicast object can fault the other ranks' GPUs.
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
         uid = [api.comm_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(uid, src=0)
         comm = api.Communicator(world, uid[0], rank, device, timeout_s=120.0)
