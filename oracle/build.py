@@ -5,16 +5,17 @@
   oracle/_build/pb_runner      oracle/ref_runner.cpp against this repository's
                                drop-in headers and libporch_b200.so
   oracle/_ref/libporch_ref.a   the reference library, compiled directly from its
-                               four sources under /root/reference/src (no CMake)
+                               four sources under <reference>/src (no CMake)
   oracle/_ref/ref_runner       oracle/ref_runner.cpp against the reference
   oracle/_ref/ref_conformance  the reference's own tests/tensor_test.cpp against
                                the reference library
   oracle/_ref/pb_conformance   the same unmodified test file against
                                libporch_b200.so (the drop-in check)
 
-The reference is read where it lies and never copied into the repository;
-the _ref outputs are git-ignored and travel to the GPU box with the snapshot.
-When /root/reference is absent (the GPU box) the prebuilt _ref files are used.
+The reference checkout (PORCH_REFERENCE, by default the `reference`
+directory beside this repository) is read where it lies and never copied
+into the repository; the _ref outputs are git-ignored and travel with the
+repository to GPU machines, which have no checkout and use them prebuilt.
 """
 
 from __future__ import annotations
@@ -28,7 +29,7 @@ ORACLE = Path(__file__).resolve().parent
 ROOT = ORACLE.parent
 BUILD = ORACLE / "_build"
 REF_OUT = ORACLE / "_ref"
-REFERENCE = Path(os.environ.get("PORCH_REFERENCE", "/root/reference"))
+REFERENCE = Path(os.environ.get("PORCH_REFERENCE", str(ROOT.parent / "reference")))
 # The system g++ links the C++ runtime dynamically; a toolchain wrapper that
 # embeds a private static copy would give this library its own exported
 # libstdc++ and clash with other C++ code in the process.

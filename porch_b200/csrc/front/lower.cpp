@@ -659,8 +659,6 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
         std::vector<int> order;
         std::ostringstream os;
         os << emit_expr_function(b, std::to_string(tag), order);
-        const bool has_acc = false;
-        (void)has_acc;
         os << "static __device__ __forceinline__ void pb_box" << tag << "(const float* const* L, float* __restrict__ out, pb_u32 cta) {\n";
         os << "    const " << I << " v0 = (" << I << ")cta * " << 256 * U << "u + threadIdx.x;\n";
         // Per-leaf load mode: 0 broadcast scalar, 1 vector, 2 strided scalars.
