@@ -11,27 +11,33 @@
 // Launches:
 //  1. pb_split_rows:      A [M,K]  -> Ahi, Alo [M,K]      (K-major as is)
 //  2. pb_split_transpose: B [K,N]  -> Bhi, Blo [N,K]      (to K-major)
-//  3. pb_gemm_tc:         one 128x256 output tile per CTA, 256 threads.
+//  3. pb_gemm_tc:         one 128x256 output tile per CTA, 320 threads.
 //     warp 0 lane 0 issues TMA loads (64B swizzle, BK = 16 fp32 = one 64-byte
 //     swizzle row) into a 4-stage ring of {Ahi, Alo, Bhi, Blo} tiles (48 KB
 //     per stage, 192 KB in all: three stages are in flight while the MMAs
 //     read the fourth, about 1.8 us of tensor work, enough to cover TMA
-//     latency from L2 or HBM); warp 1
+//     latency from L2 or HBM); warp 9
 //     allocates 512 TMEM columns and its lane 0 issues tcgen05.mma
-//     (kind::tf32, M=128, N=256, K=8; 3 products x 2 k-steps per stage):
-//     Ahi*Bhi accumulates in columns 0..255 and the small Ahi*Blo + Alo*Bhi
-//     terms in columns 256..511, so the large accumulator is rounded once per
-//     k-step instead of three times; the epilogue adds the two,
-//     committing each stage back to the producer and the last one to the
-//     epilogue barrier; then all eight warps read the accumulators with
-//     tcgen05.ld (warp w owns TMEM lanes 32(w%4)..+31 = tile rows, and
-//     column half w/4), apply the fused epilogue and store.
+//     (kind::tf32, M=128, N=256, K=8; 3 products x 2 k-steps per stage),
+//     committing each stage back to the producer.
+//     Accumulation: the tensor core's fp32 accumulator loses low-order bits
+//     on every MMA it adds into, so one accumulator over all of K (1024
+//     k-steps at K = 8192) drifts ~6e-5 relative -- five times an fp32 FMA
+//     chain. Here the MMAs of each period of 4 k-blocks (64 of K) start from
+//     zero in one of two 256-column TMEM buffers (p % 2), and eight warps
+//     that are otherwise idle until the epilogue drain the finished period
+//     with tcgen05.ld into per-thread fp32 sums (round to nearest) while the
+//     MMAs fill the other buffer; the MMA thread reuses a buffer only after
+//     its drain has arrived on that buffer's barrier. Warp w drains TMEM
+//     lanes 32(w%4)..+31 (its tile rows) and column half w/4, then applies
+//     the fused epilogue to its sums and stores.
 // Every mbarrier wait is bounded (clock64 budget); on expiry the kernel
 // records a code in the device error word, stops issuing, waits (bounded)
 // for its own copies and MMAs in flight, frees its TMEM and returns.
 // No TMA multicast is used anywhere.
 #include "lower.hpp"
 
+#include <cmath>
 #include <cstdlib>
 #include <sstream>
 
@@ -63,6 +69,10 @@ static __device__ __forceinline__ pb_u32 pb_smem(const void* p) {
 
 static __device__ __forceinline__ void pb_mbar_init(pb_u32 bar, pb_u32 count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(bar), "r"(count) : "memory");
+}
+
+static __device__ __forceinline__ void pb_mbar_arrive(pb_u32 bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(bar) : "memory");
 }
 
 static __device__ __forceinline__ void pb_mbar_expect_tx(pb_u32 bar, pb_u32 bytes) {
@@ -247,17 +257,35 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
         const int64_t tiles_m = M / kBM, tiles_n = N / kBN;
         const int64_t num_kb = K / kBK;
         const int group_m = 16;
+        // Accumulation period in k-blocks. The drift of a tensor-core
+        // accumulator grows with the number of MMAs added into one period
+        // (6 per k-block: 3 products x 2 k-steps), independent of K, while
+        // an fp32 FMA chain's error grows as sqrt(K); a period of at most
+        // sqrt(K) / 2 k-blocks keeps ours about half the chain's at every K
+        // (measured: one accumulator over 8192 of K drifts 5x the chain, a
+        // period over all of K = 512 almost 5x). Capped at 32 (draining
+        // costs a few percent per launch at 8), a power of two dividing
+        // K / 16, at least 4 (K % 64 == 0).
+        int period = 4;
+        while (period < 32 && num_kb % (period * 2) == 0 &&
+               static_cast<double>(period * 2) <= std::sqrt(static_cast<double>(K)) / 2.0)
+            period *= 2;
         std::ostringstream src;
-        src << kernel_prelude() << gemm_device_source() << efn;
+        src << kernel_prelude() << "#define PB_PERIOD " << period << "\n" << gemm_device_source() << efn;
         std::ostringstream body;
+        // Roles (320 threads): warps 0-7 drain the accumulator periods and
+        // run the epilogue (warp w: TMEM lane quadrant w % 4 = tile rows
+        // 32(w%4).., column half w / 4), warp 8 lane 0 issues TMA, warp 9
+        // allocates TMEM and its lane 0 issues the MMAs.
         body << "    extern __shared__ float4 pb_dyn_smem[];\n"
-             << "    __shared__ __align__(8) unsigned long long full_bar[PB_STAGES], empty_bar[PB_STAGES], acc_bar;\n"
+             << "    __shared__ __align__(8) unsigned long long full_bar[PB_STAGES], empty_bar[PB_STAGES];\n"
+             << "    __shared__ __align__(8) unsigned long long accf[2], acce[2], done_bar;\n"
              << "    __shared__ pb_u32 tmem_slot;\n"
              << "    __shared__ int abort_flag;\n"
              << "    __shared__ int issued, consumed;\n"
              << "    const pb_u32 warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;\n"
              << "    const pb_u32 base = (pb_smem(pb_dyn_smem) + 1023u) & ~1023u;\n"
-             // Tile order: groups of " << group_m << " M-tiles sweep N (L2 reuse of A and B).
+             // Tile order: groups of group_m M-tiles sweep N (L2 reuse of A and B).
              << "    const pb_u32 tiles_m = " << tiles_m << "u, tiles_n = " << tiles_n << "u;\n"
              << "    const pb_u32 per_group = " << group_m << "u * tiles_n;\n"
              << "    const pb_u32 g = blockIdx.x / per_group, first_m = g * " << group_m << "u;\n"
@@ -270,10 +298,11 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
              << "        issued = 0;\n"
              << "        consumed = 0;\n"
              << "        for (int s = 0; s < PB_STAGES; ++s) { pb_mbar_init(pb_smem(&full_bar[s]), 1); pb_mbar_init(pb_smem(&empty_bar[s]), 1); }\n"
-             << "        pb_mbar_init(pb_smem(&acc_bar), 1);\n"
+             << "        for (int b = 0; b < 2; ++b) { pb_mbar_init(pb_smem(&accf[b]), 1); pb_mbar_init(pb_smem(&acce[b]), 8); }\n"
+             << "        pb_mbar_init(pb_smem(&done_bar), 1);\n"
              << "        asm volatile(\"fence.mbarrier_init.release.cluster;\" ::: \"memory\");\n"
              << "    }\n"
-             << "    if (warp == 1) {\n"
+             << "    if (warp == 9) {\n"
              << "        asm volatile(\"tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;\" :: \"r\"(pb_smem(&tmem_slot)) : \"memory\");\n"
              << "        asm volatile(\"tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\" ::: \"memory\");\n"
              << "    }\n"
@@ -282,57 +311,91 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
              << "    asm volatile(\"tcgen05.fence::after_thread_sync;\" ::: \"memory\");\n"
              << "    const pb_u32 tmem = tmem_slot;\n"
              << "    const int num_kb = " << num_kb << ";\n"
-             << "    if (warp == 0 && lane == 0) {\n"
+             << "    const int periods = num_kb / PB_PERIOD;\n"
+             << "    if (warp == 8) {\n"
+             << "        if (lane == 0) {\n"
              // producer
-             << "        for (int kb = 0; kb < num_kb; ++kb) {\n"
-             << "            const int s = kb % PB_STAGES;\n"
-             << "            const pb_u32 phase = (pb_u32)(kb / PB_STAGES) & 1u;\n"
-             << "            if (!pb_wait(pb_smem(&empty_bar[s]), phase ^ 1u, &abort_flag, err, 1)) break;\n"
-             << "            const pb_u32 st = base + (pb_u32)s * PB_STAGE_BYTES;\n"
-             << "            const pb_u32 fb = pb_smem(&full_bar[s]);\n"
-             << "            pb_mbar_expect_tx(fb, PB_STAGE_BYTES);\n"
-             << "            pb_tma_load(st, &tm_ahi, fb, kb * PB_BK, m0);\n"
-             << "            pb_tma_load(st + PB_TILE_A_BYTES, &tm_alo, fb, kb * PB_BK, m0);\n"
-             << "            pb_tma_load(st + 2 * PB_TILE_A_BYTES, &tm_bhi, fb, kb * PB_BK, n0);\n"
-             << "            pb_tma_load(st + 2 * PB_TILE_A_BYTES + PB_TILE_B_BYTES, &tm_blo, fb, kb * PB_BK, n0);\n"
-             << "            issued = kb + 1;\n"
-             << "        }\n"
-             << "    } else if (warp == 1 && lane == 0) {\n"
-             // MMA issuer
-             << "        for (int kb = 0; kb < num_kb; ++kb) {\n"
-             << "            const int s = kb % PB_STAGES;\n"
-             << "            const pb_u32 phase = (pb_u32)(kb / PB_STAGES) & 1u;\n"
-             << "            if (!pb_wait(pb_smem(&full_bar[s]), phase, &abort_flag, err, 2)) break;\n"
-             << "            consumed = kb + 1;\n"
-             << "            asm volatile(\"tcgen05.fence::after_thread_sync;\" ::: \"memory\");\n"
-             << "            const pb_u32 st = base + (pb_u32)s * PB_STAGE_BYTES;\n"
-             << "            #pragma unroll\n"
-             << "            for (int kk = 0; kk < PB_BK / 8; ++kk) {\n"
-             << "                const pb_u64 ahi = pb_desc(st + kk * 32);\n"
-             << "                const pb_u64 alo = pb_desc(st + PB_TILE_A_BYTES + kk * 32);\n"
-             << "                const pb_u64 bhi = pb_desc(st + 2 * PB_TILE_A_BYTES + kk * 32);\n"
-             << "                const pb_u64 blo = pb_desc(st + 2 * PB_TILE_A_BYTES + PB_TILE_B_BYTES + kk * 32);\n"
-             << "                pb_mma(tmem, ahi, bhi, (kb | kk) != 0);\n"
-             << "                pb_mma(tmem + PB_BN, ahi, blo, (kb | kk) != 0);\n"
-             << "                pb_mma(tmem + PB_BN, alo, bhi, 1u);\n"
+             << "            for (int kb = 0; kb < num_kb; ++kb) {\n"
+             << "                const int s = kb % PB_STAGES;\n"
+             << "                const pb_u32 phase = (pb_u32)(kb / PB_STAGES) & 1u;\n"
+             << "                if (!pb_wait(pb_smem(&empty_bar[s]), phase ^ 1u, &abort_flag, err, 1)) break;\n"
+             << "                const pb_u32 st = base + (pb_u32)s * PB_STAGE_BYTES;\n"
+             << "                const pb_u32 fb = pb_smem(&full_bar[s]);\n"
+             << "                pb_mbar_expect_tx(fb, PB_STAGE_BYTES);\n"
+             << "                pb_tma_load(st, &tm_ahi, fb, kb * PB_BK, m0);\n"
+             << "                pb_tma_load(st + PB_TILE_A_BYTES, &tm_alo, fb, kb * PB_BK, m0);\n"
+             << "                pb_tma_load(st + 2 * PB_TILE_A_BYTES, &tm_bhi, fb, kb * PB_BK, n0);\n"
+             << "                pb_tma_load(st + 2 * PB_TILE_A_BYTES + PB_TILE_B_BYTES, &tm_blo, fb, kb * PB_BK, n0);\n"
+             << "                issued = kb + 1;\n"
              << "            }\n"
-             << "            pb_commit(pb_smem(&empty_bar[s]));\n"
              << "        }\n"
-             // Whether or not the loop finished, tell the epilogue once every
-             // MMA issued so far has completed.
-             << "        pb_commit(pb_smem(&acc_bar));\n"
-             << "    }\n"
-             << "    __syncwarp();\n"
-             // epilogue: all eight warps. Warp w reads TMEM lanes
-             // 32*(w%4).. (its tile rows; tcgen05.ld lets warps w and w+4
-             // share a lane quadrant) and columns half w/4 of the tile.
-             << "    const bool acc_ok = __all_sync(0xffffffffu, pb_wait(pb_smem(&acc_bar), 0u, &abort_flag, err, 3) && !abort_flag);\n"
-             << "    asm volatile(\"tcgen05.fence::after_thread_sync;\" ::: \"memory\");\n"
-             << "    if (acc_ok) {\n"
+             << "        __syncwarp();\n"
+             << "    } else if (warp == 9) {\n"
+             << "        if (lane == 0) {\n"
+             // MMA issuer: period p (PB_PERIOD k-blocks) accumulates from zero
+             // into TMEM buffer p % 2 (columns 256 (p % 2)..+255); before
+             // reusing a buffer it waits for the drain of period p - 2.
+             << "            for (int kb = 0; kb < num_kb; ++kb) {\n"
+             << "                const int s = kb % PB_STAGES;\n"
+             << "                const pb_u32 phase = (pb_u32)(kb / PB_STAGES) & 1u;\n"
+             << "                const int per = kb / PB_PERIOD, pos = kb % PB_PERIOD;\n"
+             << "                const pb_u32 buf = (pb_u32)per & 1u;\n"
+             << "                if (pos == 0 && per >= 2) {\n"
+             << "                    if (!pb_wait(pb_smem(&acce[buf]), (pb_u32)((per >> 1) - 1) & 1u, &abort_flag, err, 6)) break;\n"
+             << "                    asm volatile(\"tcgen05.fence::after_thread_sync;\" ::: \"memory\");\n"
+             << "                }\n"
+             << "                if (!pb_wait(pb_smem(&full_bar[s]), phase, &abort_flag, err, 2)) break;\n"
+             << "                consumed = kb + 1;\n"
+             << "                asm volatile(\"tcgen05.fence::after_thread_sync;\" ::: \"memory\");\n"
+             << "                const pb_u32 st = base + (pb_u32)s * PB_STAGE_BYTES;\n"
+             << "                const pb_u32 d = tmem + buf * (pb_u32)PB_BN;\n"
+             << "                #pragma unroll\n"
+             << "                for (int kk = 0; kk < PB_BK / 8; ++kk) {\n"
+             << "                    const pb_u64 ahi = pb_desc(st + kk * 32);\n"
+             << "                    const pb_u64 alo = pb_desc(st + PB_TILE_A_BYTES + kk * 32);\n"
+             << "                    const pb_u64 bhi = pb_desc(st + 2 * PB_TILE_A_BYTES + kk * 32);\n"
+             << "                    const pb_u64 blo = pb_desc(st + 2 * PB_TILE_A_BYTES + PB_TILE_B_BYTES + kk * 32);\n"
+             << "                    pb_mma(d, ahi, bhi, (pos | kk) != 0);\n"
+             << "                    pb_mma(d, ahi, blo, 1u);\n"
+             << "                    pb_mma(d, alo, bhi, 1u);\n"
+             << "                }\n"
+             << "                pb_commit(pb_smem(&empty_bar[s]));\n"
+             << "                if (pos == PB_PERIOD - 1) pb_commit(pb_smem(&accf[buf]));\n"
+             << "            }\n"
+             // Whether or not the loop finished: completes once every MMA
+             // issued so far has (the teardown waits for it after an abort).
+             << "            pb_commit(pb_smem(&done_bar));\n"
+             << "        }\n"
+             << "        __syncwarp();\n"
+             << "    } else {\n"
+             // drain + epilogue warps
              << "        const pb_u32 quad = warp & 3u, half = warp >> 2;\n"
-             << "        const int r = m0 + (int)(quad * 32u + lane);\n"
-             << "        const pb_u64 rr = (pb_u64)r;\n"
-             << "        (void)rr;\n";
+             << "        float acc[PB_BN / 2];\n"
+             << "        #pragma unroll\n"
+             << "        for (int j = 0; j < PB_BN / 2; ++j) acc[j] = 0.0f;\n"
+             << "        bool ok = true;\n"
+             << "        for (int per = 0; per < periods; ++per) {\n"
+             << "            const pb_u32 buf = (pb_u32)per & 1u;\n"
+             << "            ok = __all_sync(0xffffffffu, pb_wait(pb_smem(&accf[buf]), (pb_u32)(per >> 1) & 1u, &abort_flag, err, 3) && !abort_flag);\n"
+             << "            if (!ok) break;\n"
+             << "            asm volatile(\"tcgen05.fence::after_thread_sync;\" ::: \"memory\");\n"
+             << "            const pb_u32 taddr = tmem + ((quad * 32u) << 16) + buf * (pb_u32)PB_BN + half * (pb_u32)(PB_BN / 2);\n"
+             << "            #pragma unroll\n"
+             << "            for (int c = 0; c < PB_BN / 64; ++c) {\n"
+             << "                pb_u32 v[32];\n"
+             << "                PB_TMEM_LD32(taddr + (pb_u32)(c * 32), v);\n"
+             << "                asm volatile(\"tcgen05.wait::ld.sync.aligned;\" ::: \"memory\");\n"
+             << "                #pragma unroll\n"
+             << "                for (int j = 0; j < 32; ++j) acc[c * 32 + j] = acc[c * 32 + j] + __uint_as_float(v[j]);\n"
+             << "            }\n"
+             << "            asm volatile(\"tcgen05.fence::before_thread_sync;\" ::: \"memory\");\n"
+             << "            __syncwarp();\n"
+             << "            if (lane == 0) pb_mbar_arrive(pb_smem(&acce[buf]));\n"
+             << "        }\n"
+             << "        if (ok) {\n"
+             << "            const int r = m0 + (int)(quad * 32u + lane);\n"
+             << "            const pb_u64 rr = (pb_u64)r;\n"
+             << "            (void)rr;\n";
         // Leaf loads by column stride: 1 and 16-byte aligned -> float4 per
         // 4 columns; 0 -> one load per row, hoisted out of the column loops;
         // otherwise one scalar per element.
@@ -343,7 +406,7 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
             if (sc == 0) {
                 leaf_mode[li] = 0;
                 std::vector<std::string> cv = {"rr", "0"};
-                body << "        const float h" << li << " = pb_ld(in" << v.buffer << " + "
+                body << "            const float h" << li << " = pb_ld(in" << v.buffer << " + "
                      << address(v.map, cv, true, 1) << ");\n";
             } else if (sc == 1 && v.map.off % 4 == 0 && sr % 4 == 0) {
                 leaf_mode[li] = 1;
@@ -351,79 +414,80 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
                 leaf_mode[li] = 2;
             }
         }
-        body << "        for (int c = (int)half * (PB_BN / 64); c < ((int)half + 1) * (PB_BN / 64); ++c) {\n"
-             << "            pb_u32 v[32], w[32];\n"
-             << "            PB_TMEM_LD32(tmem + ((quad * 32u) << 16) + (pb_u32)(c * 32), v);\n"
-             << "            PB_TMEM_LD32(tmem + ((quad * 32u) << 16) + (pb_u32)(PB_BN + c * 32), w);\n"
-             << "            asm volatile(\"tcgen05.wait::ld.sync.aligned;\" ::: \"memory\");\n"
-             << "            const int cbase = n0 + c * 32;\n"
-             << "            float* orow = out + rr * " << N << "ull + cbase;\n"
-             << "            #pragma unroll\n"
-             << "            for (int j = 0; j < 32; j += 4) {\n"
-             << "                const pb_u64 cc = (pb_u64)(cbase + j);\n"
-             << "                (void)cc;\n";
+        body << "            #pragma unroll\n"
+             << "            for (int c = 0; c < PB_BN / 64; ++c) {\n"
+             << "                const int cbase = n0 + (int)half * (PB_BN / 2) + c * 32;\n"
+             << "                float* orow = out + rr * " << N << "ull + cbase;\n"
+             << "                #pragma unroll\n"
+             << "                for (int j = 0; j < 32; j += 4) {\n"
+             << "                    const pb_u64 cc = (pb_u64)(cbase + j);\n"
+             << "                    (void)cc;\n";
         std::vector<std::string> cvar = {"rr", "cc"};
         for (size_t li = 0; li < order.size(); ++li) {
             if (leaf_mode[li] != 1) continue;
             const vnode& v = b.nodes[static_cast<size_t>(order[li])];
-            body << "                const float4 q" << li << " = pb_ld4(in" << v.buffer << " + "
+            body << "                    const float4 q" << li << " = pb_ld4(in" << v.buffer << " + "
                  << address(v.map, cvar, true, -1) << ");\n";
         }
-        body << "                float y[4];\n"
-             << "                #pragma unroll\n"
-             << "                for (int e = 0; e < 4; ++e) {\n"
-             << "                    const pb_u64 ce = cc + (pb_u64)e;\n"
-             << "                    (void)ce;\n";
+        body << "                    float y[4];\n"
+             << "                    #pragma unroll\n"
+             << "                    for (int e = 0; e < 4; ++e) {\n"
+             << "                        const pb_u64 ce = cc + (pb_u64)e;\n"
+             << "                        (void)ce;\n";
         std::vector<std::string> evar = {"rr", "ce"};
         for (size_t li = 0; li < order.size(); ++li) {
             const vnode& v = b.nodes[static_cast<size_t>(order[li])];
             if (leaf_mode[li] == 0)
-                body << "                    const float x" << li << " = h" << li << ";\n";
+                body << "                        const float x" << li << " = h" << li << ";\n";
             else if (leaf_mode[li] == 1)
-                body << "                    const float x" << li << " = e == 0 ? q" << li << ".x : e == 1 ? q" << li
+                body << "                        const float x" << li << " = e == 0 ? q" << li << ".x : e == 1 ? q" << li
                      << ".y : e == 2 ? q" << li << ".z : q" << li << ".w;\n";
             else
-                body << "                    const float x" << li << " = pb_ld(in" << v.buffer << " + "
+                body << "                        const float x" << li << " = pb_ld(in" << v.buffer << " + "
                      << address(v.map, evar, true, -1) << ");\n";
         }
-        body << "                    y[e] = pb_e0(__uint_as_float(v[j + e]) + __uint_as_float(w[j + e])";
+        body << "                        y[e] = pb_e0(acc[c * 32 + j + e]";
         for (size_t li = 0; li < order.size(); ++li) body << ", x" << li;
         body << ");\n"
+             << "                    }\n"
+             << "                    pb_st4(orow + j, make_float4(y[0], y[1], y[2], y[3]));\n"
              << "                }\n"
-             << "                pb_st4(orow + j, make_float4(y[0], y[1], y[2], y[3]));\n"
              << "            }\n"
              << "        }\n"
              << "    }\n"
-             // Teardown after an abort: wait (bounded, ignoring the abort
-             // flag) for the MMAs issued so far and for every TMA copy issued
-             // but not consumed, so nothing writes freed TMEM or shared memory.
+             // Teardown: wait (bounded, ignoring the abort flag) for the
+             // commit that follows every MMA issued -- so no MMA or commit
+             // arrival lands after the CTA leaves -- and, after an abort, for
+             // every TMA copy issued but not consumed, so nothing writes
+             // freed TMEM or shared memory.
              << "    __syncthreads();\n"
-             << "    if (abort_flag && threadIdx.x == 0) {\n"
+             << "    if (threadIdx.x == 0) {\n"
              << "        int dummy = 0;\n"
              << "        volatile int never = 0;\n"
-             << "        (void)pb_wait(pb_smem(&acc_bar), 0u, &never, &dummy, 4);\n"
-             << "        for (int kb = consumed; kb < issued; ++kb) {\n"
-             << "            (void)pb_wait(pb_smem(&full_bar[kb % PB_STAGES]), (pb_u32)(kb / PB_STAGES) & 1u, &never, &dummy, 5);\n"
-             << "        }\n"
+             << "        (void)pb_wait(pb_smem(&done_bar), 0u, &never, &dummy, 4);\n"
+             << "        if (abort_flag)\n"
+             << "            for (int kb = consumed; kb < issued; ++kb)\n"
+             << "                (void)pb_wait(pb_smem(&full_bar[kb % PB_STAGES]), (pb_u32)(kb / PB_STAGES) & 1u, &never, &dummy, 5);\n"
              << "    }\n"
              << "    asm volatile(\"tcgen05.fence::before_thread_sync;\" ::: \"memory\");\n"
              << "    __syncthreads();\n"
-             << "    if (warp == 1) {\n"
+             << "    if (warp == 9) {\n"
              << "        asm volatile(\"tcgen05.fence::after_thread_sync;\" ::: \"memory\");\n"
              << "        asm volatile(\"tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;\" :: \"r\"(tmem) : \"memory\");\n"
              << "    }\n";
         launch_spec l;
         l.name = "pb_gemm_tc_" + hex8(src.str() + body.str());
-        src << "extern \"C\" __global__ void __launch_bounds__(256, 1) " << l.name
+        src << "extern \"C\" __global__ void __launch_bounds__(320, 1) " << l.name
             << "(const __grid_constant__ pb_tmap tm_ahi, const __grid_constant__ pb_tmap tm_alo, "
                "const __grid_constant__ pb_tmap tm_bhi, const __grid_constant__ pb_tmap tm_blo, ";
         for (size_t i = 0; i < k.leaves.size(); ++i) src << "const float* __restrict__ in" << i << ", ";
         src << "float* __restrict__ out, int* __restrict__ err) {\n" << body.str() << "}\n";
         l.source = src.str();
         l.schedule = "gemm tcgen05 3xTF32 128x256x16, 4-stage TMA ring (64B swizzle, no multicast), "
-                     "TMEM accumulator, fused epilogue, grouped tile order";
+                     "two TMEM accumulators drained every 64 of K into fp32 registers, fused epilogue, "
+                     "grouped tile order";
         l.grid = {static_cast<uint32_t>(tiles_m * tiles_n), 1, 1};
-        l.block = {256, 1, 1};
+        l.block = {320, 1, 1};
         l.smem = kStages * (2 * kBM * kBK * 4 + 2 * kBN * kBK * 4) + 1024;
         auto tmap_arg = [&](int temp, int64_t rows, int box_rows) {
             kernel_arg a;
