@@ -355,7 +355,8 @@ namespace porch::detail {
         int nmaps = 0;
         for (launch_spec& l : p->launches) {
             pbrt_function fn = nullptr;
-            if (device < static_cast<int>(l.functions.size())) fn = l.functions[device];
+            const bool slot = device < static_cast<int>(l.per_device->function.size());
+            if (slot) fn = l.per_device->function[device].load(std::memory_order_acquire);
             if (fn == nullptr) {
                 std::scoped_lock lock{p->resolve_mutex};
                 check(pbrt_get_function(device, l.image_key, l.name.c_str(), &fn));
@@ -370,9 +371,9 @@ namespace porch::detail {
                     const int64_t fit = std::max<int64_t>(1, int64_t{per_sm} * sms);
                     pgrid = static_cast<uint32_t>(std::min<int64_t>(l.persistent_units, fit));
                 }
-                if (device < static_cast<int>(l.functions.size())) {
-                    l.persistent_grid[device] = pgrid;
-                    l.functions[device] = fn;
+                if (slot) {
+                    l.per_device->persistent_grid[device].store(pgrid, std::memory_order_relaxed);
+                    l.per_device->function[device].store(fn, std::memory_order_release);
                 }
             }
             if (l.args.size() > 64) throw std::runtime_error("kernel has too many arguments");
@@ -417,9 +418,10 @@ namespace porch::detail {
                 params[i] = &values[i];
             }
             std::array<uint32_t, 3> grid = l.grid;
-            if (l.persistent_units > 0 && device < static_cast<int>(l.persistent_grid.size()) &&
-                l.persistent_grid[device] != 0)
-                grid[0] = l.persistent_grid[device];
+            if (l.persistent_units > 0 && slot) {
+                const uint32_t pg = l.per_device->persistent_grid[device].load(std::memory_order_relaxed);
+                if (pg != 0) grid[0] = pg;
+            }
             check(pbrt_launch(device, fn, grid.data(), l.block.data(), l.smem,
                               stream->stream, params, nullptr));
         }

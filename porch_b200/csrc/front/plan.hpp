@@ -10,6 +10,7 @@
 #include "detail.hpp"
 
 #include <array>
+#include <atomic>
 #include <map>
 #include <string>
 #include <vector>
@@ -77,10 +78,14 @@ namespace porch::detail {
         // exactly the CTAs that fit at once (SMs x occupancy), so no CTA waits
         // for a second wave. 0 = launch `grid` as given.
         int64_t persistent_units = 0;
-        std::array<uint32_t, 16> persistent_grid{};
-        // Resolved function handle per device (filled on first launch).
-        std::array<pbrt_function, 16> functions{};
-        std::mutex* resolve_mutex = nullptr;
+        // Per device, filled on first launch under the plan's resolve mutex
+        // and read without it by every later launch (from any thread): the
+        // function is published with release order after the grid.
+        struct resolved {
+            std::array<std::atomic<pbrt_function>, 16> function{};
+            std::array<std::atomic<uint32_t>, 16> persistent_grid{};
+        };
+        std::shared_ptr<resolved> per_device = std::make_shared<resolved>();
     };
 
     struct plan {

@@ -1,0 +1,76 @@
+"""Several host threads on one device (the reference's threading contract:
+handles copy across threads, a shared lazy tensor materialises once,
+streams are per thread -- include/porch/tensor.hpp, src/tensor.cpp:1070-1079,
+src/cuda_jit.cpp:524-528).
+
+Each thread builds and realises graphs of every kernel family on its own
+stream, some shared across threads, first-use plan resolution included;
+every result must equal the single-threaded one bit for bit.
+"""
+
+import threading
+
+import numpy as np
+import pytest
+
+
+def _graphs(api, t):
+    x, y, w = t["x"], t["y"], t["w"]
+    return {
+        "elementwise": (x + y) * 2.0 - 1.0,
+        "view": api.concat(api.transpose(x[0::2, 0:64]) + 1.0, y[0:64, 0:256], 0),
+        "softmax": api.softmax(x, 1),
+        "reduce0": api.sum(x, 0),
+        "reduce1": api.max(y, 1),
+        "matmul": api.relu(api.matmul(x, w)),
+    }
+
+
+@pytest.mark.gpu
+def test_threads_realise_the_same_values(gpu):
+    api = gpu
+    rng = np.random.default_rng(17)
+    hx = rng.normal(0, 1, (512, 256)).astype(np.float32)
+    hy = rng.normal(0, 1, (512, 256)).astype(np.float32)
+    hw = rng.uniform(-1, 1, (256, 1024)).astype(np.float32) / 16
+    shared = {"x": api.tensor([512, 256], hx), "y": api.tensor([512, 256], hy),
+              "w": api.tensor([256, 1024], hw)}
+    # A lazy tensor shared by every thread: realised exactly once.
+    lazy = api.as_tensor(api.exp(shared["x"]) * 0.5)
+
+    # The threads are the first to realise these graphs, so plan building,
+    # compilation and per-device function resolution race as well.
+    results = {}
+    errors = []
+    start = threading.Barrier(6)
+
+    def worker(i):
+        try:
+            start.wait()
+            for rep in range(4):
+                # Half the threads reuse the shared inputs, half make their own.
+                if i % 2:
+                    t = shared
+                else:
+                    t = {"x": api.tensor([512, 256], hx), "y": api.tensor([512, 256], hy),
+                         "w": api.tensor([256, 1024], hw)}
+                for k, e in _graphs(api, t).items():
+                    results[(i, rep, k)] = api.materialize(e).cpu()
+                results[(i, rep, "lazy")] = lazy.cpu()
+        except Exception as exc:  # reported below, not lost in the thread
+            errors.append((i, repr(exc)))
+
+    threads = [threading.Thread(target=worker, args=(i,)) for i in range(6)]
+    for th in threads:
+        th.start()
+    for th in threads:
+        th.join(timeout=300)
+    assert not any(th.is_alive() for th in threads)
+    assert not errors, errors[:10]
+
+    want = {k: api.materialize(e).cpu() for k, e in _graphs(api, shared).items()}
+    want["lazy"] = lazy.cpu()
+    bad = [key for key, got in results.items()
+           if not np.array_equal(got.view(np.uint32), want[key[2]].view(np.uint32))]
+    assert len(results) == 6 * 4 * 7
+    assert not bad, bad[:10]
