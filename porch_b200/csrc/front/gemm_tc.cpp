@@ -272,7 +272,23 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
             period *= 2;
         std::ostringstream src;
         src << kernel_prelude() << "#define PB_PERIOD " << period << "\n" << gemm_device_source() << efn;
+        // Tile t -> output origin, tiles ordered in groups of group_m M-tiles
+        // that sweep N (consecutive tiles, run at the same time by the
+        // persistent CTAs, share A and B panels in L2).
+        src << "static __device__ __forceinline__ void pb_tile_origin(pb_u32 t, int& m0, int& n0) {\n"
+            << "    const pb_u32 tiles_m = " << tiles_m << "u, tiles_n = " << tiles_n << "u;\n"
+            << "    const pb_u32 per_group = " << group_m << "u * tiles_n;\n"
+            << "    const pb_u32 g = t / per_group, first_m = g * " << group_m << "u;\n"
+            << "    const pb_u32 gm = (tiles_m - first_m) < " << group_m << "u ? (tiles_m - first_m) : " << group_m << "u;\n"
+            << "    m0 = (int)((first_m + (t % per_group) % gm) * PB_BM);\n"
+            << "    n0 = (int)(((t % per_group) / gm) * PB_BN);\n"
+            << "}\n";
         std::ostringstream body;
+        // Persistent CTAs (one per SM) loop over tiles t = blockIdx.x,
+        // + gridDim.x, ...; the k-block counter g and the period counter run
+        // on across tiles, so the producer fetches the next tile's stages
+        // and the MMAs start its first period while the eight drain warps
+        // still run the previous tile's epilogue from their registers.
         // Roles (320 threads): warps 0-7 drain the accumulator periods and
         // run the epilogue (warp w: TMEM lane quadrant w % 4 = tile rows
         // 32(w%4).., column half w / 4), warp 8 lane 0 issues TMA, warp 9
@@ -285,14 +301,7 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
              << "    __shared__ int issued, consumed;\n"
              << "    const pb_u32 warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;\n"
              << "    const pb_u32 base = (pb_smem(pb_dyn_smem) + 1023u) & ~1023u;\n"
-             // Tile order: groups of group_m M-tiles sweep N (L2 reuse of A and B).
-             << "    const pb_u32 tiles_m = " << tiles_m << "u, tiles_n = " << tiles_n << "u;\n"
-             << "    const pb_u32 per_group = " << group_m << "u * tiles_n;\n"
-             << "    const pb_u32 g = blockIdx.x / per_group, first_m = g * " << group_m << "u;\n"
-             << "    const pb_u32 gm = (tiles_m - first_m) < " << group_m << "u ? (tiles_m - first_m) : " << group_m << "u;\n"
-             << "    const pb_u32 tm = first_m + (blockIdx.x % per_group) % gm;\n"
-             << "    const pb_u32 tn = (blockIdx.x % per_group) / gm;\n"
-             << "    const int m0 = (int)(tm * PB_BM), n0 = (int)(tn * PB_BN);\n"
+             << "    const pb_u32 tiles = " << tiles_m * tiles_n << "u;\n"
              << "    if (threadIdx.x == 0) {\n"
              << "        abort_flag = 0;\n"
              << "        issued = 0;\n"
@@ -315,84 +324,99 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
              << "    if (warp == 8) {\n"
              << "        if (lane == 0) {\n"
              // producer
-             << "            for (int kb = 0; kb < num_kb; ++kb) {\n"
-             << "                const int s = kb % PB_STAGES;\n"
-             << "                const pb_u32 phase = (pb_u32)(kb / PB_STAGES) & 1u;\n"
-             << "                if (!pb_wait(pb_smem(&empty_bar[s]), phase ^ 1u, &abort_flag, err, 1)) break;\n"
-             << "                const pb_u32 st = base + (pb_u32)s * PB_STAGE_BYTES;\n"
-             << "                const pb_u32 fb = pb_smem(&full_bar[s]);\n"
-             << "                pb_mbar_expect_tx(fb, PB_STAGE_BYTES);\n"
-             << "                pb_tma_load(st, &tm_ahi, fb, kb * PB_BK, m0);\n"
-             << "                pb_tma_load(st + PB_TILE_A_BYTES, &tm_alo, fb, kb * PB_BK, m0);\n"
-             << "                pb_tma_load(st + 2 * PB_TILE_A_BYTES, &tm_bhi, fb, kb * PB_BK, n0);\n"
-             << "                pb_tma_load(st + 2 * PB_TILE_A_BYTES + PB_TILE_B_BYTES, &tm_blo, fb, kb * PB_BK, n0);\n"
-             << "                issued = kb + 1;\n"
+             << "            int g = 0;\n"
+             << "            bool stop = false;\n"
+             << "            for (pb_u32 t = blockIdx.x; t < tiles && !stop; t += gridDim.x) {\n"
+             << "                int m0, n0;\n"
+             << "                pb_tile_origin(t, m0, n0);\n"
+             << "                for (int kb = 0; kb < num_kb; ++kb, ++g) {\n"
+             << "                    const int s = g % PB_STAGES;\n"
+             << "                    const pb_u32 phase = (pb_u32)(g / PB_STAGES) & 1u;\n"
+             << "                    if (!pb_wait(pb_smem(&empty_bar[s]), phase ^ 1u, &abort_flag, err, 1)) { stop = true; break; }\n"
+             << "                    const pb_u32 st = base + (pb_u32)s * PB_STAGE_BYTES;\n"
+             << "                    const pb_u32 fb = pb_smem(&full_bar[s]);\n"
+             << "                    pb_mbar_expect_tx(fb, PB_STAGE_BYTES);\n"
+             << "                    pb_tma_load(st, &tm_ahi, fb, kb * PB_BK, m0);\n"
+             << "                    pb_tma_load(st + PB_TILE_A_BYTES, &tm_alo, fb, kb * PB_BK, m0);\n"
+             << "                    pb_tma_load(st + 2 * PB_TILE_A_BYTES, &tm_bhi, fb, kb * PB_BK, n0);\n"
+             << "                    pb_tma_load(st + 2 * PB_TILE_A_BYTES + PB_TILE_B_BYTES, &tm_blo, fb, kb * PB_BK, n0);\n"
+             << "                    issued = g + 1;\n"
+             << "                }\n"
              << "            }\n"
              << "        }\n"
              << "        __syncwarp();\n"
              << "    } else if (warp == 9) {\n"
              << "        if (lane == 0) {\n"
-             // MMA issuer: period p (PB_PERIOD k-blocks) accumulates from zero
-             // into TMEM buffer p % 2 (columns 256 (p % 2)..+255); before
-             // reusing a buffer it waits for the drain of period p - 2.
-             << "            for (int kb = 0; kb < num_kb; ++kb) {\n"
-             << "                const int s = kb % PB_STAGES;\n"
-             << "                const pb_u32 phase = (pb_u32)(kb / PB_STAGES) & 1u;\n"
-             << "                const int per = kb / PB_PERIOD, pos = kb % PB_PERIOD;\n"
-             << "                const pb_u32 buf = (pb_u32)per & 1u;\n"
-             << "                if (pos == 0 && per >= 2) {\n"
-             << "                    if (!pb_wait(pb_smem(&acce[buf]), (pb_u32)((per >> 1) - 1) & 1u, &abort_flag, err, 6)) break;\n"
+             // MMA issuer: period p (PB_PERIOD k-blocks, never straddling a
+             // tile) accumulates from zero into TMEM buffer p % 2 (columns
+             // 256 (p % 2)..+255); before reusing a buffer it waits for the
+             // drain of period p - 2.
+             << "            int g = 0;\n"
+             << "            bool stop = false;\n"
+             << "            for (pb_u32 t = blockIdx.x; t < tiles && !stop; t += gridDim.x) {\n"
+             << "                for (int kb = 0; kb < num_kb; ++kb, ++g) {\n"
+             << "                    const int s = g % PB_STAGES;\n"
+             << "                    const pb_u32 phase = (pb_u32)(g / PB_STAGES) & 1u;\n"
+             << "                    const int per = g / PB_PERIOD, pos = g % PB_PERIOD;\n"
+             << "                    const pb_u32 buf = (pb_u32)per & 1u;\n"
+             << "                    if (pos == 0 && per >= 2) {\n"
+             << "                        if (!pb_wait(pb_smem(&acce[buf]), (pb_u32)((per >> 1) - 1) & 1u, &abort_flag, err, 6)) { stop = true; break; }\n"
+             << "                        asm volatile(\"tcgen05.fence::after_thread_sync;\" ::: \"memory\");\n"
+             << "                    }\n"
+             << "                    if (!pb_wait(pb_smem(&full_bar[s]), phase, &abort_flag, err, 2)) { stop = true; break; }\n"
+             << "                    consumed = g + 1;\n"
              << "                    asm volatile(\"tcgen05.fence::after_thread_sync;\" ::: \"memory\");\n"
+             << "                    const pb_u32 st = base + (pb_u32)s * PB_STAGE_BYTES;\n"
+             << "                    const pb_u32 d = tmem + buf * (pb_u32)PB_BN;\n"
+             << "                    #pragma unroll\n"
+             << "                    for (int kk = 0; kk < PB_BK / 8; ++kk) {\n"
+             << "                        const pb_u64 ahi = pb_desc(st + kk * 32);\n"
+             << "                        const pb_u64 alo = pb_desc(st + PB_TILE_A_BYTES + kk * 32);\n"
+             << "                        const pb_u64 bhi = pb_desc(st + 2 * PB_TILE_A_BYTES + kk * 32);\n"
+             << "                        const pb_u64 blo = pb_desc(st + 2 * PB_TILE_A_BYTES + PB_TILE_B_BYTES + kk * 32);\n"
+             << "                        pb_mma(d, ahi, bhi, (pos | kk) != 0);\n"
+             << "                        pb_mma(d, ahi, blo, 1u);\n"
+             << "                        pb_mma(d, alo, bhi, 1u);\n"
+             << "                    }\n"
+             << "                    pb_commit(pb_smem(&empty_bar[s]));\n"
+             << "                    if (pos == PB_PERIOD - 1) pb_commit(pb_smem(&accf[buf]));\n"
              << "                }\n"
-             << "                if (!pb_wait(pb_smem(&full_bar[s]), phase, &abort_flag, err, 2)) break;\n"
-             << "                consumed = kb + 1;\n"
-             << "                asm volatile(\"tcgen05.fence::after_thread_sync;\" ::: \"memory\");\n"
-             << "                const pb_u32 st = base + (pb_u32)s * PB_STAGE_BYTES;\n"
-             << "                const pb_u32 d = tmem + buf * (pb_u32)PB_BN;\n"
-             << "                #pragma unroll\n"
-             << "                for (int kk = 0; kk < PB_BK / 8; ++kk) {\n"
-             << "                    const pb_u64 ahi = pb_desc(st + kk * 32);\n"
-             << "                    const pb_u64 alo = pb_desc(st + PB_TILE_A_BYTES + kk * 32);\n"
-             << "                    const pb_u64 bhi = pb_desc(st + 2 * PB_TILE_A_BYTES + kk * 32);\n"
-             << "                    const pb_u64 blo = pb_desc(st + 2 * PB_TILE_A_BYTES + PB_TILE_B_BYTES + kk * 32);\n"
-             << "                    pb_mma(d, ahi, bhi, (pos | kk) != 0);\n"
-             << "                    pb_mma(d, ahi, blo, 1u);\n"
-             << "                    pb_mma(d, alo, bhi, 1u);\n"
-             << "                }\n"
-             << "                pb_commit(pb_smem(&empty_bar[s]));\n"
-             << "                if (pos == PB_PERIOD - 1) pb_commit(pb_smem(&accf[buf]));\n"
              << "            }\n"
-             // Whether or not the loop finished: completes once every MMA
-             // issued so far has (the teardown waits for it after an abort).
+             // Whether or not the loops finished: completes once every MMA
+             // issued so far has (the teardown waits for it).
              << "            pb_commit(pb_smem(&done_bar));\n"
              << "        }\n"
              << "        __syncwarp();\n"
              << "    } else {\n"
              // drain + epilogue warps
              << "        const pb_u32 quad = warp & 3u, half = warp >> 2;\n"
-             << "        float acc[PB_BN / 2];\n"
-             << "        #pragma unroll\n"
-             << "        for (int j = 0; j < PB_BN / 2; ++j) acc[j] = 0.0f;\n"
+             << "        int per = 0;\n"
              << "        bool ok = true;\n"
-             << "        for (int per = 0; per < periods; ++per) {\n"
-             << "            const pb_u32 buf = (pb_u32)per & 1u;\n"
-             << "            ok = __all_sync(0xffffffffu, pb_wait(pb_smem(&accf[buf]), (pb_u32)(per >> 1) & 1u, &abort_flag, err, 3) && !abort_flag);\n"
-             << "            if (!ok) break;\n"
-             << "            asm volatile(\"tcgen05.fence::after_thread_sync;\" ::: \"memory\");\n"
-             << "            const pb_u32 taddr = tmem + ((quad * 32u) << 16) + buf * (pb_u32)PB_BN + half * (pb_u32)(PB_BN / 2);\n"
+             << "        for (pb_u32 t = blockIdx.x; t < tiles && ok; t += gridDim.x) {\n"
+             << "            int m0, n0;\n"
+             << "            pb_tile_origin(t, m0, n0);\n"
+             << "            float acc[PB_BN / 2];\n"
              << "            #pragma unroll\n"
-             << "            for (int c = 0; c < PB_BN / 64; ++c) {\n"
-             << "                pb_u32 v[32];\n"
-             << "                PB_TMEM_LD32(taddr + (pb_u32)(c * 32), v);\n"
-             << "                asm volatile(\"tcgen05.wait::ld.sync.aligned;\" ::: \"memory\");\n"
+             << "            for (int j = 0; j < PB_BN / 2; ++j) acc[j] = 0.0f;\n"
+             << "            for (int q = 0; q < periods; ++q, ++per) {\n"
+             << "                const pb_u32 buf = (pb_u32)per & 1u;\n"
+             << "                ok = __all_sync(0xffffffffu, pb_wait(pb_smem(&accf[buf]), (pb_u32)(per >> 1) & 1u, &abort_flag, err, 3) && !abort_flag);\n"
+             << "                if (!ok) break;\n"
+             << "                asm volatile(\"tcgen05.fence::after_thread_sync;\" ::: \"memory\");\n"
+             << "                const pb_u32 taddr = tmem + ((quad * 32u) << 16) + buf * (pb_u32)PB_BN + half * (pb_u32)(PB_BN / 2);\n"
              << "                #pragma unroll\n"
-             << "                for (int j = 0; j < 32; ++j) acc[c * 32 + j] = acc[c * 32 + j] + __uint_as_float(v[j]);\n"
+             << "                for (int c = 0; c < PB_BN / 64; ++c) {\n"
+             << "                    pb_u32 v[32];\n"
+             << "                    PB_TMEM_LD32(taddr + (pb_u32)(c * 32), v);\n"
+             << "                    asm volatile(\"tcgen05.wait::ld.sync.aligned;\" ::: \"memory\");\n"
+             << "                    #pragma unroll\n"
+             << "                    for (int j = 0; j < 32; ++j) acc[c * 32 + j] = acc[c * 32 + j] + __uint_as_float(v[j]);\n"
+             << "                }\n"
+             << "                asm volatile(\"tcgen05.fence::before_thread_sync;\" ::: \"memory\");\n"
+             << "                __syncwarp();\n"
+             << "                if (lane == 0) pb_mbar_arrive(pb_smem(&acce[buf]));\n"
              << "            }\n"
-             << "            asm volatile(\"tcgen05.fence::before_thread_sync;\" ::: \"memory\");\n"
-             << "            __syncwarp();\n"
-             << "            if (lane == 0) pb_mbar_arrive(pb_smem(&acce[buf]));\n"
-             << "        }\n"
-             << "        if (ok) {\n"
+             << "            if (!ok) break;\n"
              << "            const int r = m0 + (int)(quad * 32u + lane);\n"
              << "            const pb_u64 rr = (pb_u64)r;\n"
              << "            (void)rr;\n";
@@ -466,8 +490,8 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
              << "        volatile int never = 0;\n"
              << "        (void)pb_wait(pb_smem(&done_bar), 0u, &never, &dummy, 4);\n"
              << "        if (abort_flag)\n"
-             << "            for (int kb = consumed; kb < issued; ++kb)\n"
-             << "                (void)pb_wait(pb_smem(&full_bar[kb % PB_STAGES]), (pb_u32)(kb / PB_STAGES) & 1u, &never, &dummy, 5);\n"
+             << "            for (int g = consumed; g < issued; ++g)\n"
+             << "                (void)pb_wait(pb_smem(&full_bar[g % PB_STAGES]), (pb_u32)(g / PB_STAGES) & 1u, &never, &dummy, 5);\n"
              << "    }\n"
              << "    asm volatile(\"tcgen05.fence::before_thread_sync;\" ::: \"memory\");\n"
              << "    __syncthreads();\n"
@@ -484,9 +508,23 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
         src << "float* __restrict__ out, int* __restrict__ err) {\n" << body.str() << "}\n";
         l.source = src.str();
         l.schedule = "gemm tcgen05 3xTF32 128x256x16, 4-stage TMA ring (64B swizzle, no multicast), "
-                     "two TMEM accumulators drained every 64 of K into fp32 registers, fused epilogue, "
+                     "two TMEM accumulators drained per period into fp32 registers, fused epilogue, "
                      "grouped tile order";
-        l.grid = {static_cast<uint32_t>(tiles_m * tiles_n), 1, 1};
+        // Persistent CTAs (grid = SMs x resident CTAs = 148) when tiles are
+        // short (K <= 4096): hiding each tile's epilogue behind the next
+        // tile's first period then wins (A/B on one box: config 5's GEMM1,
+        // K = 4096, 6 % fewer cycles). Longer tiles run one per CTA
+        // (grid = tiles), where hardware scheduling keeps the running tiles
+        // closer together in L2 (K = 8192 and 16384: 1-3 % fewer cycles than
+        // persistent). The kernel is the same; its tile loop runs once.
+        const bool persistent = K <= 4096;
+        l.grid = {static_cast<uint32_t>(persistent ? std::min<int64_t>(tiles_m * tiles_n, 148)
+                                                   : tiles_m * tiles_n),
+                  1, 1};
+        if (persistent) {
+            l.persistent_units = tiles_m * tiles_n;
+            l.schedule += ", persistent CTAs (epilogue overlaps the next tile)";
+        }
         l.block = {320, 1, 1};
         l.smem = kStages * (2 * kBM * kBK * 4 + 2 * kBN * kBK * 4) + 1024;
         auto tmap_arg = [&](int temp, int64_t rows, int box_rows) {
