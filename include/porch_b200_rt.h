@@ -153,6 +153,9 @@ int pbrt_error_check(int device, pbrt_stream stream, int* code);
 int pbrt_profile_enable(int enable);
 int pbrt_profile_read(char* buffer, size_t length);
 uint64_t pbrt_launch_count(void);
+/* NVRTC compilations run by this process, and images loaded instead from
+ * the on-disk cache ($PORCH_B200_CACHE_DIR), since start. */
+void pbrt_compile_stats(uint64_t* nvrtc_compiles, uint64_t* disk_cache_hits);
 
 /* ---- fault injection (host side only) --------------------------------- */
 /* spec: comma-separated "<site>:<n>" entries; the n-th subsequent call at that

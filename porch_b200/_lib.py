@@ -103,6 +103,7 @@ def _declare(L: ctypes.CDLL) -> None:
         "pbrt_last_error": (c_char_p, []),
         "pbrt_fault_inject": (c_int, [c_char_p]),
         "pbrt_launch_count": (c_uint64, []),
+        "pbrt_compile_stats": (None, [P(c_uint64), P(c_uint64)]),
         "pbrt_stream_current": (c_int, [c_int, P(c_void_p)]),
         "pbrt_stream_synchronize": (c_int, [c_int, c_void_p]),
         "pbrt_mem_alloc_async": (c_int, [c_int, c_size_t, c_void_p, P(c_uint64)]),

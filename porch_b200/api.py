@@ -486,6 +486,13 @@ def fill_synthetic(out: np.ndarray, seed: int, dist: str, a: float, b: float) ->
     return out
 
 
+def compile_stats() -> dict[str, int]:
+    """NVRTC compilations and on-disk cache hits in this process so far."""
+    n, d = c_uint64(), c_uint64()
+    lib().pbrt_compile_stats(byref(n), byref(d))
+    return {"nvrtc_compiles": n.value, "disk_cache_hits": d.value}
+
+
 def launch_count() -> int:
     return int(lib().pb_launch_count())
 

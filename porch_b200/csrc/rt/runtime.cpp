@@ -21,6 +21,7 @@
 
 #include <cuda.h>
 #include <dlfcn.h>
+#include <unistd.h>
 #include <nccl.h>
 #include <nvrtc.h>
 
@@ -455,6 +456,31 @@ uint64_t finish_hash(uint64_t h) {
 std::string disk_cache_dir() {
     const char* dir = std::getenv("PORCH_B200_CACHE_DIR");
     return dir ? std::string{dir} : std::string{};
+}
+
+std::atomic<uint64_t> g_nvrtc_compiles{0};
+std::atomic<uint64_t> g_disk_hits{0};
+
+// Writes `bytes` to `path` through a private temporary name and a rename,
+// so a reader (another process sharing the cache) sees the whole file or
+// none of it.
+bool write_file_atomically(const std::string& path, const std::string& bytes) {
+    char suffix[48];
+    std::snprintf(suffix, sizeof suffix, ".tmp.%d.%llx", static_cast<int>(getpid()),
+                  static_cast<unsigned long long>(
+                      std::hash<std::thread::id>{}(std::this_thread::get_id())));
+    const std::string tmp = path + suffix;
+    {
+        std::ofstream f(tmp, std::ios::binary | std::ios::trunc);
+        if (!f) return false;
+        f.write(bytes.data(), static_cast<std::streamsize>(bytes.size()));
+        if (!f) return false;
+    }
+    if (std::rename(tmp.c_str(), path.c_str()) != 0) {
+        (void)std::remove(tmp.c_str());
+        return false;
+    }
+    return true;
 }
 
 // ----------------------------------------------------------- profiling --
@@ -932,6 +958,7 @@ int pbrt_compile(const char* source, const char* const* options,
                 img->text = text;
                 img->image.assign((std::istreambuf_iterator<char>(kimg)), {});
                 img->cubin = want_cubin != 0;
+                g_disk_hits.fetch_add(1, std::memory_order_relaxed);
                 std::scoped_lock lock{c.mutex};
                 c.images.emplace(h, std::move(img));
                 *key = h;
@@ -984,11 +1011,13 @@ int pbrt_compile(const char* source, const char* const* options,
             return fail(PBRT_ERR_COMPILE, "nvrtcGetPTX failed");
         if (img->image.empty() || img->image.back() != '\0') img->image.push_back('\0');
     }
+    g_nvrtc_compiles.fetch_add(1, std::memory_order_relaxed);
     if (!dir.empty()) {
-        std::ofstream ktext(dir + "/" + name + ".key", std::ios::binary);
-        ktext << text;
-        std::ofstream kimg(dir + "/" + name + ".img", std::ios::binary);
-        kimg << img->image;
+        // The image first, the key last: a key on disk implies its image.
+        // A failed write only loses the cache entry.
+        const std::string base = dir + "/" + name;
+        if (write_file_atomically(base + ".img", img->image))
+            (void)write_file_atomically(base + ".key", text);
     }
     std::scoped_lock lock{c.mutex};
     c.images.emplace(h, std::move(img));
@@ -1290,6 +1319,11 @@ int pbrt_profile_read(char* buffer, size_t length) {
 }
 
 uint64_t pbrt_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+void pbrt_compile_stats(uint64_t* nvrtc_compiles, uint64_t* disk_cache_hits) {
+    if (nvrtc_compiles) *nvrtc_compiles = g_nvrtc_compiles.load(std::memory_order_relaxed);
+    if (disk_cache_hits) *disk_cache_hits = g_disk_hits.load(std::memory_order_relaxed);
+}
 
 int pbrt_fault_inject(const char* spec) { return parse_fault_spec(spec); }
 
