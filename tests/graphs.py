@@ -95,12 +95,20 @@ def evaluate_oracle(program: str, inputs: Sequence[np.ndarray], threads: int | N
 class _Gen:
     """Random well-formed programs over small shapes."""
 
-    def __init__(self, rng: random.Random, integer_values: bool):
+    def __init__(self, rng: random.Random, integer_values: bool, large: bool = False):
         self.rng = rng
         self.lines: list[str] = []
         self.inputs: list[np.ndarray] = []
         self.integer_values = integer_values
         self.has_inexact = False
+        # Large mode: extents up to thousands (at most LARGE_LIMIT elements
+        # per operand); the default draws are unchanged, seed for seed.
+        self.large = large
+
+    LARGE_LIMIT = 1 << 21
+
+    def _too_big(self, shape) -> bool:
+        return self.large and int(np.prod(shape)) > self.LARGE_LIMIT
 
     def emit(self, text: str) -> int:
         self.lines.append(f"{len(self.lines)} {text}")
@@ -116,6 +124,10 @@ class _Gen:
         return self.emit(f"input {len(self.inputs) - 1}")
 
     def rand_shape(self) -> list[int]:
+        if self.large:
+            r = self.rng.choice([1, 2, 2, 3])
+            ext = {1: [1000, 4096, 65536], 2: [1, 3, 64, 100, 257, 512], 3: [1, 3, 16, 33, 64]}[r]
+            return [self.rng.choice(ext) for _ in range(r)]
         r = self.rng.choice([1, 2, 2, 2, 3])
         return [self.rng.choice([1, 2, 3, 4, 5, 7, 8, 16, 33]) for _ in range(r)]
 
@@ -151,6 +163,8 @@ class _Gen:
             steps = [rng.choice([1, 1, 2, 3]) for _ in shape]
             starts = [rng.randint(0, 2) for _ in shape]
             big = [st + (s - 1) * k + 1 + rng.randint(0, 2) for s, st, k in zip(shape, starts, steps)]
+            if self._too_big(big):
+                return self.new_input(shape)
             a = self.expr(big, depth - 1)
             t = self.emit(f"tensor {a}")
             spec = ";".join(f"s{st}:{st + (s - 1) * k + 1}:{k}" for s, st, k in zip(shape, starts, steps))
@@ -182,7 +196,7 @@ class _Gen:
             # reduction producing `shape`
             ax = rng.randrange(len(shape) + 1)
             keep = rng.random() < 0.5
-            n = rng.choice([1, 3, 8, 33])
+            n = rng.choice([1, 33, 257, 1000] if self.large else [1, 3, 8, 33])
             if keep:
                 if ax >= len(shape) or shape[ax] != 1:
                     return self.new_input(shape)
@@ -193,6 +207,8 @@ class _Gen:
                 if len(shape) == 1 and shape[0] == 1 and rng.random() < 0.5:
                     src = [n]
                     ax = 0
+            if self._too_big(src):
+                return self.new_input(shape)
             a = self.expr(src, depth - 1)
             op = rng.choice(["sum", "max"])
             if op == "sum":
@@ -205,7 +221,7 @@ class _Gen:
                 self.has_inexact = True
             return self.emit(f"{op} {a}")
         if len(shape) == 2:
-            k = rng.choice([1, 3, 8, 17])
+            k = rng.choice([8, 64, 300] if self.large else [1, 3, 8, 17])
             a = self.expr([shape[0], k], depth - 1)
             b = self.expr([k, shape[1]], depth - 1)
             self.has_inexact = True
@@ -213,14 +229,14 @@ class _Gen:
         return self.new_input(shape)
 
 
-def random_program(seed: int, integer_values: bool = True, depth: int = 4):
+def random_program(seed: int, integer_values: bool = True, depth: int = 4, large: bool = False):
     """Returns (program text, inputs, exact). `exact` says the program uses
     only operations whose fp32 result is fixed by IEEE rounding (+ - * /,
     reciprocal, maximum/minimum, max reductions and data movement), so the
     product must match the oracle bit for bit; exp, sum, softmax and matmul
     are compared with a tolerance."""
     rng = random.Random(seed)
-    g = _Gen(rng, integer_values)
+    g = _Gen(rng, integer_values, large)
     shape = g.rand_shape()
     root = g.expr(shape, depth)
     if rng.random() < 0.15 and len(shape) >= 1:

@@ -135,3 +135,42 @@ def test_c5_staged_matches_reference(gpu):
     # the row scale (the matmuls' sqrt(K)-normalised error carries through).
     err = np.abs(ours.astype(np.float64) - ref.astype(np.float64)) / np.abs(ref).max(axis=1, keepdims=True)
     assert float(err.max()) <= 1e-4, float(err.max())
+
+
+LARGE_SEEDS = list(range(7000, 7040))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("seed", LARGE_SEEDS)
+def test_large_random_programs_match_reference(gpu, seed):
+    """Random programs over every node kind at extents up to thousands, with
+    integer-valued inputs: every operation but exp/logistic/softmax is then
+    exact in fp32 whatever the order (sums and matmul products of small
+    integers included), so those programs must equal the reference's output
+    bit for bit; programs with exp must still match within 1e-5 relative
+    where no sum, softmax or matmul sits downstream of it, and within the
+    reduction scale otherwise."""
+    text, ins, _ = graphs.random_program(seed, integer_values=True, depth=4, large=True)
+    ops = {line.split()[1] for line in text.strip().splitlines()}
+    try:
+        ref = _run_reference(text, ins)
+    except AssertionError:
+        # The reference rejects the program (or cannot realise a scalar):
+        # ours must reject it as well.
+        with pytest.raises((ValueError, IndexError, RuntimeError)):
+            graphs.evaluate_product(gpu, text, ins)
+        return
+    got = graphs.evaluate_product(gpu, text, ins)
+    assert list(got.shape) == list(ref.shape)
+    if not ops & {"exp", "logistic", "softmax"}:
+        assert_bitwise(got, ref, f"seed {seed}")
+    elif not ops & {"sum", "softmax", "matmul"}:
+        # The same __expf on both sides, in the same operation order.
+        assert_bitwise(got, ref, f"seed {seed}")
+    else:
+        g64, r64 = got.astype(np.float64), ref.astype(np.float64)
+        fin = np.isfinite(r64)
+        assert np.array_equal(np.isfinite(g64), fin), f"seed {seed}"
+        scale = np.maximum(np.abs(r64), np.sqrt(np.mean(r64[fin] ** 2)) if fin.any() else 1.0)
+        err = np.abs(g64 - r64)[fin] / np.where(scale[fin] == 0, 1.0, scale[fin])
+        assert err.size == 0 or float(err.max()) <= 1e-4, (f"seed {seed}", float(err.max()))
