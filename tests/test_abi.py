@@ -96,6 +96,19 @@ def _plan(api, expr):
     return api.describe(expr)
 
 
+def test_small_m_matmul_splits_k(api):
+    """Fewer output tiles than two waves of SMs: the tcgen05 GEMM splits K
+    and a combine kernel applies the epilogue; big tiles counts do not."""
+    def kernels(m, k, n):
+        a, b, bi = api.placeholder([m, k]), api.placeholder([k, n]), api.placeholder([n])
+        plan = _plan(api, api.relu(api.matmul(a, b) + api.broadcast_to(bi, [m, n])))
+        return [line for line in plan.splitlines() if line.startswith("kernel ")]
+    small = kernels(128, 4096, 4096)
+    assert "split-K x8" in small[-2] and "split-K combine" in small[-1], small
+    big = kernels(8192, 8192, 8192)
+    assert "split-K" not in "".join(big), big
+
+
 def test_benchmark_plans(api):
     g = api.benchmark_graphs(placeholder=True)
     kernels = {name: [l for l in _plan(api, e).splitlines() if l.startswith("kernel ")]

@@ -167,7 +167,9 @@ def test_matmul_epilogue_against_fp64(gpu, m, k, n):
     assert matmul_error(got, ref, k) <= 1e-5
 
 
-TC_SHAPES = [(512, 512, 512), (256, 1024, 768), (1024, 768, 512), (384, 512, 1024)]
+TC_SHAPES = [(512, 512, 512), (256, 1024, 768), (1024, 768, 512), (384, 512, 1024),
+             # few tiles: split-K into 8, 8 and 16 K-ranges
+             (128, 4096, 1024), (256, 2048, 512), (128, 8192, 1024)]
 
 
 @pytest.mark.parametrize("m,k,n", TC_SHAPES)
