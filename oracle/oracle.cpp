@@ -367,6 +367,25 @@ namespace {
         const size_t count = numel(out_info.shape);
         result->values.assign(count, 0.0F);
         if (count == 0) return result;
+        // A launch with a non-empty output refuses an empty input buffer
+        // (src/cuda_jit.cpp:794-803 elementwise, :875-884 reductions); the
+        // nested reductions were materialised (and checked) first above.
+        {
+            bool empty = false;
+            std::vector<const node*> stack{root.get()};
+            while (!stack.empty()) {
+                const node* n = stack.back();
+                stack.pop_back();
+                if (n == nullptr) continue;
+                if (n->k == kind::input && n->input && numel(n->input->shape) == 0) empty = true;
+                stack.push_back(n->lhs.get());
+                stack.push_back(n->rhs.get());
+            }
+            if (empty)
+                throw std::invalid_argument(root->k == kind::sum || root->k == kind::max
+                                                ? "CUDA reduction input is empty"
+                                                : "CUDA elementwise input is empty");
+        }
         float* out = result->values.data();
 
         if (root->k == kind::matmul) {

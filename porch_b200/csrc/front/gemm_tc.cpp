@@ -179,7 +179,7 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
     } // namespace
 
     int lowerer::emit_gemm_tc(int id, const box& b, kernel& k, const kernel_arg& A,
-                              const kernel_arg& B, int64_t M, int64_t N, int64_t K) {
+                              const kernel_arg& B, int64_t M, int64_t N, int64_t K, int* nonfinite) {
         (void)id;
         if (tensor_cores_disabled()) return -1;
         if (M % kBM != 0 || N % kBN != 0 || K % 64 != 0) return -1;
@@ -192,12 +192,29 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
         const int b_hi = new_temp(static_cast<size_t>(N * K) * 4);
         const int b_lo = new_temp(static_cast<size_t>(N * K) * 4);
         const int out = new_temp(static_cast<size_t>(M * N) * 4);
+        // Set by the split kernels when an operand holds Inf or NaN; the
+        // tensor-core kernels then leave the output to the CUDA-core GEMM
+        // that follows them in the plan.
+        const int nf = new_temp(256);
+        *nonfinite = nf;
         auto temp_arg = [](int t) {
             kernel_arg a;
             a.kind = arg_kind::temp;
             a.index = t;
             return a;
         };
+        {
+            launch_spec l;
+            l.name = "pb_nonfinite_clear";
+            l.source = std::string(kernel_prelude()) +
+                       "extern \"C\" __global__ void pb_nonfinite_clear(int* nf) { nf[0] = 0; }\n";
+            l.schedule = "clear the non-finite operand flag";
+            l.grid = {1, 1, 1};
+            l.block = {1, 1, 1};
+            l.args = {temp_arg(nf)};
+            finish_kernel(l);
+            p_.launches.push_back(std::move(l));
+        }
 
         // ---- 1. split A rows (contiguous, float4) --------------------------
         {
@@ -205,10 +222,11 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
             std::ostringstream src;
             src << kernel_prelude() << gemm_device_source();
             src << "extern \"C\" __global__ void __launch_bounds__(256) pb_split_rows(const float* __restrict__ x, "
-                   "float* __restrict__ hi, float* __restrict__ lo) {\n"
+                   "float* __restrict__ hi, float* __restrict__ lo, int* __restrict__ nf) {\n"
                 << "    for (pb_u64 i = (pb_u64)blockIdx.x * 256u + threadIdx.x; i < " << n4
                 << "ull; i += (pb_u64)gridDim.x * 256u) {\n"
                 << "        const float4 v = pb_ld4(x + 4 * i);\n"
+                << "        if (!(isfinite(v.x) && isfinite(v.y) && isfinite(v.z) && isfinite(v.w))) atomicOr(nf, 1);\n"
                 << "        float4 h, l;\n"
                 << "        h.x = pb_tf32_hi(v.x); l.x = pb_tf32_rn(v.x - h.x);\n"
                 << "        h.y = pb_tf32_hi(v.y); l.y = pb_tf32_rn(v.y - h.y);\n"
@@ -220,7 +238,7 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
             l.source = src.str();
             l.schedule = "3xTF32 split of A (hi = rn(x), lo = rn(x - hi))";
             l.grid = {static_cast<uint32_t>(std::min<int64_t>((n4 + 255) / 256, 148 * 16)), 1, 1};
-            l.args = {A, temp_arg(a_hi), temp_arg(a_lo)};
+            l.args = {A, temp_arg(a_hi), temp_arg(a_lo), temp_arg(nf)};
             finish_kernel(l);
             p_.launches.push_back(std::move(l));
         }
@@ -229,7 +247,7 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
             std::ostringstream src;
             src << kernel_prelude() << gemm_device_source();
             src << "extern \"C\" __global__ void __launch_bounds__(256) pb_split_transpose(const float* __restrict__ x, "
-                   "float* __restrict__ hi, float* __restrict__ lo) {\n"
+                   "float* __restrict__ hi, float* __restrict__ lo, int* __restrict__ nf) {\n"
                 << "    __shared__ float t[64][65];\n"
                 << "    const pb_u64 k0 = (pb_u64)blockIdx.y * 64u, n0 = (pb_u64)blockIdx.x * 64u;\n"
                 << "    #pragma unroll\n    for (int u = 0; u < 16; ++u) {\n"
@@ -239,6 +257,7 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
                 << "    #pragma unroll\n    for (int u = 0; u < 16; ++u) {\n"
                 << "        const pb_u32 r = threadIdx.x / 64u + 4u * u, c = threadIdx.x % 64u;\n"
                 << "        const float v = t[c][r];\n"
+                << "        if (!isfinite(v)) atomicOr(nf, 1);\n"
                 << "        const float h = pb_tf32_hi(v);\n"
                 << "        const pb_u64 o = (n0 + r) * " << K << "ull + k0 + c;\n"
                 << "        hi[o] = h;\n        lo[o] = pb_tf32_rn(v - h);\n    }\n}\n";
@@ -247,7 +266,7 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
             l.source = src.str();
             l.schedule = "3xTF32 split of B with transpose to K-major";
             l.grid = {static_cast<uint32_t>(N / 64), static_cast<uint32_t>(K / 64), 1};
-            l.args = {B, temp_arg(b_hi), temp_arg(b_lo)};
+            l.args = {B, temp_arg(b_hi), temp_arg(b_lo), temp_arg(nf)};
             finish_kernel(l);
             p_.launches.push_back(std::move(l));
         }
@@ -320,7 +339,8 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
         // run the epilogue (warp w: TMEM lane quadrant w % 4 = tile rows
         // 32(w%4).., column half w / 4), warp 8 lane 0 issues TMA, warp 9
         // allocates TMEM and its lane 0 issues the MMAs.
-        body << "    extern __shared__ float4 pb_dyn_smem[];\n"
+        body << "    if (*(const volatile int*)nf != 0) return;  // non-finite operand: CUDA-core GEMM\n"
+             << "    extern __shared__ float4 pb_dyn_smem[];\n"
              << "    __shared__ __align__(8) unsigned long long full_bar[PB_STAGES], empty_bar[PB_STAGES];\n"
              << "    __shared__ __align__(8) unsigned long long accf[2], acce[2], done_bar;\n"
              << "    __shared__ pb_u32 tmem_slot;\n"
@@ -557,7 +577,8 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
             << "(const __grid_constant__ pb_tmap tm_ahi, const __grid_constant__ pb_tmap tm_alo, "
                "const __grid_constant__ pb_tmap tm_bhi, const __grid_constant__ pb_tmap tm_blo, ";
         for (size_t i = 0; i < k.leaves.size(); ++i) src << "const float* __restrict__ in" << i << ", ";
-        src << "float* __restrict__ out, int* __restrict__ err) {\n" << body.str() << "}\n";
+        src << "float* __restrict__ out, int* __restrict__ err, const int* __restrict__ nf) {\n" << body.str()
+            << "}\n";
         l.source = src.str();
         l.schedule = "gemm tcgen05 3xTF32 128x256x16, 4-stage TMA ring (64B swizzle, no multicast), "
                      "two TMEM accumulators drained per period into fp32 registers, fused epilogue, "
@@ -596,6 +617,7 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
         kernel_arg e;
         e.kind = arg_kind::error_word;
         l.args.push_back(e);
+        l.args.push_back(temp_arg(nf));
         finish_kernel(l);
         p_.launches.push_back(std::move(l));
         if (split == 1) return out;
@@ -606,6 +628,7 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
             std::ostringstream ks;
             ks << kernel_prelude() << efn;
             std::ostringstream kb;
+            kb << "    if (*(const volatile int*)nf != 0) return;  // the CUDA-core GEMM writes out\n";
             kb << "    for (pb_u64 i = (pb_u64)blockIdx.x * 256u + threadIdx.x; i < " << n4
                << "ull; i += (pb_u64)gridDim.x * 256u) {\n"
                << "        const pb_u64 o = 4u * i, rr = o / " << N << "ull, cc = o % " << N << "ull;\n"
@@ -624,7 +647,8 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
             r.name = "pb_splitk_" + hex8(ks.str() + kb.str());
             ks << "extern \"C\" __global__ void __launch_bounds__(256) " << r.name << "(";
             for (size_t i = 0; i < k.leaves.size(); ++i) ks << "const float* __restrict__ in" << i << ", ";
-            ks << "const float* __restrict__ part, float* __restrict__ out) {\n" << kb.str() << "}\n";
+            ks << "const float* __restrict__ part, float* __restrict__ out, const int* __restrict__ nf) {\n"
+               << kb.str() << "}\n";
             r.source = ks.str();
             r.schedule = "split-K combine: " + std::to_string(split) +
                          " partials summed in split order, fused epilogue";
@@ -633,6 +657,7 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
             r.args = k.leaves;
             r.args.push_back(temp_arg(part));
             r.args.push_back(temp_arg(out));
+            r.args.push_back(temp_arg(nf));
             finish_kernel(r);
             p_.launches.push_back(std::move(r));
         }

@@ -305,6 +305,24 @@ namespace porch::detail {
         return os.str();
     }
 
+    // The reference launches every nested sum/max first and the root graph
+    // last, each refusing an empty input buffer when its own output is not
+    // empty (src/cuda_jit.cpp:794-803, 875-884); the first launch to meet an
+    // empty slot names the kind of launch it is.
+    std::string empty_input_message(const graph& g, int slot) {
+        std::vector<char> reads(g.nodes.size(), 0); // node's subtree reads `slot`
+        for (size_t i = 0; i < g.nodes.size(); ++i) { // children precede parents
+            const gnode& n = g.nodes[i];
+            reads[i] = (n.kind == expr_kind::input && n.slot == slot) ||
+                       (n.a >= 0 && reads[static_cast<size_t>(n.a)]) ||
+                       (n.b >= 0 && reads[static_cast<size_t>(n.b)]);
+            if ((n.kind == expr_kind::sum || n.kind == expr_kind::max) && n.a >= 0 &&
+                reads[static_cast<size_t>(n.a)] && checked_numel(n.shape) != 0)
+                return "CUDA reduction input is empty";
+        }
+        return "CUDA elementwise input is empty";
+    }
+
     tensor materialize_graph(const tensor_expr::node& root) {
         host_profiler& hp = hprof();
         const bool timing = hp.on.load(std::memory_order_relaxed);
@@ -330,10 +348,11 @@ namespace porch::detail {
         plan* p = b->p.get();
         if (timing) ta = now_ns();
 
-        for (const auto& s : g.slots) {
+        for (size_t si = 0; si < g.slots.size(); ++si) {
+            const auto& s = g.slots[si];
             const auto& st = cuda_jit::buffer_access::state(s->device_values);
             if (st == nullptr || st->ptr == 0)
-                throw std::invalid_argument("CUDA elementwise input is empty");
+                throw std::invalid_argument(empty_input_message(g, static_cast<int>(si)));
             if (st->device != device)
                 throw std::invalid_argument("tensor expression devices must match");
             order_read(*st, stream);

@@ -1629,13 +1629,22 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
         if (boxes.size() != 1) return -1;
         const kernel_arg A = as_buffer(m.a);
         const kernel_arg B = as_buffer(m.b);
-        if (const int t = emit_gemm_tc(id, boxes[0], k, A, B, M, N, K); t >= 0) return t;
+        int nonfinite = -1;
+        if (const int t = emit_gemm_tc(id, boxes[0], k, A, B, M, N, K, &nonfinite); t >= 0) {
+            // Inf or NaN in an operand: the 3xTF32 expansion turns inf * 0
+            // (an inf hi times a zero lo) into NaN where the reference's fp32
+            // chain gives +-inf, so that case reruns on the CUDA cores with
+            // the reference's own arithmetic (a k-ordered FMA chain), into
+            // the same output; it returns at once when every value is finite.
+            emit_gemm_simt(boxes[0], k, A, B, M, N, K, t, nonfinite);
+            return t;
+        }
         return emit_gemm_simt(boxes[0], k, A, B, M, N, K);
     }
 
     int lowerer::emit_gemm_simt(const box& b, kernel& k, const kernel_arg& A, const kernel_arg& B,
-                                int64_t M, int64_t N, int64_t K) {
-        const int out = new_temp(static_cast<size_t>(M * N) * sizeof(float));
+                                int64_t M, int64_t N, int64_t K, int out_temp, int guard_temp) {
+        const int out = out_temp >= 0 ? out_temp : new_temp(static_cast<size_t>(M * N) * sizeof(float));
         rank_ = 2;
         const bool wide = M * N >= (int64_t{1} << 31) - 4096 || M * K >= (int64_t{1} << 31) - 4096 ||
                           K * N >= (int64_t{1} << 31) - 4096;
@@ -1646,6 +1655,7 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
         src << emit_expr_function(b, "0", order);
         std::vector<std::string> cvar = {"r", "c"};
         std::ostringstream body;
+        if (guard_temp >= 0) body << "    if (*(const volatile int*)guard == 0) return;\n";
         body << "    __shared__ float As[16][68];\n    __shared__ float Bs[16][68];\n";
         body << "    const pb_u32 tx = threadIdx.x & 15u, ty = threadIdx.x >> 4;\n";
         body << "    const " << I << " row0 = (" << I << ")blockIdx.y * 64u, col0 = (" << I << ")blockIdx.x * 64u;\n";
@@ -1684,11 +1694,13 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
         src << "extern \"C\" __global__ void __launch_bounds__(256) " << l.name
             << "(const float* __restrict__ A, const float* __restrict__ B, ";
         for (size_t i = 0; i < k.leaves.size(); ++i) src << "const float* __restrict__ in" << i << ", ";
-        src << "float* __restrict__ out) {\n" << body.str() << "}\n";
+        src << "float* __restrict__ out" << (guard_temp >= 0 ? ", const int* guard" : "") << ") {\n"
+            << body.str() << "}\n";
         l.source = src.str();
         l.grid = {static_cast<uint32_t>((N + 63) / 64), static_cast<uint32_t>((M + 63) / 64), 1};
         l.block = {256, 1, 1};
         l.schedule = "gemm CUDA-core 64x64x16 tiles, k-ordered FMA chain, fused epilogue";
+        if (guard_temp >= 0) l.schedule += " (runs only for non-finite operands)";
         l.args.push_back(A);
         l.args.push_back(B);
         for (const kernel_arg& a : k.leaves) l.args.push_back(a);
@@ -1696,6 +1708,12 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
         o.kind = arg_kind::temp;
         o.index = out;
         l.args.push_back(o);
+        if (guard_temp >= 0) {
+            kernel_arg gk;
+            gk.kind = arg_kind::temp;
+            gk.index = guard_temp;
+            l.args.push_back(gk);
+        }
         finish_kernel(l);
         p_.launches.push_back(std::move(l));
         return out;

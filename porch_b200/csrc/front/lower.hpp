@@ -106,11 +106,15 @@ namespace porch::detail {
         int emit_reduce(int id);
         int emit_softmax(int id, int x);
         int emit_gemm(int id, int mm);
+        // CUDA-core GEMM (fp32 FMA chain in k order). out_temp >= 0 writes
+        // into that temp; guard_temp >= 0 runs only when its first int is set.
         int emit_gemm_simt(const box& b, kernel& k, const kernel_arg& A, const kernel_arg& B,
-                           int64_t M, int64_t N, int64_t K);
-        // tcgen05 3xTF32 path; returns -1 when the shape is not eligible.
+                           int64_t M, int64_t N, int64_t K, int out_temp = -1, int guard_temp = -1);
+        // tcgen05 3xTF32 path; returns -1 when the shape is not eligible. On
+        // success *nonfinite receives a temp whose first int is set when an
+        // operand holds Inf or NaN (the tensor-core result is then skipped).
         int emit_gemm_tc(int id, const box& b, kernel& k, const kernel_arg& A,
-                         const kernel_arg& B, int64_t M, int64_t N, int64_t K);
+                         const kernel_arg& B, int64_t M, int64_t N, int64_t K, int* nonfinite);
 
         const graph& g_;
         plan& p_;

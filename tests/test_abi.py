@@ -104,7 +104,9 @@ def test_small_m_matmul_splits_k(api):
         plan = _plan(api, api.relu(api.matmul(a, b) + api.broadcast_to(bi, [m, n])))
         return [line for line in plan.splitlines() if line.startswith("kernel ")]
     small = kernels(128, 4096, 4096)
-    assert "split-K x8" in small[-2] and "split-K combine" in small[-1], small
+    # ..., tcgen05 GEMM, split-K combine, guarded CUDA-core GEMM (non-finite operands)
+    assert "split-K x8" in small[-3] and "split-K combine" in small[-2], small
+    assert "non-finite" in small[-1], small
     big = kernels(8192, 8192, 8192)
     assert "split-K" not in "".join(big), big
 

@@ -1,0 +1,164 @@
+"""Edge cases: zero-size dimensions, NaN/Inf operands, and tensors past 2^31
+elements (the 64-bit index paths).
+
+The reference's rules (src/tensor.cpp): an empty result launches nothing
+(:1023-1028); IEEE arithmetic in the generated code (:616-683) with
+`(l > r ? l : r)` maxima, so NaN handling follows from the comparison form;
+its matmul is an fp32 FMA chain, so Inf/NaN operands give Inf/NaN exactly
+as IEEE says (the 3xTF32 path hands such operands to the same chain).
+"""
+
+import numpy as np
+import pytest
+
+import graphs
+from tolerances import assert_bitwise, assert_relative
+
+ZERO_SIZE = [
+    ("0 input 0\n1 exp 0\n", [[0, 5]]),
+    ("0 input 0\n1 input 1\n2 add 0 1\n", [[3, 0], [3, 0]]),
+    ("0 input 0\n1 sum 0 1 0\n", [[4, 0]]),
+    ("0 input 0\n1 max 0 0 1\n", [[0, 6]]),
+    ("0 input 0\n1 transpose 0\n", [[0, 7]]),
+    ("0 input 0\n1 input 1\n2 concat 0 1 0\n", [[0, 3], [2, 3]]),
+    ("0 input 0\n1 tensor 0\n2 index 1 s2:2:1;s0:3:1\n", [[4, 3]]),
+]
+
+
+# Where the output is not empty but an input is, the reference refuses the
+# launch; the oracle restates that rule and the CUDA path must agree.
+REFUSED = {2: "CUDA reduction input is empty", 3: "CUDA reduction input is empty",
+           5: "CUDA elementwise input is empty"}
+
+
+@pytest.mark.parametrize("case", range(len(ZERO_SIZE)))
+def test_oracle_zero_size_rules(oracle_lib, case):
+    program, shapes = ZERO_SIZE[case]
+    ins = [np.zeros(s, np.float32) for s in shapes]
+    if case in REFUSED:
+        with pytest.raises(ValueError, match=REFUSED[case]):
+            graphs.evaluate_oracle(program, ins)
+    else:
+        assert graphs.evaluate_oracle(program, ins).size == 0
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("case", range(len(ZERO_SIZE)))
+def test_zero_size_dimensions_match_oracle(gpu, case):
+    program, shapes = ZERO_SIZE[case]
+    rng = np.random.default_rng(1)
+    ins = [rng.normal(0, 1, s).astype(np.float32) for s in shapes]
+    if case in REFUSED:
+        with pytest.raises(ValueError, match=REFUSED[case]):
+            graphs.evaluate_product(gpu, program, ins)
+        return
+    want = graphs.evaluate_oracle(program, ins)
+    got = graphs.evaluate_product(gpu, program, ins)
+    assert list(got.shape) == list(want.shape)
+    assert_bitwise(got, want, program)
+
+
+SPECIALS = np.array([np.nan, np.inf, -np.inf, 0.0, -0.0, 1.0, -2.5, 3.4e38, -3.4e38, 1e-45],
+                    dtype=np.float32)
+# A NaN inside a max reduction makes `(m > x ? m : x)` depend on the order
+# in which values are combined (the reference's 256-wide block tree, the
+# host oracle's loop and this library's warp tree all differ), so the
+# reductions and softmax get +-Inf and extremes but no NaN.
+NO_NAN = {"softmax", "max"}
+NONFINITE_PROGRAMS = [
+    ("0 input 0\n1 input 1\n2 add 0 1\n", True),
+    ("0 input 0\n1 input 1\n2 multiply 0 1\n", True),
+    ("0 input 0\n1 input 1\n2 divide 0 1\n", True),
+    ("0 input 0\n1 input 1\n2 maximum 0 1\n", True),
+    ("0 input 0\n1 input 1\n2 minimum 0 1\n", True),
+    ("0 input 0\n1 relu 0\n", True),
+    ("0 input 0\n1 reciprocal 0\n", True),
+    ("0 input 0\n1 exp 0\n", False),
+    ("0 input 0\n1 logistic 0\n", False),
+    ("0 input 0\n1 softmax 0 1\n", False),
+    ("0 input 0\n1 max 0 1 0\n", True),
+]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("program,exact", NONFINITE_PROGRAMS)
+def test_nan_and_inf_operands_match_oracle(gpu, program, exact):
+    # Every pair of special values, as rows of a [10, 10] grid.
+    specials = SPECIALS
+    if {line.split()[1] for line in program.strip().splitlines()} & NO_NAN:
+        specials = np.where(np.isnan(SPECIALS), np.float32(7.0), SPECIALS).astype(np.float32)
+    a = np.repeat(specials[:, None], 10, axis=1)
+    b = np.repeat(specials[None, :], 10, axis=0)
+    n_inputs = program.count("input")
+    ins = [a, b][:n_inputs]
+    want = graphs.evaluate_oracle(program, ins)
+    got = graphs.evaluate_product(gpu, program, ins)
+    if exact:
+        assert_bitwise(got, want, program)
+    else:
+        assert_relative(got, want, 1e-5, program)
+
+
+@pytest.mark.gpu
+def test_nonfinite_matmul_operands_match_the_reference(gpu):
+    """Inf and NaN in tensor-core-eligible operands: the same non-finite
+    pattern as the reference's own fp32 chain, finite entries within the
+    matmul tolerance of it."""
+    import test_ref_fullsize as ref
+
+    rng = np.random.default_rng(9)
+    m = k = n = 512
+    a = rng.uniform(-1, 1, (m, k)).astype(np.float32)
+    b = rng.uniform(-1, 1, (k, n)).astype(np.float32)
+    a[3, 7] = np.inf
+    a[10, 100] = -np.inf
+    a[200, :4] = np.nan
+    b[5, 9] = np.inf
+    b[7, 300] = 0.0  # inf * 0 -> NaN in row 3 only where the chain meets it
+    prog = "0 input 0\n1 input 1\n2 matmul 0 1\n"
+    assert "tcgen05" in gpu.describe(gpu.matmul(gpu.tensor([m, k], a), gpu.tensor([k, n], b)))
+    got = graphs.evaluate_product(gpu, prog, [a, b])
+    want = ref._run_reference(prog, [a, b])
+    assert np.array_equal(np.isnan(got), np.isnan(want))
+    assert np.array_equal(np.isposinf(got), np.isposinf(want))
+    assert np.array_equal(np.isneginf(got), np.isneginf(want))
+    fin = np.isfinite(want)
+    assert np.max(np.abs(got[fin] - want[fin])) <= 1e-4
+    # And with finite operands the same plan takes the tensor-core path: the
+    # CUDA-core kernel returns at once (results equal to the reference's
+    # within the 3xTF32 tolerance).
+    a2, b2 = np.nan_to_num(a, posinf=1.0, neginf=-1.0), np.nan_to_num(b, posinf=1.0, neginf=-1.0)
+    got2 = graphs.evaluate_product(gpu, prog, [a2, b2])
+    want2 = ref._run_reference(prog, [a2, b2])
+    assert np.max(np.abs(got2 - want2)) <= 1e-4
+
+
+BIG = (1 << 31) + 8
+
+
+@pytest.mark.gpu
+def test_elementwise_past_2_31_elements(gpu):
+    api = gpu
+    c = api.tensor([1], np.array([1.5], dtype=np.float32))
+    y = api.materialize(api.broadcast_to(c, [BIG]) * 2.0 + 1.0)
+    assert y.shape() == [BIG]
+    tail = api.materialize(y[BIG - 16:BIG]).cpu()
+    head = api.materialize(y[0:16]).cpu()
+    assert np.all(tail == 4.0) and np.all(head == 4.0)
+
+
+@pytest.mark.gpu
+def test_softmax_and_column_sum_past_2_31_elements(gpu):
+    api = gpu
+    rows, cols = (1 << 21) + 1, 1024
+    rng = np.random.default_rng(3)
+    row = rng.normal(0, 1, (1, cols)).astype(np.float32)
+    x = api.broadcast_to(api.tensor([1, cols], row), [rows, cols])
+    p = api.materialize(api.softmax(x, 1))
+    last = api.materialize(p[rows - 2:rows, 0:cols]).cpu()
+    want = graphs.evaluate_oracle("0 input 0\n1 softmax 0 1\n", [row])
+    assert_relative(last[0:1], want, 1e-5, "first of the last two rows")
+    assert_relative(last[1:2], want, 1e-5, "last row")
+    ones = api.broadcast_to(api.tensor([1, cols], np.ones((1, cols), np.float32)), [rows, cols])
+    s = api.materialize(api.sum(ones, 0)).cpu()
+    assert np.all(s == np.float32(rows))  # exact: integers below 2^24
