@@ -228,6 +228,8 @@ int pb_comm_wait(pb_comm* comm);
  * The split operands live in a fixed 64 MiB device array that every GPU
  * loading this library holds until exit; calls needing more than that
  * (2 * (M*K + N*K) floats) are rejected with PB_ERR_INVALID_ARGUMENT.
+ * Operands must be finite: with Inf or NaN in A or B the call returns
+ * PB_ERR_INVALID_ARGUMENT and C is unspecified (pb_materialize handles them).
  * All calls share the array, so calls that overlap on the GPU race. The first
  * call on each device sets that device up (symbol address, kernel limits);
  * make it outside any stream capture. The call enqueues on `stream`

@@ -135,6 +135,8 @@ namespace {
                                                       float* __restrict__ lo, u64 n4) {
         for (u64 i = (u64)blockIdx.x * 256u + threadIdx.x; i < n4; i += (u64)gridDim.x * 256u) {
             const float4 v = __ldg(reinterpret_cast<const float4*>(x) + i);
+            if (!(isfinite(v.x) && isfinite(v.y) && isfinite(v.z) && isfinite(v.w)))
+                atomicOr(&pb_noalloc_error[3], 1);
             float4 h, l;
             h.x = tf32_hi(v.x); l.x = tf32_rn(v.x - h.x);
             h.y = tf32_hi(v.y); l.y = tf32_rn(v.y - h.y);
@@ -160,6 +162,7 @@ namespace {
         for (int u = 0; u < 16; ++u) {
             const u32 r = threadIdx.x / 64u + 4u * u, c = threadIdx.x % 64u;
             const float v = t[c][r];
+            if (!isfinite(v)) atomicOr(&pb_noalloc_error[3], 1);
             const float h = tf32_hi(v);
             const u64 o = (n0 + r) * K + k0 + c;
             hi[o] = h;
@@ -385,10 +388,15 @@ extern "C" int pb_matmul_3xtf32_noalloc(const float* a, const float* b, float* c
     e = cudaMemcpyFromSymbolAsync(err, pb_noalloc_error, sizeof err, 0, cudaMemcpyDeviceToHost, s);
     if (e == cudaSuccess) e = cudaStreamSynchronize(s);
     if (e != cudaSuccess) return cuda_fail(e, "reading the error word");
-    if (err[0] != 0) {
+    if (err[0] != 0 || err[3] != 0) {
         const int zero[4] = {0, 0, 0, 0};
         (void)cudaMemcpyToSymbolAsync(pb_noalloc_error, zero, sizeof zero, 0, cudaMemcpyHostToDevice, s);
         (void)cudaStreamSynchronize(s);
+        if (err[0] == 0)
+            return fail(PB_ERR_INVALID_ARGUMENT,
+                        "pb_matmul_3xtf32_noalloc: A or B holds Inf or NaN, which the 3xTF32 "
+                        "expansion cannot carry (an Inf high part times a zero low part is NaN); "
+                        "pb_materialize handles them with an fp32 FMA chain");
         char msg[160];
         std::snprintf(msg, sizeof msg, "pb_matmul_3xtf32_noalloc: a bounded wait gave up (code %#x, block %d)",
                       err[0], err[1]);

@@ -63,3 +63,30 @@ def test_noalloc_matmul_rejects_sizes_beyond_its_scratch(gpu):
     assert "scratch" in L.pb_last_error().decode()
     # Shapes the kernel cannot tile are rejected too.
     assert L.pb_matmul_3xtf32_noalloc(pa, pa, pa, 100, 256, 64, None) == 1
+
+
+def test_noalloc_matmul_refuses_nonfinite_operands_and_recovers(gpu):
+    api = gpu
+    from porch_b200._lib import lib
+
+    L = lib()
+    m = k = n = 512
+    rng = np.random.default_rng(77)
+    a = rng.uniform(-1, 1, (m, k)).astype(np.float32)
+    b = rng.uniform(-1, 1, (k, n)).astype(np.float32)
+    bad = a.copy()
+    bad[5, 6] = np.inf
+    A_bad = _device_tensor(api, [m, k], bad)
+    A = _device_tensor(api, [m, k], a)
+    B = _device_tensor(api, [k, n], b)
+    C = _device_tensor(api, [m, n], np.zeros(m * n, dtype=np.float32))
+    pab, _ = A_bad.device_data()
+    pa, _ = A.device_data()
+    pb, _ = B.device_data()
+    pc, _ = C.device_data()
+    assert L.pb_matmul_3xtf32_noalloc(pab, pb, pc, m, n, k, None) == 1
+    assert "Inf or NaN" in L.pb_last_error().decode()
+    # The flag was cleared: a finite call afterwards succeeds.
+    assert L.pb_matmul_3xtf32_noalloc(pa, pb, pc, m, n, k, None) == 0, L.pb_last_error().decode()
+    ref = a.astype(np.float64) @ b.astype(np.float64)
+    assert matmul_error(C.cpu().reshape(m, n), ref, k) <= MATMUL_TOL
