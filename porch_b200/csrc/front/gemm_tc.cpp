@@ -182,7 +182,11 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
                               const kernel_arg& B, int64_t M, int64_t N, int64_t K, int* nonfinite) {
         (void)id;
         if (tensor_cores_disabled()) return -1;
-        if (M % kBM != 0 || N % kBN != 0 || K % 64 != 0) return -1;
+        // Any M; N and K multiples of 4 (16-byte TMA row strides for the
+        // K-major hi/lo arrays and float4 epilogue stores). Edge tiles read
+        // zeros past M, N and K (TMA out-of-bounds fill) and mask their
+        // stores.
+        if (N % 4 != 0 || K % 4 != 0 || M < 1) return -1;
         if (M * N * K < (int64_t{1} << 27)) return -1;
         if (M > (int64_t{1} << 30) || N > (int64_t{1} << 30) || K > (int64_t{1} << 30)) return -1;
         rank_ = 2;
@@ -252,10 +256,12 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
                 << "    const pb_u64 k0 = (pb_u64)blockIdx.y * 64u, n0 = (pb_u64)blockIdx.x * 64u;\n"
                 << "    #pragma unroll\n    for (int u = 0; u < 16; ++u) {\n"
                 << "        const pb_u32 r = threadIdx.x / 64u + 4u * u, c = threadIdx.x % 64u;\n"
-                << "        t[r][c] = pb_ld(x + (k0 + r) * " << N << "ull + n0 + c);\n    }\n"
+                << "        t[r][c] = (k0 + r < " << K << "ull && n0 + c < " << N << "ull) ? pb_ld(x + (k0 + r) * " << N
+                << "ull + n0 + c) : 0.0f;\n    }\n"
                 << "    __syncthreads();\n"
                 << "    #pragma unroll\n    for (int u = 0; u < 16; ++u) {\n"
                 << "        const pb_u32 r = threadIdx.x / 64u + 4u * u, c = threadIdx.x % 64u;\n"
+                << "        if (n0 + r >= " << N << "ull || k0 + c >= " << K << "ull) continue;\n"
                 << "        const float v = t[c][r];\n"
                 << "        if (!isfinite(v)) atomicOr(nf, 1);\n"
                 << "        const float h = pb_tf32_hi(v);\n"
@@ -265,7 +271,7 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
             l.name = "pb_split_transpose";
             l.source = src.str();
             l.schedule = "3xTF32 split of B with transpose to K-major";
-            l.grid = {static_cast<uint32_t>(N / 64), static_cast<uint32_t>(K / 64), 1};
+            l.grid = {static_cast<uint32_t>((N + 63) / 64), static_cast<uint32_t>((K + 63) / 64), 1};
             l.args = {B, temp_arg(b_hi), temp_arg(b_lo), temp_arg(nf)};
             finish_kernel(l);
             p_.launches.push_back(std::move(l));
@@ -273,8 +279,8 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
         // ---- 3. tcgen05 GEMM + epilogue -------------------------------------
         std::vector<int> order;
         const std::string efn = emit_expr_function(b, "0", order);
-        const int64_t tiles_m = M / kBM, tiles_n = N / kBN;
-        const int64_t num_kb = K / kBK;
+        const int64_t tiles_m = (M + kBM - 1) / kBM, tiles_n = (N + kBN - 1) / kBN;
+        const int64_t raw_kb = (K + kBK - 1) / kBK;
         const int group_m = 16;
         // Accumulation period in k-blocks. The drift of a tensor-core
         // accumulator grows with the number of MMAs added into one period
@@ -283,12 +289,13 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
         // sqrt(K) / 2 k-blocks keeps ours about half the chain's at every K
         // (measured: one accumulator over 8192 of K drifts 5x the chain, a
         // period over all of K = 512 almost 5x). Capped at 32 (draining
-        // costs a few percent per launch at 8), a power of two dividing
-        // K / 16, at least 4 (K % 64 == 0).
+        // costs a few percent per launch at 8), a power of two, at least 4;
+        // the k-blocks are padded to a whole number of periods (past K the
+        // TMA loads read zeros, which add exactly nothing).
         int period = 4;
-        while (period < 32 && num_kb % (period * 2) == 0 &&
-               static_cast<double>(period * 2) <= std::sqrt(static_cast<double>(K)) / 2.0)
+        while (period < 32 && static_cast<double>(period * 2) <= std::sqrt(static_cast<double>(K)) / 2.0)
             period *= 2;
+        const int64_t num_kb = (raw_kb + period - 1) / period * period;
         // Split-K when the tiles leave most SMs idle (fewer tiles than half
         // of 148 SMs: a short batch, a thin row block): S K-ranges per tile
         // (a power of two up to 16, each a whole number of periods and at
@@ -524,16 +531,22 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
             // Raw partial tile of this K split; the split-K kernel below
             // sums the partials and applies the epilogue.
             body << "            const pb_u64 sp = (pb_u64)(t % PB_SPLIT);\n"
+                 << "            if (rr < " << M << "ull) {\n"
                  << "            #pragma unroll\n"
                  << "            for (int c = 0; c < PB_BN / 64; ++c) {\n"
                  << "                const int cbase = n0 + (int)half * (PB_BN / 2) + c * 32;\n"
                  << "                float* orow = out + sp * " << M * N << "ull + rr * " << N << "ull + cbase;\n"
                  << "                #pragma unroll\n"
                  << "                for (int j = 0; j < 32; j += 4)\n"
-                 << "                    pb_st4(orow + j, make_float4(acc[c * 32 + j], acc[c * 32 + j + 1], "
+                 << "                    if ((pb_u64)(cbase + j) < " << N << "ull)\n"
+                 << "                        pb_st4(orow + j, make_float4(acc[c * 32 + j], acc[c * 32 + j + 1], "
                     "acc[c * 32 + j + 2], acc[c * 32 + j + 3]));\n"
+                 << "            }\n"
                  << "            }\n";
         } else {
+            // Rows past M and columns past N (edge tiles) are neither read
+            // (leaves) nor written.
+            body << "            if (rr < " << M << "ull) {\n";
             emit_hoisted(body, "            ");
             body << "            #pragma unroll\n"
                  << "            for (int c = 0; c < PB_BN / 64; ++c) {\n"
@@ -542,10 +555,11 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
                  << "                #pragma unroll\n"
                  << "                for (int j = 0; j < 32; j += 4) {\n"
                  << "                    const pb_u64 cc = (pb_u64)(cbase + j);\n"
-                 << "                    (void)cc;\n";
+                 << "                    if (cc >= " << N << "ull) continue;\n";
             emit_epilogue4(body, "                    ", "acc[c * 32 + j + e]");
             body << "                    pb_st4(orow + j, make_float4(y[0], y[1], y[2], y[3]));\n"
                  << "                }\n"
+                 << "            }\n"
                  << "            }\n";
         }
         body

@@ -169,13 +169,16 @@ def test_matmul_epilogue_against_fp64(gpu, m, k, n):
 
 TC_SHAPES = [(512, 512, 512), (256, 1024, 768), (1024, 768, 512), (384, 512, 1024),
              # few tiles: split-K into 8, 8 and 16 K-ranges
-             (128, 4096, 1024), (256, 2048, 512), (128, 8192, 1024)]
+             (128, 4096, 1024), (256, 2048, 512), (128, 8192, 1024),
+             # edge tiles: M, N, K not multiples of the tile (zero fill past
+             # the edges, masked stores), with and without split-K
+             (1000, 520, 1004), (300, 4096, 772), (129, 4100, 260)]
 
 
 @pytest.mark.parametrize("m,k,n", TC_SHAPES)
 def test_tcgen05_3xtf32_matmul(gpu, m, k, n):
-    """Shapes eligible for the tcgen05 path (M%128, N%256, K%64): the plan
-    must use it, and the result must hold fp32 accuracy: within the
+    """Shapes eligible for the tcgen05 path (N, K multiples of 4 and
+    M*N*K >= 2^27): the plan must use it, and the result must hold fp32 accuracy: within the
     normalised 1e-5 bound, and within 4x the error of the reference's
     sequential fp32 accumulation (a plain one-pass TF32 product is about
     1000x worse than fp32 and fails this)."""
