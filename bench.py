@@ -64,7 +64,7 @@ KEYS = {
 }
 # Kernel family whose launches the roofline line describes.
 DOMINANT = {"c1_elementwise": "pb_elem", "c2_view": "pb_elem", "c3a_softmax": "pb_softmax",
-            "c3b_relu_logistic": "pb_elem", "c4_matmul": "pb_gemm", "c5_mlp": "pb_gemm"}
+            "c3b_relu_logistic": "pb_elem", "c4_matmul": "pb_gemm_tc", "c5_mlp": "pb_gemm_tc"}
 
 
 def peaks() -> dict:
