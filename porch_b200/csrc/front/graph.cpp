@@ -365,8 +365,12 @@ namespace porch::detail {
         if (timing) t2 = now_ns();
 
         uint64_t error_word = 0;
-        uint64_t values[64];
-        void* params[64];
+        // Kernel arguments: one 8-byte pointer or value per argument (tensor
+        // maps apart); up to 2048 of them fit the 32 KB parameter space of
+        // sm_100 launches, so a graph may read that many distinct tensors.
+        constexpr size_t kMaxArgs = 2048;
+        thread_local std::vector<uint64_t> values;
+        thread_local std::vector<void*> params;
         struct alignas(64) tensor_map_storage {
             unsigned char bytes[128];
         };
@@ -395,7 +399,11 @@ namespace porch::detail {
                     l.per_device->function[device].store(fn, std::memory_order_release);
                 }
             }
-            if (l.args.size() > 64) throw std::runtime_error("kernel has too many arguments");
+            if (l.args.size() > kMaxArgs) throw std::runtime_error("kernel has too many arguments");
+            if (values.size() < l.args.size()) {
+                values.resize(l.args.size());
+                params.resize(l.args.size());
+            }
             for (size_t i = 0; i < l.args.size(); ++i) {
                 const kernel_arg& a = l.args[i];
                 switch (a.kind) {
@@ -442,7 +450,7 @@ namespace porch::detail {
                 if (pg != 0) grid[0] = pg;
             }
             check(pbrt_launch(device, fn, grid.data(), l.block.data(), l.smem,
-                              stream->stream, params, nullptr));
+                              stream->stream, params.data(), nullptr));
         }
         if (timing) t3 = now_ns();
 

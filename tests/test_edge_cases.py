@@ -162,3 +162,21 @@ def test_softmax_and_column_sum_past_2_31_elements(gpu):
     ones = api.broadcast_to(api.tensor([1, cols], np.ones((1, cols), np.float32)), [rows, cols])
     s = api.materialize(api.sum(ones, 0)).cpu()
     assert np.all(s == np.float32(rows))  # exact: integers below 2^24
+
+
+@pytest.mark.gpu
+def test_graph_reading_many_distinct_tensors(gpu):
+    """300 distinct inputs in one fused kernel (more than 64 kernel
+    arguments; the reference passes its inputs as one parameter vector)."""
+    api = gpu
+    rng = np.random.default_rng(21)
+    arrays = [rng.integers(-4, 5, 1000).astype(np.float32) for _ in range(300)]
+    tensors = [api.tensor([1000], a) for a in arrays]
+    expr = tensors[0] + 0.0
+    for t in tensors[1:]:
+        expr = expr + t
+    got = api.materialize(expr).cpu()
+    want = np.zeros(1000, np.float32)
+    for a in arrays:
+        want = (want + a).astype(np.float32)
+    assert_bitwise(got, want, "300-input sum")
