@@ -1659,10 +1659,16 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
         src << emit_expr_function(b, "0", order);
         std::vector<std::string> cvar = {"r", "c"};
         std::ostringstream body;
+        // 64x64 output tiles, walked with a grid-stride loop: the guarded
+        // fallback of the tensor-core GEMM gets a small grid, so when every
+        // operand is finite it costs one short launch, not tiles' worth.
+        const int64_t tiles_n = (N + 63) / 64, tiles = tiles_n * ((M + 63) / 64);
         if (guard_temp >= 0) body << "    if (*(const volatile int*)guard == 0) return;\n";
         body << "    __shared__ float As[16][68];\n    __shared__ float Bs[16][68];\n";
         body << "    const pb_u32 tx = threadIdx.x & 15u, ty = threadIdx.x >> 4;\n";
-        body << "    const " << I << " row0 = (" << I << ")blockIdx.y * 64u, col0 = (" << I << ")blockIdx.x * 64u;\n";
+        body << "    for (" << I << " tile = blockIdx.x; tile < " << lit(tiles, wide) << "; tile += gridDim.x) {\n";
+        body << "    const " << I << " row0 = (tile / " << lit(tiles_n, wide) << ") * 64u, col0 = (tile % "
+             << lit(tiles_n, wide) << ") * 64u;\n";
         body << "    float acc[4][4];\n";
         body << "    #pragma unroll\n    for (int i = 0; i < 4; ++i)\n        #pragma unroll\n        for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;\n";
         body << "    for (" << I << " k0 = 0; k0 < " << lit(K, wide) << "; k0 += 16u) {\n";
@@ -1693,6 +1699,7 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
         body << "                out[r * " << lit(N, wide) << " + c] = pb_e0(acc[i][j]";
         for (size_t li = 0; li < order.size(); ++li) body << ", x" << li;
         body << ");\n            }\n        }\n";
+        body << "    __syncthreads();  // shared tiles are reused by the next output tile\n    }\n";
         launch_spec l;
         l.name = "pb_gemm_simt_" + hex64(hash_string(src.str() + body.str())).substr(0, 8);
         src << "extern \"C\" __global__ void __launch_bounds__(256) " << l.name
@@ -1701,7 +1708,8 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
         src << "float* __restrict__ out" << (guard_temp >= 0 ? ", const int* guard" : "") << ") {\n"
             << body.str() << "}\n";
         l.source = src.str();
-        l.grid = {static_cast<uint32_t>((N + 63) / 64), static_cast<uint32_t>((M + 63) / 64), 1};
+        if (tiles > 0x7fffffff) throw std::invalid_argument("matmul output is too large for one launch");
+        l.grid = {static_cast<uint32_t>(guard_temp >= 0 ? std::min<int64_t>(tiles, 148 * 8) : tiles), 1, 1};
         l.block = {256, 1, 1};
         l.schedule = "gemm CUDA-core 64x64x16 tiles, k-ordered FMA chain, fused epilogue";
         if (guard_temp >= 0) l.schedule += " (runs only for non-finite operands)";
