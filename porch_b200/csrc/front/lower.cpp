@@ -150,9 +150,13 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
         if (n.kind == expr_kind::matmul || n.kind == expr_kind::sum ||
             n.kind == expr_kind::max)
             return true;
+        // Only a softmax over the last axis has a kernel of its own; over
+        // another axis the pattern lowers as its reductions and elementwise
+        // ops, so it must not stop the elementwise walk (materialize would
+        // hand it straight back here).
         int x = 0;
         size_t axis = 0;
-        return match_softmax(id, x, axis);
+        return match_softmax(id, x, axis) && axis + 1 == n.shape.size();
     }
 
     // Finds the single matmul whose output feeds `id` through elementwise
@@ -1228,6 +1232,7 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
         std::ostringstream body;
         launch_spec l;
         std::string desc;
+        int threads = 256;
         // The loop over the reduction axis of a strided reduction: eight
         // independent loads (and prologues) per step, then combined in k
         // order -- the same result as one at a time, with eight loads in
@@ -1254,8 +1259,71 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
             value_at("k", "v", "        ");
             os << "        " << combine("acc", "v") << "\n    }\n";
         };
+        // Pass 2 of a reduction split into row chunks: `chunks` partials per
+        // output, laid out [chunk][output]. A CTA of 512 threads covers W
+        // outputs (32, or 8 when there are too few outputs to spread 32-wide
+        // CTAs over the GPU) with G = 512 / W groups; group g combines chunks
+        // g, g+G, ... in order (eight loads in flight). The G group results
+        // are then combined in a fixed two-level order through shared
+        // memory, so the result does not depend on scheduling.
+        auto emit_chunk_combine = [&](int partial, int64_t chunks, const std::string& what) {
+            const bool pwide = wide || chunks * outputs >= (int64_t{1} << 31) - 4096;
+            const std::string PI = pwide ? "pb_u64" : "pb_u32";
+            const int W = outputs >= 32 * 148 ? 32 : 8;
+            const int G = 512 / W;
+            const std::string Ws = std::to_string(W), Gs = std::to_string(G), Ss = std::to_string(G / 8);
+            std::ostringstream b2;
+            b2 << "    __shared__ float red[" << Gs << "][" << W + 1 << "];\n";
+            b2 << "    __shared__ float red2[8][" << W + 1 << "];\n";
+            b2 << "    const pb_u32 j = threadIdx.x % " << Ws << "u, g = threadIdx.x / " << Ws << "u;\n";
+            b2 << "    const " << PI << " o = (" << PI << ")blockIdx.x * " << Ws << "u + j;\n";
+            b2 << "    float acc = " << init << ";\n";
+            b2 << "    if (o < " << lit(outputs, pwide) << ") {\n";
+            b2 << "        " << PI << " c = g;\n";
+            b2 << "        for (; c + " << 7 * G << "u < " << lit(chunks, pwide) << "; c += " << 8 * G
+               << "u) {\n            float vv[8];\n";
+            b2 << "            #pragma unroll\n            for (int u = 0; u < 8; ++u) vv[u] = part[(c + " << Gs
+               << "u * (" << PI << ")u) * " << lit(outputs, pwide) << " + o];\n";
+            b2 << "            #pragma unroll\n            for (int u = 0; u < 8; ++u) { const float v = vv[u]; "
+               << combine("acc", "v") << " }\n        }\n";
+            b2 << "        for (; c < " << lit(chunks, pwide) << "; c += " << Gs << "u) {\n";
+            b2 << "            const float v = part[c * " << lit(outputs, pwide) << " + o]; " << combine("acc", "v")
+               << "\n        }\n    }\n";
+            b2 << "    red[g][j] = acc;\n    __syncthreads();\n";
+            b2 << "    if (g < 8u) {\n        float s = red[g * " << Ss << "u][j];\n";
+            b2 << "        #pragma unroll\n        for (int w = 1; w < " << Ss << "; ++w) { const float v = red[g * "
+               << Ss << "u + w][j]; " << combine("s", "v") << " }\n";
+            b2 << "        red2[g][j] = s;\n    }\n    __syncthreads();\n";
+            b2 << "    if (g == 0u && o < " << lit(outputs, pwide) << ") {\n";
+            b2 << "        float s = red2[0][j];\n";
+            b2 << "        #pragma unroll\n        for (int w = 1; w < 8; ++w) { const float v = red2[w][j]; "
+               << combine("s", "v") << " }\n";
+            b2 << "        out[o] = s;\n    }\n";
+            launch_spec l2;
+            l2.name = "pb_reduce_comb_" + hex64(hash_string(b2.str())).substr(0, 8);
+            std::ostringstream s2;
+            s2 << kernel_prelude() << "extern \"C\" __global__ void __launch_bounds__(512) " << l2.name
+               << "(const float* __restrict__ part, float* __restrict__ out) {\n" << b2.str() << "}\n";
+            l2.source = s2.str();
+            l2.schedule = std::string(is_sum ? "sum " : "max ") + what + " pass 2 (combine " +
+                          std::to_string(chunks) + " partials, " + Gs + " interleaved groups, in fixed order)";
+            l2.grid = {static_cast<uint32_t>((outputs + W - 1) / W), 1, 1};
+            l2.block = {512, 1, 1};
+            kernel_arg pa;
+            pa.kind = arg_kind::temp;
+            pa.index = partial;
+            kernel_arg oa;
+            oa.kind = arg_kind::temp;
+            oa.index = out;
+            l2.args = {pa, oa};
+            finish_kernel(l2);
+            p_.launches.push_back(std::move(l2));
+        };
         if (inner == 1) {
             // Row reduction: one warp per output row, 8 rows per CTA.
+            // Four consecutive elements per load: leaves must be unit-stride
+            // (or broadcast) along the axis. A reduced axis followed by
+            // extent-1 dimensions can carry any stride, so check it here.
             bool vec = A % 4 == 0;
             for (int li : order) {
                 const vnode& v = r.b.nodes[static_cast<size_t>(li)];
@@ -1264,9 +1332,83 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
                     if (affine_at(v.map, r.b.lo) % 4 != 0) vec = false;
                     for (size_t d = 0; d < ax; ++d)
                         if (v.map.st[d] % 4 != 0 && S[d] > 1) vec = false;
+                } else if (sa != 0) {
+                    vec = false;
                 }
             }
             const int V = vec ? 4 : 1;
+            // Few long rows: a warp per row would leave too few CTAs to
+            // spread evenly over the SMs, so the 8 warps of a CTA share one
+            // row instead (threads stride the row, four loads in flight per
+            // leaf, then the warps combine in warp order).
+            const bool block_row = outer < 148 * 8 * 8 && A >= 2048;
+            if (block_row) {
+                // Longer rows take bigger CTAs: more, shorter waves of equal
+                // CTAs leave a smaller partial last wave.
+                threads = A >= 16384 ? 1024 : (A >= 8192 ? 512 : 256);
+                const int64_t step = static_cast<int64_t>(threads) * V;
+                const int warps = threads / 32;
+                body << "    __shared__ float red[" << warps << "];\n";
+                body << "    const pb_u32 warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;\n";
+                body << "    const " << I << " row = (" << I << ")blockIdx.x;\n";
+                body << "    " << I << " t = row;\n";
+                for (int d = static_cast<int>(ax) - 1; d >= 0; --d) {
+                    body << "    const " << I << " c" << d << " = t % " << lit(S[static_cast<size_t>(d)], wide)
+                         << "; t /= " << lit(S[static_cast<size_t>(d)], wide) << ";\n";
+                }
+                for (int d = static_cast<int>(ax) + 1; d < R; ++d) body << "    const " << I << " c" << d << " = 0;\n";
+                const char* comps[4] = {"x", "y", "z", "w"};
+                // Loads of the leaves at row offset `kexpr` into x<u>_<leaf>.
+                auto loads = [&](const std::string& kexpr, const std::string& u, const std::string& ind) {
+                    body << ind << "const " << I << " c" << ax << "_" << u << " = " << kexpr << ";\n";
+                    std::vector<std::string> cv = cvar;
+                    cv[ax] = "c" + std::to_string(ax) + "_" + u;
+                    for (size_t li = 0; li < order.size(); ++li) {
+                        const vnode& v = r.b.nodes[static_cast<size_t>(order[li])];
+                        const std::string base = "in" + std::to_string(v.buffer);
+                        const std::string addr = address(v.map, cv, wide, -1);
+                        const std::string nm = "x" + u + "_" + std::to_string(li);
+                        if (V == 4 && v.map.st[ax] == 1)
+                            body << ind << "const float4 " << nm << " = pb_ld4(" << base << " + " << addr << ");\n";
+                        else if (V == 4)
+                            body << ind << "const float " << nm << "s = pb_ld(" << base << " + " << addr
+                                 << "); const float4 " << nm << " = make_float4(" << nm << "s, " << nm << "s, " << nm
+                                 << "s, " << nm << "s);\n";
+                        else
+                            body << ind << "const float " << nm << " = pb_ld(" << base << " + " << addr << ");\n";
+                    }
+                };
+                auto fold = [&](const std::string& u, const std::string& ind) {
+                    for (int e = 0; e < V; ++e) {
+                        body << ind << "{ const float v = pb_e0(";
+                        for (size_t li = 0; li < order.size(); ++li)
+                            body << (li ? ", " : "") << "x" << u << "_" << li
+                                 << (V == 4 ? std::string(".") + comps[e] : "");
+                        body << "); " << combine("acc", "v") << " }\n";
+                    }
+                };
+                body << "    float acc = " << init << ";\n";
+                body << "    " << I << " k = threadIdx.x * " << V << "u;\n";
+                body << "    for (; k + " << 3 * step << "u < " << lit(A, wide) << "; k += " << 4 * step << "u) {\n";
+                for (int u = 0; u < 4; ++u)
+                    loads("k + " + std::to_string(u * step) + "u", std::to_string(u), "        ");
+                for (int u = 0; u < 4; ++u) fold(std::to_string(u), "        ");
+                body << "    }\n";
+                body << "    for (; k < " << lit(A, wide) << "; k += " << step << "u) {\n";
+                loads("k", "0", "        ");
+                fold("0", "        ");
+                body << "    }\n";
+                body << "    #pragma unroll\n    for (int o = 16; o > 0; o >>= 1) { const float v = "
+                        "__shfl_xor_sync(0xffffffffu, acc, o); "
+                     << combine("acc", "v") << " }\n";
+                body << "    if (lane == 0) red[warp] = acc;\n    __syncthreads();\n";
+                body << "    if (threadIdx.x == 0) {\n        float s2 = red[0];\n";
+                body << "        #pragma unroll\n        for (int w = 1; w < " << warps << "; ++w) { const float v = red[w]; "
+                     << combine("s2", "v") << " }\n        out[row] = s2;\n    }\n";
+                l.grid = {static_cast<uint32_t>(outer), 1, 1};
+                desc = "row reduction (CTA of " + std::to_string(threads) + " per row, 4 loads in flight) V=" +
+                       std::to_string(V);
+            } else {
             body << "    const pb_u32 warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;\n";
             body << "    const " << I << " row = (" << I << ")blockIdx.x * 8u + warp;\n";
             body << "    if (row >= " << lit(outer, wide) << ") return;\n";
@@ -1311,6 +1453,109 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
             const int64_t ctas = (outer + 7) / 8;
             l.grid = {static_cast<uint32_t>(ctas), 1, 1};
             desc = "row reduction (warp per row) V=" + std::to_string(V);
+            }
+        } else if (R == 2 && ax == 0 && S[1] % 4 == 0 && S[1] >= 64 && [&] {
+                       for (int li : order) {
+                           const vnode& v = r.b.nodes[static_cast<size_t>(li)];
+                           const int64_t sc = v.map.st[1];
+                           if (sc == 1 && (affine_at(v.map, r.b.lo) % 4 != 0 || v.map.st[0] % 4 != 0)) return false;
+                           if (sc != 0 && sc != 1) return false;
+                       }
+                       return true;
+                   }()) {
+            // Column reduction of a [A, C] operand whose rows are unit-stride
+            // and 16-byte aligned: column tiles of 128 (a float4 per lane);
+            // the 8 warps of a CTA take every 8th row of the CTA's row chunk
+            // (eight float4 loads in flight per lane), then combine their
+            // partials in warp order through shared memory. Row chunks fill
+            // the GPU as in the strided form; chunk partials are combined in
+            // chunk order, so results do not depend on scheduling.
+            const int64_t C = S[1];
+            const int64_t col_tiles = (C + 127) / 128;
+            // Four CTAs per SM already keep 128 KB of loads in flight per SM;
+            // more row chunks would only lengthen pass 2.
+            const int64_t target = 148 * 4;
+            int64_t chunks = std::max<int64_t>(1, std::min<int64_t>((target + col_tiles - 1) / col_tiles, A / 64));
+            const int64_t per = (A + chunks - 1) / chunks;
+            chunks = (A + per - 1) / per;
+            const int part = chunks > 1 ? new_temp(static_cast<size_t>(chunks * C) * sizeof(float)) : out;
+            const bool pwide = wide || chunks * C >= (int64_t{1} << 31) - 4096;
+            const std::string PI = pwide ? "pb_u64" : "pb_u32";
+            const char* comps[4] = {"x", "y", "z", "w"};
+            auto combine4 = [&](std::ostringstream& os, const std::string& acc, const std::string& v,
+                                const std::string& ind) {
+                for (int e = 0; e < 4; ++e)
+                    os << ind << combine(acc + "." + comps[e], v + "." + comps[e]) << "\n";
+            };
+            auto value4 = [&](std::ostringstream& os, const std::string& k, const std::string& dst,
+                              const std::string& ind) {
+                os << ind << "{\n" << ind << "    const " << I << " c0 = " << k << ";\n";
+                for (size_t li = 0; li < order.size(); ++li) {
+                    const vnode& v = r.b.nodes[static_cast<size_t>(order[li])];
+                    const std::string addr = address(v.map, cvar, wide, -1);
+                    if (v.map.st[1] == 1)
+                        os << ind << "    const float4 x" << li << " = pb_ld4(in" << v.buffer << " + " << addr << ");\n";
+                    else
+                        os << ind << "    const float s" << li << " = pb_ld(in" << v.buffer << " + " << addr
+                           << "); const float4 x" << li << " = make_float4(s" << li << ", s" << li << ", s" << li
+                           << ", s" << li << ");\n";
+                }
+                for (int e = 0; e < 4; ++e) {
+                    os << ind << "    " << dst << "." << comps[e] << " = pb_e0(";
+                    for (size_t li = 0; li < order.size(); ++li) os << (li ? ", " : "") << "x" << li << "." << comps[e];
+                    os << ");\n";
+                }
+                os << ind << "}\n";
+            };
+            std::ostringstream b1;
+            b1 << "    __shared__ float4 red[8][32];\n";
+            b1 << "    const pb_u32 warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;\n";
+            b1 << "    const " << I << " c1 = (" << I << ")blockIdx.x * 128u + lane * 4u;\n";
+            b1 << "    const bool active = c1 < " << lit(C, wide) << ";\n";
+            b1 << "    const " << I << " k0 = (" << I << ")blockIdx.y * " << lit(per, wide) << ";\n";
+            b1 << "    const " << I << " k1 = k0 + " << lit(per, wide) << " < " << lit(A, wide) << " ? k0 + "
+               << lit(per, wide) << " : " << lit(A, wide) << ";\n";
+            b1 << "    float4 acc = make_float4(" << init << ", " << init << ", " << init << ", " << init << ");\n";
+            b1 << "    if (active) {\n";
+            b1 << "        " << I << " k = k0 + warp;\n";
+            b1 << "        for (; k + 56u < k1; k += 64u) {\n            float4 vv[8];\n";
+            b1 << "            #pragma unroll\n            for (int u = 0; u < 8; ++u)\n";
+            value4(b1, "k + 8u * (" + I + ")u", "vv[u]", "            ");
+            b1 << "            #pragma unroll\n            for (int u = 0; u < 8; ++u) {\n";
+            combine4(b1, "acc", "vv[u]", "                ");
+            b1 << "            }\n        }\n";
+            b1 << "        for (; k < k1; k += 8u) {\n            float4 v;\n";
+            value4(b1, "k", "v", "            ");
+            combine4(b1, "acc", "v", "            ");
+            b1 << "        }\n    }\n";
+            b1 << "    red[warp][lane] = acc;\n    __syncthreads();\n";
+            b1 << "    if (warp == 0 && active) {\n";
+            b1 << "        float4 s = red[0][lane];\n";
+            b1 << "        #pragma unroll\n        for (int w = 1; w < 8; ++w) {\n            const float4 v = red[w][lane];\n";
+            combine4(b1, "s", "v", "            ");
+            b1 << "        }\n";
+            b1 << "        pb_st4(" << (chunks > 1 ? "part" : "out") << " + (" << PI << ")blockIdx.y * " << lit(C, pwide)
+               << " + (" << PI << ")c1, s);\n    }\n";
+            launch_spec l1;
+            l1.name = "pb_reduce_cols_" + hex64(hash_string(src.str() + b1.str())).substr(0, 8);
+            std::ostringstream s1;
+            s1 << src.str() << "extern \"C\" __global__ void __launch_bounds__(256) " << l1.name << "(";
+            for (size_t i = 0; i < r.k.leaves.size(); ++i) s1 << "const float* __restrict__ in" << i << ", ";
+            s1 << "float* __restrict__ " << (chunks > 1 ? "part" : "out") << ") {\n" << b1.str() << "}\n";
+            l1.source = s1.str();
+            l1.schedule = std::string(is_sum ? "sum " : "max ") + "column reduction (128-column tiles, 8 warps on " +
+                          "interleaved rows, " + std::to_string(chunks) + " row chunks of " + std::to_string(per) + ")";
+            l1.grid = {static_cast<uint32_t>(col_tiles), static_cast<uint32_t>(chunks), 1};
+            l1.block = {256, 1, 1};
+            l1.args = r.k.leaves;
+            kernel_arg pa;
+            pa.kind = arg_kind::temp;
+            pa.index = part;
+            l1.args.push_back(pa);
+            finish_kernel(l1);
+            p_.launches.push_back(std::move(l1));
+            if (chunks > 1) emit_chunk_combine(part, chunks, "column reduction");
+            return out;
         } else {
             // Strided reduction: one thread per output, coalesced across the
             // inner dimensions. When the outputs alone give too few CTAs to
@@ -1363,37 +1608,7 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
                 finish_kernel(l1);
                 p_.launches.push_back(std::move(l1));
 
-                std::ostringstream b2;
-                b2 << "    const " << PI << " o = (" << PI << ")blockIdx.x * 256u + threadIdx.x;\n";
-                b2 << "    if (o >= " << lit(outputs, pwide) << ") return;\n";
-                b2 << "    float acc = part[o];\n";
-                b2 << "    " << PI << " c = 1;\n";
-                b2 << "    for (; c + 8u <= " << lit(chunks, pwide) << "; c += 8u) {\n        float vv[8];\n";
-                b2 << "        #pragma unroll\n        for (int u = 0; u < 8; ++u) vv[u] = part[(c + (" << PI
-                   << ")u) * " << lit(outputs, pwide) << " + o];\n";
-                b2 << "        #pragma unroll\n        for (int u = 0; u < 8; ++u) { const float v = vv[u]; "
-                   << combine("acc", "v") << " }\n    }\n";
-                b2 << "    for (; c < " << lit(chunks, pwide) << "; ++c) {\n";
-                b2 << "        const float v = part[c * " << lit(outputs, pwide) << " + o]; " << combine("acc", "v")
-                   << "\n    }\n";
-                b2 << "    out[o] = acc;\n";
-                launch_spec l2;
-                l2.name = "pb_reduce_comb_" + hex64(hash_string(b2.str())).substr(0, 8);
-                std::ostringstream s2;
-                s2 << kernel_prelude() << "extern \"C\" __global__ void __launch_bounds__(256) " << l2.name
-                   << "(const float* __restrict__ part, float* __restrict__ out) {\n" << b2.str() << "}\n";
-                l2.source = s2.str();
-                l2.schedule = std::string(is_sum ? "sum " : "max ") + "strided reduction pass 2 (combine " +
-                              std::to_string(chunks) + " partials in order)";
-                l2.grid = {static_cast<uint32_t>(col_ctas), 1, 1};
-                l2.block = {256, 1, 1};
-                l2.args = {pa};
-                kernel_arg oa;
-                oa.kind = arg_kind::temp;
-                oa.index = out;
-                l2.args.push_back(oa);
-                finish_kernel(l2);
-                p_.launches.push_back(std::move(l2));
+                emit_chunk_combine(partial, chunks, "strided reduction");
                 return out;
             }
             body << "    const " << I << " o = (" << I << ")blockIdx.x * 256u + threadIdx.x;\n";
@@ -1412,12 +1627,12 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
             desc = "strided reduction (thread per output)";
         }
         l.name = "pb_reduce_" + hex64(hash_string(src.str() + body.str())).substr(0, 8);
-        src << "extern \"C\" __global__ void __launch_bounds__(256) " << l.name << "(";
+        src << "extern \"C\" __global__ void __launch_bounds__(" << threads << ") " << l.name << "(";
         for (size_t i = 0; i < r.k.leaves.size(); ++i) src << "const float* __restrict__ in" << i << ", ";
         src << "float* __restrict__ out) {\n" << body.str() << "}\n";
         l.source = src.str();
         l.schedule = std::string(is_sum ? "sum " : "max ") + desc;
-        l.block = {256, 1, 1};
+        l.block = {static_cast<uint32_t>(threads), 1, 1};
         l.args = r.k.leaves;
         kernel_arg o;
         o.kind = arg_kind::temp;
@@ -1453,6 +1668,8 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
                 if (affine_at(v.map, r.b.lo) % 4 != 0) vec = false;
                 for (size_t d = 0; d < ax; ++d)
                     if (v.map.st[d] % 4 != 0 && S[d] > 1) vec = false;
+            } else if (v.map.st[ax] != 0) {
+                vec = false;  // strided along the axis (trailing extent-1 dimensions)
             }
         }
         const int V = vec ? 4 : 1;

@@ -240,7 +240,10 @@ def random_program(seed: int, integer_values: bool = True, depth: int = 4, large
     shape = g.rand_shape()
     root = g.expr(shape, depth)
     if rng.random() < 0.15 and len(shape) >= 1:
-        root = g.emit(f"softmax {root} {len(shape) - 1}")
+        # Mostly the last axis (the row kernel); otherwise any axis (the
+        # pattern then lowers as reductions plus an elementwise pass).
+        ax = len(shape) - 1 if rng.random() < 0.6 else rng.randrange(len(shape))
+        root = g.emit(f"softmax {root} {ax}")
         g.has_inexact = True
     text = "\n".join(g.lines) + "\n"
     return text, g.inputs, not g.has_inexact

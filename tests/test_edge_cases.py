@@ -12,7 +12,7 @@ import numpy as np
 import pytest
 
 import graphs
-from tolerances import assert_bitwise, assert_relative
+from tolerances import assert_bitwise, assert_relative, assert_sum_close
 
 ZERO_SIZE = [
     ("0 input 0\n1 exp 0\n", [[0, 5]]),
@@ -180,3 +180,83 @@ def test_graph_reading_many_distinct_tensors(gpu):
     for a in arrays:
         want = (want + a).astype(np.float32)
     assert_bitwise(got, want, "300-input sum")
+
+
+# A reduced axis followed by extent-1 dimensions can have any stride (the
+# row-vectorised loads need unit stride), and a softmax over an axis other
+# than the last lowers as its two reductions and an elementwise pass
+# (reference: src/ops.cpp:7-14 builds softmax from max, exp, sum, divide).
+STRIDED_AXIS = [
+    ("0 input 0\n1 transpose 0\n2 reshape 1 4,100,1\n3 sum 2 1 0\n", [[100, 4]]),
+    ("0 input 0\n1 transpose 0\n2 reshape 1 8,64,1\n3 max 2 1 1\n", [[64, 8]]),
+    ("0 input 0\n1 softmax 0 1\n", [[4, 100, 3]]),
+    ("0 input 0\n1 transpose 0\n2 reshape 1 4,100,1\n3 softmax 2 1\n", [[100, 4]]),
+    ("0 input 0\n1 softmax 0 0\n", [[64, 8]]),
+]
+
+
+def _strided_inputs(shapes, seed):
+    rng = np.random.default_rng(seed)
+    return [rng.normal(0, 1, s).astype(np.float32) for s in shapes]
+
+
+def _numpy_of(program, x):
+    """numpy restatement of the five STRIDED_AXIS programs."""
+    x = x.astype(np.float64)
+    lines = program.strip().splitlines()
+    last = lines[-1].split()
+    if "transpose" in program:
+        x = x.T.reshape([int(d) for d in lines[2].split()[3].split(",")])
+    axis = int(last[3])
+    if last[1] == "sum":
+        return x.sum(axis=axis, keepdims=last[4] == "1")
+    if last[1] == "max":
+        return x.max(axis=axis, keepdims=last[4] == "1")
+    e = np.exp(x - x.max(axis=axis, keepdims=True))
+    return e / e.sum(axis=axis, keepdims=True)
+
+
+@pytest.mark.parametrize("case", range(len(STRIDED_AXIS)))
+def test_oracle_strided_axis_and_inner_softmax(oracle_lib, case):
+    program, shapes = STRIDED_AXIS[case]
+    ins = _strided_inputs(shapes, 5)
+    got = graphs.evaluate_oracle(program, ins)
+    want = _numpy_of(program, ins[0])
+    if " sum " in program:
+        abs_sum = np.abs(ins[0].astype(np.float64)).T.reshape(4, 100, 1).sum(axis=1)
+        assert_sum_close(got, want, abs_sum, 100, 1e-5, program)
+    else:
+        assert_relative(got, want.astype(np.float32), 1e-5, program)
+
+
+@pytest.mark.parametrize("case", range(len(STRIDED_AXIS)))
+def test_strided_axis_plans(api, case):
+    """Plans on placeholders: no softmax row kernel for an inner axis, and no
+    four-wide loads along a strided reduced axis."""
+    program, shapes = STRIDED_AXIS[case]
+    orig = api.tensor
+    try:
+        api.tensor = lambda s, values, device=0: api.placeholder(list(s))
+        e = graphs.build(api, program, [np.zeros(sh, np.float32) for sh in shapes])
+    finally:
+        api.tensor = orig
+    kernels = [line for line in api.describe(e).splitlines() if line.startswith("kernel ")]
+    assert kernels and not any("softmax row kernel" in k for k in kernels), kernels
+    if "transpose" in program:
+        assert not any("row reduction" in k and "V=4" in k for k in kernels), kernels
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("case", range(len(STRIDED_AXIS)))
+def test_strided_axis_and_inner_softmax_match_oracle(gpu, case):
+    program, shapes = STRIDED_AXIS[case]
+    ins = _strided_inputs(shapes, 6)
+    want = graphs.evaluate_oracle(program, ins)
+    got = graphs.evaluate_product(gpu, program, ins)
+    if " max " in program:
+        assert_bitwise(got, want, program)
+    elif " sum " in program:
+        x = np.abs(ins[0].astype(np.float64)).T.reshape(4, 100, 1)
+        assert_sum_close(got, want, x.sum(axis=1), 100, 1e-5, program)
+    else:
+        assert_relative(got, want, 1e-5, program)

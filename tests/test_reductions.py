@@ -3,7 +3,9 @@
 
 A reduction whose outputs alone give too few CTAs to fill the GPU (a tall
 tensor reduced over axis 0) is split into row chunks: pass 1 writes one
-partial per (chunk, output), pass 2 combines them in chunk order.
+partial per (chunk, output), pass 2 combines them in a fixed order. A 2-D
+operand with unit-stride rows of at least 64 columns (a multiple of 4) is
+read in 128-column tiles, a float4 per lane, eight rows in flight per warp.
 CPU: the plans. GPU: parity with the host oracle (max bit for bit -- the
 maximum does not depend on the order -- sum within the reduction tolerance).
 """
@@ -23,6 +25,19 @@ CASES = [
     ([64, 4096, 8], 1, False, "sum", None),
     ([3, 1000, 5], 1, True, "max", None),
     ([8, 8], 0, False, "sum", None),
+    # Column tiles (unit-stride rows of >= 64 columns, a multiple of 4):
+    ([262144, 256], 0, False, "sum", None),
+    ([1000, 260], 0, False, "sum", "exp"),
+    ([1003, 128], 0, True, "max", None),
+    ([64, 128], 0, False, "max", "relu"),
+    # Narrow or transposed columns keep the thread-per-output form:
+    ([100000, 4], 0, False, "sum", None),
+    ([300, 8], 0, False, "max", None),
+    ([2048, 384], 0, False, "sum", "transpose"),
+    # Few long rows: a CTA per row (8 warps share it).
+    ([4096, 16384], 1, False, "sum", None),
+    ([300, 2049], 1, False, "max", "exp"),
+    ([4, 50, 3000], 2, True, "sum", "relu"),
 ]
 
 
@@ -34,6 +49,16 @@ def _program(shape, axis, keepdim, op, prologue):
         src = 1
     lines.append(f"{len(lines)} {op} {src} {axis} {int(keepdim)}")
     return "\n".join(lines) + "\n"
+
+
+def _host_prologue(x, prologue):
+    if prologue == "exp":
+        return np.exp(x)
+    if prologue == "relu":
+        return np.maximum(x, 0)
+    if prologue == "transpose":
+        return x.T
+    return x
 
 
 def _inputs(shape, seed):
@@ -55,7 +80,30 @@ def test_tall_leading_axis_reduction_plans_two_passes(api):
     plan = api.describe(e)
     kernels = [line for line in plan.splitlines() if line.startswith("kernel ")]
     assert len(kernels) == 2, plan
-    assert "pass 1" in kernels[0] and "pass 2" in kernels[1], plan
+    assert "column reduction (128-column tiles" in kernels[0] and "pass 2" in kernels[1], plan
+    e = _placeholder_expr(api, _program([100000, 4], 0, False, "sum", None), [100000, 4])
+    kernels = [line for line in api.describe(e).splitlines() if line.startswith("kernel ")]
+    assert len(kernels) == 2 and "pass 1" in kernels[0] and "pass 2" in kernels[1], kernels
+
+
+def test_unit_stride_columns_plan_column_tiles(api):
+    e = _placeholder_expr(api, _program([262144, 256], 0, False, "sum", None), [262144, 256])
+    kernels = [line for line in api.describe(e).splitlines() if line.startswith("kernel ")]
+    assert len(kernels) == 2 and "column reduction (128-column tiles" in kernels[0], kernels
+    assert "pass 2" in kernels[1] and "fixed order" in kernels[1], kernels
+    # A transposed operand has strided columns: thread per output instead.
+    e = _placeholder_expr(api, _program([2048, 384], 0, False, "sum", "transpose"), [2048, 384])
+    kernels = [line for line in api.describe(e).splitlines() if line.startswith("kernel ")]
+    assert "strided reduction" in kernels[0], kernels
+
+
+def test_few_long_rows_plan_a_cta_per_row(api):
+    e = _placeholder_expr(api, _program([4096, 16384], 1, False, "sum", None), [4096, 16384])
+    kernels = [line for line in api.describe(e).splitlines() if line.startswith("kernel ")]
+    assert len(kernels) == 1 and "per row" in kernels[0] and "CTA of 1024" in kernels[0] and "V=4" in kernels[0], kernels
+    e = _placeholder_expr(api, _program([65536, 1024], 1, False, "sum", None), [65536, 1024])
+    kernels = [line for line in api.describe(e).splitlines() if line.startswith("kernel ")]
+    assert "warp per row" in kernels[0], kernels
 
 
 def test_wide_row_reduction_stays_one_pass(api):
@@ -71,14 +119,10 @@ def test_oracle_reductions_match_numpy(oracle_lib, case):
         pytest.skip("large case: GPU test only")
     ins = _inputs(shape, 3)
     got = graphs.evaluate_oracle(_program(shape, axis, keepdim, op, prologue), ins)
-    x = ins[0].astype(np.float64)
-    if prologue == "exp":
-        x = np.exp(x)
-    elif prologue == "relu":
-        x = np.maximum(x, 0)
+    x = _host_prologue(ins[0].astype(np.float64), prologue)
     if op == "sum":
         assert_sum_close(got, x.sum(axis=axis, keepdims=keepdim), np.abs(x).sum(axis=axis, keepdims=keepdim),
-                         shape[axis], REL_TOL, str(case))
+                         x.shape[axis], REL_TOL, str(case))
     else:
         assert_relative(got, x.max(axis=axis, keepdims=keepdim).astype(np.float32), REL_TOL, str(case))
 
@@ -96,7 +140,6 @@ def test_cuda_reductions_match_oracle(gpu, case):
     elif op == "max":
         assert_relative(got, want, REL_TOL, str(case))
     else:
-        x = ins[0].astype(np.float64)
-        x = np.exp(x) if prologue == "exp" else (np.maximum(x, 0) if prologue == "relu" else x)
+        x = _host_prologue(ins[0].astype(np.float64), prologue)
         abs_sum = np.abs(x).sum(axis=axis, keepdims=keepdim)
-        assert_sum_close(got, want, abs_sum, shape[axis], REL_TOL, str(case))
+        assert_sum_close(got, want, abs_sum, x.shape[axis], REL_TOL, str(case))
