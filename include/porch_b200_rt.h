@@ -88,6 +88,14 @@ int pbrt_stream_wait_event(int device, pbrt_stream stream, pbrt_event event);
 int pbrt_mem_alloc_async(int device, size_t bytes, pbrt_stream stream,
                          uint64_t* pointer);
 int pbrt_mem_free_async(int device, uint64_t pointer, pbrt_stream stream);
+/* Plain allocation (cuMemAlloc), usable on any stream at once. Growing the
+ * stream-ordered pool can block the calling thread until the stream's queued
+ * work drains (measured: up to 116 ms for 64 MB behind a busy GEMM queue),
+ * so the library's caching allocator takes its blocks from here. The free
+ * waits for all work on the device (cuMemFree), so it is used only when the
+ * cache is trimmed. */
+int pbrt_mem_alloc(int device, size_t bytes, uint64_t* pointer);
+int pbrt_mem_free(int device, uint64_t pointer);
 int pbrt_host_alloc(size_t bytes, void** pointer); /* page-locked */
 int pbrt_host_free(void* pointer);
 int pbrt_memcpy_h2d_async(int device, uint64_t dst, const void* src,

@@ -191,10 +191,14 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
         if (M > (int64_t{1} << 30) || N > (int64_t{1} << 30) || K > (int64_t{1} << 30)) return -1;
         rank_ = 2;
 
-        const int a_hi = new_temp(static_cast<size_t>(M * K) * 4);
-        const int a_lo = new_temp(static_cast<size_t>(M * K) * 4);
-        const int b_hi = new_temp(static_cast<size_t>(N * K) * 4);
-        const int b_lo = new_temp(static_cast<size_t>(N * K) * 4);
+        // The K-major hi/lo arrays have rows of Kp = K rounded up to 32
+        // (zeros past K), so every row starts on a 128-byte line and the
+        // TMA boxes (64-byte rows) never straddle one.
+        const int64_t Kp = (K + 31) / 32 * 32;
+        const int a_hi = new_temp(static_cast<size_t>(M * Kp) * 4);
+        const int a_lo = new_temp(static_cast<size_t>(M * Kp) * 4);
+        const int b_hi = new_temp(static_cast<size_t>(N * Kp) * 4);
+        const int b_lo = new_temp(static_cast<size_t>(N * Kp) * 4);
         const int out = new_temp(static_cast<size_t>(M * N) * 4);
         // Set by the split kernels when an operand holds Inf or NaN; the
         // tensor-core kernels then leave the output to the CUDA-core GEMM
@@ -222,14 +226,21 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
 
         // ---- 1. split A rows (contiguous, float4) --------------------------
         {
-            const int64_t n4 = M * K / 4;
+            const int64_t n4 = M * Kp / 4;
             std::ostringstream src;
             src << kernel_prelude() << gemm_device_source();
             src << "extern \"C\" __global__ void __launch_bounds__(256) pb_split_rows(const float* __restrict__ x, "
                    "float* __restrict__ hi, float* __restrict__ lo, int* __restrict__ nf) {\n"
                 << "    for (pb_u64 i = (pb_u64)blockIdx.x * 256u + threadIdx.x; i < " << n4
-                << "ull; i += (pb_u64)gridDim.x * 256u) {\n"
-                << "        const float4 v = pb_ld4(x + 4 * i);\n"
+                << "ull; i += (pb_u64)gridDim.x * 256u) {\n";
+            if (Kp == K) {
+                src << "        const float4 v = pb_ld4(x + 4 * i);\n";
+            } else {
+                src << "        const pb_u64 r = i / " << Kp / 4 << "ull, c = i % " << Kp / 4 << "ull;\n"
+                    << "        const float4 v = c < " << K / 4 << "ull ? pb_ld4(x + r * " << K
+                    << "ull + 4 * c) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);\n";
+            }
+            src
                 << "        if (!(isfinite(v.x) && isfinite(v.y) && isfinite(v.z) && isfinite(v.w))) atomicOr(nf, 1);\n"
                 << "        float4 h, l;\n"
                 << "        h.x = pb_tf32_hi(v.x); l.x = pb_tf32_rn(v.x - h.x);\n"
@@ -261,17 +272,17 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
                 << "    __syncthreads();\n"
                 << "    #pragma unroll\n    for (int u = 0; u < 16; ++u) {\n"
                 << "        const pb_u32 r = threadIdx.x / 64u + 4u * u, c = threadIdx.x % 64u;\n"
-                << "        if (n0 + r >= " << N << "ull || k0 + c >= " << K << "ull) continue;\n"
+                << "        if (n0 + r >= " << N << "ull || k0 + c >= " << Kp << "ull) continue;\n"
                 << "        const float v = t[c][r];\n"
                 << "        if (!isfinite(v)) atomicOr(nf, 1);\n"
                 << "        const float h = pb_tf32_hi(v);\n"
-                << "        const pb_u64 o = (n0 + r) * " << K << "ull + k0 + c;\n"
+                << "        const pb_u64 o = (n0 + r) * " << Kp << "ull + k0 + c;\n"
                 << "        hi[o] = h;\n        lo[o] = pb_tf32_rn(v - h);\n    }\n}\n";
             launch_spec l;
             l.name = "pb_split_transpose";
             l.source = src.str();
             l.schedule = "3xTF32 split of B with transpose to K-major";
-            l.grid = {static_cast<uint32_t>((N + 63) / 64), static_cast<uint32_t>((K + 63) / 64), 1};
+            l.grid = {static_cast<uint32_t>((N + 63) / 64), static_cast<uint32_t>((Kp + 63) / 64), 1};
             l.args = {B, temp_arg(b_hi), temp_arg(b_lo), temp_arg(nf)};
             finish_kernel(l);
             p_.launches.push_back(std::move(l));
@@ -289,17 +300,16 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
         // sqrt(K) / 2 k-blocks keeps ours about half the chain's at every K
         // (measured: one accumulator over 8192 of K drifts 5x the chain, a
         // period over all of K = 512 almost 5x). Capped at 32 (draining
-        // costs a few percent per launch at 8), a power of two, at least 4;
-        // the k-blocks are padded to a whole number of periods (past K the
-        // TMA loads read zeros, which add exactly nothing).
+        // costs a few percent per launch at 8), a power of two, at least 4.
+        // A tile's last period may be shorter (it then drifts less).
         int period = 4;
         while (period < 32 && static_cast<double>(period * 2) <= std::sqrt(static_cast<double>(K)) / 2.0)
             period *= 2;
-        const int64_t num_kb = (raw_kb + period - 1) / period * period;
         // Split-K when the tiles leave most SMs idle (fewer tiles than half
         // of 148 SMs: a short batch, a thin row block): S K-ranges per tile
-        // (a power of two up to 16, each a whole number of periods and at
-        // least 256 of K), S chosen to fill whole waves best. Each unit
+        // (a power of two up to 16, each at least 256 of K; the k-blocks
+        // are padded to a multiple of S, past K the TMA loads read zeros,
+        // which add exactly nothing), S chosen to fill whole waves best. Each unit
         // writes its raw partial tile; a second kernel sums the S partials
         // in split order and applies the fused epilogue. Measured on one
         // box: 16 tiles (128 x 4096 x 4096) 2.9x faster with S = 8; at 128
@@ -310,7 +320,7 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
         if (tiles < 74) {
             double best = static_cast<double>(tiles) / 148.0;
             for (int64_t s = 2; s <= 16; s *= 2) {
-                if (num_kb % (s * period) != 0 || num_kb / s < 16) break;
+                if (raw_kb / s < 16) break;
                 const int64_t u = tiles * s;
                 const double eff = static_cast<double>(u) / (148.0 * static_cast<double>((u + 147) / 148));
                 if (eff > best + 1e-9) {
@@ -319,7 +329,7 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
                 }
             }
         }
-        const int64_t kb_unit = num_kb / split;
+        const int64_t kb_unit = (raw_kb + split - 1) / split;
         const int64_t units = tiles * split;
         const int part = split > 1 ? new_temp(static_cast<size_t>(split * M * N) * 4) : -1;
         std::ostringstream src;
@@ -374,7 +384,7 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
              << "    asm volatile(\"tcgen05.fence::after_thread_sync;\" ::: \"memory\");\n"
              << "    const pb_u32 tmem = tmem_slot;\n"
              << "    const int num_kb = " << kb_unit << ";  // k-blocks per work unit\n"
-             << "    const int periods = num_kb / PB_PERIOD;\n"
+             << "    const int periods = (num_kb + PB_PERIOD - 1) / PB_PERIOD;  // the last may be partial\n"
              << "    if (warp == 8) {\n"
              << "        if (lane == 0) {\n"
              // producer
@@ -407,13 +417,13 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
              // tile) accumulates from zero into TMEM buffer p % 2 (columns
              // 256 (p % 2)..+255); before reusing a buffer it waits for the
              // drain of period p - 2.
-             << "            int g = 0;\n"
+             << "            int g = 0, per_base = 0;\n"
              << "            bool stop = false;\n"
-             << "            for (pb_u32 t = blockIdx.x; t < tiles && !stop; t += gridDim.x) {\n"
+             << "            for (pb_u32 t = blockIdx.x; t < tiles && !stop; t += gridDim.x, per_base += periods) {\n"
              << "                for (int kb = 0; kb < num_kb; ++kb, ++g) {\n"
              << "                    const int s = g % PB_STAGES;\n"
              << "                    const pb_u32 phase = (pb_u32)(g / PB_STAGES) & 1u;\n"
-             << "                    const int per = g / PB_PERIOD, pos = g % PB_PERIOD;\n"
+             << "                    const int per = per_base + kb / PB_PERIOD, pos = kb % PB_PERIOD;\n"
              << "                    const pb_u32 buf = (pb_u32)per & 1u;\n"
              << "                    if (pos == 0 && per >= 2) {\n"
              << "                        if (!pb_wait(pb_smem(&acce[buf]), (pb_u32)((per >> 1) - 1) & 1u, &abort_flag, err, 6)) { stop = true; break; }\n"
@@ -435,7 +445,7 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
              << "                        pb_mma(d, alo, bhi, 1u);\n"
              << "                    }\n"
              << "                    pb_commit(pb_smem(&empty_bar[s]));\n"
-             << "                    if (pos == PB_PERIOD - 1) pb_commit(pb_smem(&accf[buf]));\n"
+             << "                    if (pos == PB_PERIOD - 1 || kb == num_kb - 1) pb_commit(pb_smem(&accf[buf]));\n"
              << "                }\n"
              << "            }\n"
              // Whether or not the loops finished: completes once every MMA
@@ -618,7 +628,7 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
             a.kind = arg_kind::tmap;
             a.index = temp;
             a.value = static_cast<uint64_t>(rows);
-            a.cols = K;
+            a.cols = Kp;
             a.box_rows = box_rows;
             a.box_cols = kBK;
             a.swizzle = 2; // 64B: the box's 16-fp32 inner extent is one swizzle row

@@ -158,14 +158,16 @@ namespace porch::detail {
             bytes = dc.cached_bytes;
             dc.cached_bytes = 0;
         }
+        // Blocks come from cuMemAlloc; cuMemFree waits for the device's
+        // queued work, so no block is freed under a running kernel.
         for (auto& [size, list] : drop)
-            for (auto& b : list) (void)pbrt_mem_free_async(device, b.ptr, b.stream->stream);
+            for (auto& b : list) (void)pbrt_mem_free(device, b.ptr);
         for (auto& p : waiting) {
             for (const auto& [dev, ev] : p.events) {
                 (void)pbrt_event_synchronize(dev, ev);
                 (void)pbrt_event_destroy(dev, ev);
             }
-            (void)pbrt_mem_free_async(device, p.ptr, p.stream->stream);
+            (void)pbrt_mem_free(device, p.ptr);
             bytes += p.capacity;
         }
         return bytes;
@@ -206,9 +208,9 @@ namespace porch::detail {
             }
             host_count(state->ptr ? "alloc_cache_hit" : "alloc_cache_miss");
             if (state->ptr == 0) {
-                int st = pbrt_mem_alloc_async(device, cls, stream->stream, &state->ptr);
+                int st = pbrt_mem_alloc(device, cls, &state->ptr);
                 if (st != PBRT_OK && release_cached_blocks(device) != 0)
-                    st = pbrt_mem_alloc_async(device, cls, stream->stream, &state->ptr);
+                    st = pbrt_mem_alloc(device, cls, &state->ptr);
                 check(st);
             }
             state->producer = stream;
@@ -296,12 +298,12 @@ namespace porch::cuda_jit {
                 detail::defer_recycle(device, ptr, capacity, std::move(free_stream), std::move(events));
                 return;
             }
-            // No events (or a block from outside the cache): drain the
-            // readers on the host, then a stream-ordered free.
+            // No events: drain the readers on the host, then free (cuMemFree
+            // also waits for the producer's queued work).
             for (const auto& [dev, ev] : events) (void)pbrt_event_destroy(dev, ev);
             for (const auto& reader : readers)
                 if (reader != free_stream) (void)pbrt_stream_synchronize(reader->device, reader->stream);
-            (void)pbrt_mem_free_async(device, ptr, free_stream->stream);
+            (void)pbrt_mem_free(device, ptr);
         } catch (...) {
         }
     }

@@ -88,6 +88,8 @@ dl_handle open_first(std::initializer_list<const char*> names) {
     X(cuEventQuery, CUresult (*)(CUevent))                                   \
     X(cuEventElapsedTime, CUresult (*)(float*, CUevent, CUevent))            \
     X(cuMemAllocAsync, CUresult (*)(CUdeviceptr*, size_t, CUstream))         \
+    X(cuMemAlloc_v2, CUresult (*)(CUdeviceptr*, size_t))                     \
+    X(cuMemFree_v2, CUresult (*)(CUdeviceptr))                               \
     X(cuMemFreeAsync, CUresult (*)(CUdeviceptr, CUstream))                   \
     X(cuDeviceGetDefaultMemPool, CUresult (*)(CUmemoryPool*, CUdevice))      \
     X(cuMemPoolSetAttribute,                                                 \
@@ -802,6 +804,25 @@ int pbrt_mem_alloc_async(int device, size_t bytes, pbrt_stream stream,
     return s;
 }
 
+int pbrt_mem_alloc(int device, size_t bytes, uint64_t* pointer) {
+    if (pointer == nullptr) return fail(PBRT_ERR_INVALID, "pointer is null");
+    environment* env = nullptr;
+    int s = use_device(device, env);
+    if (s != PBRT_OK) return s;
+    if (fault_fires(fault_alloc)) return PBRT_ERR_INJECTED;
+    CUdeviceptr p = 0;
+    s = check(*env, env->cu.cuMemAlloc_v2(&p, bytes), "cuMemAlloc");
+    *pointer = static_cast<uint64_t>(p);
+    return s;
+}
+
+int pbrt_mem_free(int device, uint64_t pointer) {
+    environment* env = nullptr;
+    int s = use_device(device, env);
+    if (s != PBRT_OK) return s;
+    return check(*env, env->cu.cuMemFree_v2(static_cast<CUdeviceptr>(pointer)), "cuMemFree");
+}
+
 int pbrt_mem_free_async(int device, uint64_t pointer, pbrt_stream stream) {
     environment* env = nullptr;
     int s = use_device(device, env);
@@ -1221,7 +1242,7 @@ int pbrt_error_word(int device, uint64_t* pointer) {
         if (s != PBRT_OK) return s;
         CUstream st = reinterpret_cast<CUstream>(ps);
         CUdeviceptr p = 0;
-        s = check(*env, env->cu.cuMemAllocAsync(&p, 64, st), "cuMemAllocAsync");
+        s = check(*env, env->cu.cuMemAlloc_v2(&p, 64), "cuMemAlloc");
         if (s != PBRT_OK) return s;
         s = check(*env, env->cu.cuMemsetD32Async(p, 0, 16, st), "cuMemsetD32Async");
         if (s != PBRT_OK) return s;

@@ -172,7 +172,10 @@ TC_SHAPES = [(512, 512, 512), (256, 1024, 768), (1024, 768, 512), (384, 512, 102
              (128, 4096, 1024), (256, 2048, 512), (128, 8192, 1024),
              # edge tiles: M, N, K not multiples of the tile (zero fill past
              # the edges, masked stores), with and without split-K
-             (1000, 520, 1004), (300, 4096, 772), (129, 4100, 260)]
+             (1000, 520, 1004), (300, 4096, 772), (129, 4100, 260),
+             # K past a multiple of 32: hi/lo rows padded with zeros to
+             # 128-byte lines, the last accumulation period of a tile short
+             (128, 4100, 4096), (2048, 2052, 2048)]
 
 
 @pytest.mark.parametrize("m,k,n", TC_SHAPES)
