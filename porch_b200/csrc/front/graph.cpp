@@ -391,6 +391,7 @@ namespace porch::detail {
                     check(pbrt_occupancy(device, fn, static_cast<int>(l.block[0] * l.block[1] * l.block[2]),
                                          l.smem, &per_sm));
                     check(pbrt_device_attribute(device, 16 /* multiprocessor count */, &sms));
+                    if (l.persistent_per_sm > 0) per_sm = std::min(per_sm, l.persistent_per_sm);
                     const int64_t fit = std::max<int64_t>(1, int64_t{per_sm} * sms);
                     pgrid = static_cast<uint32_t>(std::min<int64_t>(l.persistent_units, fit));
                 }

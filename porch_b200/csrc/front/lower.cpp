@@ -1673,9 +1673,24 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
             }
         }
         const int V = vec ? 4 : 1;
-        const int T = A >= 2048 ? 256 : (A >= 512 ? 128 : 32);
-        const int64_t NI = (A + static_cast<int64_t>(T) * V - 1) / (static_cast<int64_t>(T) * V);
+        const int T0 = A >= 2048 ? 256 : (A >= 512 ? 128 : 32);
+        const int64_t NI = (A + static_cast<int64_t>(T0) * V - 1) / (static_cast<int64_t>(T0) * V);
         const bool in_registers = NI * V <= 64;
+        // Longer rows stream twice (online max/sum, then the write). The
+        // CTAs resident at once are capped so that their rows stay in L2
+        // and the second read comes from L2, not HBM: four 256-thread CTAs
+        // per SM while their rows take at most 48 MB, three up to 64 MB
+        // (16 KB of loads in flight per CTA, and enough CTAs to hide each
+        // other's barriers), else one 1024-thread CTA per SM (64 KB of loads
+        // in flight). Measured on one box against the unlimited 256-thread
+        // grid, as fractions of one read + one write: 0.64 -> 0.83 at
+        // [8192, 16388], 0.65 -> 0.73 at [16384, 20000], 0.63 -> 0.71 at
+        // [4096, 32768], 0.62 -> 0.72 at [2048, 65536].
+        const int64_t row_bytes = A * 4;
+        const int stream_per_sm = 148 * 4 * row_bytes <= (int64_t{48} << 20)   ? 4
+                                  : 148 * 3 * row_bytes <= (int64_t{64} << 20) ? 3
+                                                                               : 1;
+        const int T = in_registers ? T0 : (stream_per_sm > 1 ? 256 : 1024);
         std::vector<std::string> cvar(static_cast<size_t>(R));
         for (int d = 0; d < R; ++d) cvar[static_cast<size_t>(d)] = "c" + std::to_string(d);
         const char* comps[4] = {"x", "y", "z", "w"};
@@ -1786,25 +1801,79 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
                 body << "                out[" << orow << " + k] = x[it][0] * rs;\n";
             body << "            }\n        }\n";
         } else {
-            // Rows too long for registers: max pass, sum pass, write pass.
+            // Rows too long for registers: an online pass keeps a running
+            // (max, sum) per thread -- four vector loads per step, the sum
+            // rescaled once per step by exp(old max - new max) -- and the
+            // block combines the pairs; a second pass writes
+            // exp(x - m) * (1 / s). Two reads and one write per element.
+            const int64_t step = static_cast<int64_t>(T) * V;
             body << "    for (" << I << " row = blockIdx.x; row < " << lit(rows, wide) << "; row += gridDim.x) {\n";
             emit_row_coords("row", "        ");
-            body << "        float m = PB_NEG_FLT_MAX;\n";
-            body << "        for (" << I << " k = threadIdx.x * " << V << "u; k < " << lit(A, wide) << "; k += "
-                 << T * V << "u) {\n            float xv[" << V << "];\n";
+            body << "        float m = PB_NEG_FLT_MAX, s = 0.0f;\n";
+            body << "        " << I << " k = threadIdx.x * " << V << "u;\n";
+            body << "        for (; k + " << 3 * step << "u < " << lit(A, wide) << "; k += " << 4 * step << "u) {\n";
+            body << "            float xv[4][" << V << "];\n";
+            for (int u = 0; u < 4; ++u)
+                emit_load("k + " + std::to_string(u * step) + "u", "xv[" + std::to_string(u) + "]", "            ");
+            body << "            float bm = m;\n";
+            body << "            #pragma unroll\n            for (int u = 0; u < 4; ++u)\n"
+                 << "                #pragma unroll\n                for (int e = 0; e < " << V
+                 << "; ++e) bm = bm > xv[u][e] ? bm : xv[u][e];\n";
+            body << "            s = s * __expf(m - bm);\n            m = bm;\n";
+            body << "            #pragma unroll\n            for (int u = 0; u < 4; ++u)\n"
+                 << "                #pragma unroll\n                for (int e = 0; e < " << V
+                 << "; ++e) s = s + __expf(xv[u][e] - m);\n";
+            body << "        }\n";
+            body << "        for (; k < " << lit(A, wide) << "; k += " << step << "u) {\n";
+            body << "            float xv[" << V << "];\n";
             emit_load("k", "xv", "            ");
-            body << "            for (int e = 0; e < " << V << "; ++e) m = m > xv[e] ? m : xv[e];\n        }\n";
-            block_reduce("m", true);
-            body << "        float s = 0.0f;\n";
-            body << "        for (" << I << " k = threadIdx.x * " << V << "u; k < " << lit(A, wide) << "; k += "
-                 << T * V << "u) {\n            float xv[" << V << "];\n";
+            body << "            float bm = m;\n";
+            body << "            #pragma unroll\n            for (int e = 0; e < " << V
+                 << "; ++e) bm = bm > xv[e] ? bm : xv[e];\n";
+            body << "            s = s * __expf(m - bm);\n            m = bm;\n";
+            body << "            #pragma unroll\n            for (int e = 0; e < " << V
+                 << "; ++e) s = s + __expf(xv[e] - m);\n";
+            body << "        }\n";
+            // Pair combine: the larger max wins, the other sum is rescaled.
+            auto pair_combine = [&](const std::string& om, const std::string& os, const std::string& ind) {
+                body << ind << "{ const float nm = m > " << om << " ? m : " << om << "; s = s * __expf(m - nm) + "
+                     << os << " * __expf(" << om << " - nm); m = nm; }\n";
+            };
+            body << "        #pragma unroll\n        for (int o = 16; o > 0; o >>= 1) {\n"
+                 << "            const float om = __shfl_xor_sync(0xffffffffu, m, o);\n"
+                 << "            const float os = __shfl_xor_sync(0xffffffffu, s, o);\n";
+            pair_combine("om", "os", "            ");
+            body << "        }\n";
+            if (T > 32) {
+                body << "        if (lane == 0) { red_m[warp] = m; red_s[warp] = s; }\n        __syncthreads();\n";
+                body << "        m = red_m[0];\n        s = red_s[0];\n";
+                body << "        #pragma unroll\n        for (int w = 1; w < " << T / 32 << "; ++w) {\n"
+                     << "            const float om = red_m[w], os = red_s[w];\n";
+                pair_combine("om", "os", "            ");
+                body << "        }\n        __syncthreads();  // red_m/red_s are rewritten by the next row\n";
+            }
+            body << "        const float rs = 1.0f / s;\n";
+            body << "        k = threadIdx.x * " << V << "u;\n";
+            body << "        for (; k + " << 3 * step << "u < " << lit(A, wide) << "; k += " << 4 * step << "u) {\n";
+            body << "            float xv[4][" << V << "];\n";
+            for (int u = 0; u < 4; ++u)
+                emit_load("k + " + std::to_string(u * step) + "u", "xv[" + std::to_string(u) + "]", "            ");
+            for (int u = 0; u < 4; ++u) {
+                const std::string kk = "k + " + std::to_string(u * step) + "u";
+                if (V == 4)
+                    body << "            pb_st4(out + " << orow << " + " << kk << ", make_float4(__expf(xv[" << u
+                         << "][0] - m) * rs, __expf(xv[" << u << "][1] - m) * rs, __expf(xv[" << u
+                         << "][2] - m) * rs, __expf(xv[" << u << "][3] - m) * rs));\n";
+                else
+                    body << "            out[" << orow << " + " << kk << "] = __expf(xv[" << u << "][0] - m) * rs;\n";
+            }
+            body << "        }\n";
+            body << "        for (; k < " << lit(A, wide) << "; k += " << step << "u) {\n";
+            body << "            float xv[" << V << "];\n";
             emit_load("k", "xv", "            ");
-            body << "            for (int e = 0; e < " << V << "; ++e) s = s + __expf(xv[e] - m);\n        }\n";
-            block_reduce("s", false);
-            body << "        for (" << I << " k = threadIdx.x * " << V << "u; k < " << lit(A, wide) << "; k += "
-                 << T * V << "u) {\n            float xv[" << V << "];\n";
-            emit_load("k", "xv", "            ");
-            body << "            for (int e = 0; e < " << V << "; ++e) out[" << orow << " + k + e] = __expf(xv[e] - m) / s;\n        }\n";
+            body << "            #pragma unroll\n            for (int e = 0; e < " << V << "; ++e) out[" << orow
+                 << " + k + e] = __expf(xv[e] - m) * rs;\n";
+            body << "        }\n";
         }
         body << "    }\n";
         launch_spec l;
@@ -1816,10 +1885,14 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
         const int64_t per_sm = 2048 / T;
         l.grid = {static_cast<uint32_t>(std::min<int64_t>(rows, 148 * per_sm)), 1, 1};
         l.persistent_units = rows; // grid = CTAs resident at once, fixed at first launch
+        if (!in_registers) {
+            l.grid[0] = static_cast<uint32_t>(std::min<int64_t>(rows, 148 * stream_per_sm));
+            l.persistent_per_sm = stream_per_sm;
+        }
         l.block = {static_cast<uint32_t>(T), 1, 1};
         l.schedule = "softmax row kernel T=" + std::to_string(T) + " V=" + std::to_string(V) +
                      (in_registers ? " (row in registers, next row prefetched, 1 read + 1 write)"
-                                   : " (3-pass streaming)");
+                                   : " (online max/sum pass + write pass, 2 reads + 1 write)");
         l.args = r.k.leaves;
         kernel_arg o;
         o.kind = arg_kind::temp;

@@ -78,6 +78,9 @@ namespace porch::detail {
         // exactly the CTAs that fit at once (SMs x occupancy), so no CTA waits
         // for a second wave. 0 = launch `grid` as given.
         int64_t persistent_units = 0;
+        // With persistent_units: at most this many CTAs per SM (0: as many
+        // as fit), e.g. to keep the rows in flight inside L2.
+        int persistent_per_sm = 0;
         // Per device, filled on first launch under the plan's resolve mutex
         // and read without it by every later launch (from any thread): the
         // function is published with release order after the grid.
