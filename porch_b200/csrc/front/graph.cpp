@@ -450,8 +450,9 @@ namespace porch::detail {
                 const uint32_t pg = l.per_device->persistent_grid[device].load(std::memory_order_relaxed);
                 if (pg != 0) grid[0] = pg;
             }
+            const uint32_t cluster[3] = {l.cluster_x, 1, 1};
             check(pbrt_launch(device, fn, grid.data(), l.block.data(), l.smem,
-                              stream->stream, params.data(), nullptr));
+                              stream->stream, params.data(), l.cluster_x > 1 ? cluster : nullptr));
         }
         if (timing) t3 = now_ns();
 

@@ -1690,7 +1690,21 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
         const int stream_per_sm = 148 * 4 * row_bytes <= (int64_t{48} << 20)   ? 4
                                   : 148 * 3 * row_bytes <= (int64_t{64} << 20) ? 3
                                                                                : 1;
-        const int T = in_registers ? T0 : (stream_per_sm > 1 ? 256 : 1024);
+        // Fewer rows than the streaming form keeps resident, each of up to
+        // 8 x 16384 values: a cluster of C CTAs (512 threads, up to 32
+        // values each in registers) per row, the CTAs' maxima and sums
+        // exchanged through distributed shared memory -- one read and one
+        // write, and rows x C CTAs to spread over the SMs. (With rows
+        // enough to fill the GPU the persistent streaming CTAs win: on one
+        // box [64, 65536] 0.31 -> 0.43 of one read + one write with
+        // clusters, but [8192, 16388] 0.83 -> 0.72 and [2048, 65536]
+        // 0.72 -> 0.62.)
+        const int64_t cl_cap = 16384;
+        const int cluster_c = in_registers || A > 8 * cl_cap || rows >= int64_t{148} * stream_per_sm
+                                  ? 1
+                                  : static_cast<int>((A + cl_cap - 1) / cl_cap);
+        const bool clustered = cluster_c > 1;
+        const int T = in_registers ? T0 : (clustered ? 512 : (stream_per_sm > 1 ? 256 : 1024));
         std::vector<std::string> cvar(static_cast<size_t>(R));
         for (int d = 0; d < R; ++d) cvar[static_cast<size_t>(d)] = "c" + std::to_string(d);
         const char* comps[4] = {"x", "y", "z", "w"};
@@ -1800,6 +1814,73 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
             else
                 body << "                out[" << orow << " + k] = x[it][0] * rs;\n";
             body << "            }\n        }\n";
+        } else if (clustered) {
+            // CTA `rank` of the row's cluster holds columns [rank * SEG,
+            // (rank + 1) * SEG) in registers. Cluster barriers (release /
+            // acquire) order each CTA's shared partial before the others
+            // read it with ld.shared::cluster; all read the C partials in
+            // rank order, so every CTA combines them identically. The last
+            // barrier keeps each CTA's shared memory alive until the others
+            // have read it.
+            const int64_t seg = ((A + cluster_c - 1) / cluster_c + 3) / 4 * 4;
+            const int64_t ni = (seg + static_cast<int64_t>(T) * V - 1) / (static_cast<int64_t>(T) * V);
+            body << "    __shared__ float cl_part[2];\n";
+            body << "    pb_u32 rank;\n    asm volatile(\"mov.u32 %0, %%cluster_ctarank;\" : \"=r\"(rank));\n";
+            body << "    const " << I << " row = (" << I << ")blockIdx.x / " << cluster_c << "u;\n";
+            body << "    {\n";
+            emit_row_coords("row", "        ");
+            body << "        const " << I << " k0 = (" << I << ")rank * " << lit(seg, wide) << ";\n";
+            body << "        const " << I << " k1 = k0 + " << lit(seg, wide) << " < " << lit(A, wide) << " ? k0 + "
+                 << lit(seg, wide) << " : " << lit(A, wide) << ";\n";
+            body << "        float x[" << ni << "][" << V << "];\n";
+            body << "        float m = PB_NEG_FLT_MAX;\n";
+            body << "        #pragma unroll\n        for (int it = 0; it < " << ni << "; ++it) {\n";
+            body << "            const " << I << " k = k0 + ((" << I << ")it * " << T << "u + threadIdx.x) * " << V
+                 << "u;\n";
+            body << "            if (k < k1) {\n";
+            emit_load("k", "x[it]", "                ");
+            body << "                #pragma unroll\n                for (int e = 0; e < " << V
+                 << "; ++e) m = m > x[it][e] ? m : x[it][e];\n";
+            body << "            }\n        }\n";
+            block_reduce("m", true);
+            body << "        if (threadIdx.x == 0) cl_part[0] = m;\n";
+            body << "        asm volatile(\"barrier.cluster.arrive.release;\\n\\tbarrier.cluster.wait.acquire;\" ::: \"memory\");\n";
+            body << "        m = PB_NEG_FLT_MAX;\n";
+            body << "        #pragma unroll\n        for (pb_u32 q = 0; q < " << cluster_c << "u; ++q) {\n"
+                 << "            pb_u32 ra;\n            float v;\n"
+                 << "            asm volatile(\"mapa.shared::cluster.u32 %0, %1, %2;\" : \"=r\"(ra) : \"r\"((pb_u32)__cvta_generic_to_shared(&cl_part[0])), \"r\"(q));\n"
+                 << "            asm volatile(\"ld.shared::cluster.f32 %0, [%1];\" : \"=f\"(v) : \"r\"(ra) : \"memory\");\n"
+                 << "            m = m > v ? m : v;\n        }\n";
+            body << "        float s = 0.0f;\n";
+            body << "        #pragma unroll\n        for (int it = 0; it < " << ni << "; ++it) {\n";
+            body << "            const " << I << " k = k0 + ((" << I << ")it * " << T << "u + threadIdx.x) * " << V
+                 << "u;\n";
+            body << "            if (k < k1) {\n";
+            body << "                #pragma unroll\n                for (int e = 0; e < " << V
+                 << "; ++e) { x[it][e] = __expf(x[it][e] - m); s = s + x[it][e]; }\n";
+            body << "            }\n        }\n";
+            block_reduce("s", false);
+            body << "        if (threadIdx.x == 0) cl_part[1] = s;\n";
+            body << "        asm volatile(\"barrier.cluster.arrive.release;\\n\\tbarrier.cluster.wait.acquire;\" ::: \"memory\");\n";
+            body << "        s = 0.0f;\n";
+            body << "        #pragma unroll\n        for (pb_u32 q = 0; q < " << cluster_c << "u; ++q) {\n"
+                 << "            pb_u32 ra;\n            float v;\n"
+                 << "            asm volatile(\"mapa.shared::cluster.u32 %0, %1, %2;\" : \"=r\"(ra) : \"r\"((pb_u32)__cvta_generic_to_shared(&cl_part[1])), \"r\"(q));\n"
+                 << "            asm volatile(\"ld.shared::cluster.f32 %0, [%1];\" : \"=f\"(v) : \"r\"(ra) : \"memory\");\n"
+                 << "            s = s + v;\n        }\n";
+            body << "        asm volatile(\"barrier.cluster.arrive.release;\" ::: \"memory\");\n";
+            body << "        const float rs = 1.0f / s;\n";
+            body << "        #pragma unroll\n        for (int it = 0; it < " << ni << "; ++it) {\n";
+            body << "            const " << I << " k = k0 + ((" << I << ")it * " << T << "u + threadIdx.x) * " << V
+                 << "u;\n";
+            body << "            if (k < k1) {\n";
+            if (V == 4)
+                body << "                pb_st4(out + " << orow
+                     << " + k, make_float4(x[it][0] * rs, x[it][1] * rs, x[it][2] * rs, x[it][3] * rs));\n";
+            else
+                body << "                out[" << orow << " + k] = x[it][0] * rs;\n";
+            body << "            }\n        }\n";
+            body << "        asm volatile(\"barrier.cluster.wait.acquire;\" ::: \"memory\");\n";
         } else {
             // Rows too long for registers: an online pass keeps a running
             // (max, sum) per thread -- four vector loads per step, the sum
@@ -1885,14 +1966,20 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
         const int64_t per_sm = 2048 / T;
         l.grid = {static_cast<uint32_t>(std::min<int64_t>(rows, 148 * per_sm)), 1, 1};
         l.persistent_units = rows; // grid = CTAs resident at once, fixed at first launch
-        if (!in_registers) {
+        if (clustered) {
+            l.grid[0] = static_cast<uint32_t>(rows * cluster_c);
+            l.persistent_units = 0;
+            l.cluster_x = static_cast<uint32_t>(cluster_c);
+        } else if (!in_registers) {
             l.grid[0] = static_cast<uint32_t>(std::min<int64_t>(rows, 148 * stream_per_sm));
             l.persistent_per_sm = stream_per_sm;
         }
         l.block = {static_cast<uint32_t>(T), 1, 1};
         l.schedule = "softmax row kernel T=" + std::to_string(T) + " V=" + std::to_string(V) +
                      (in_registers ? " (row in registers, next row prefetched, 1 read + 1 write)"
-                                   : " (online max/sum pass + write pass, 2 reads + 1 write)");
+                      : clustered ? " (cluster of " + std::to_string(cluster_c) +
+                                        " CTAs per row, row in registers, partials through DSMEM, 1 read + 1 write)"
+                                  : std::string(" (online max/sum pass + write pass, 2 reads + 1 write)"));
         l.args = r.k.leaves;
         kernel_arg o;
         o.kind = arg_kind::temp;

@@ -81,6 +81,9 @@ namespace porch::detail {
         // With persistent_units: at most this many CTAs per SM (0: as many
         // as fit), e.g. to keep the rows in flight inside L2.
         int persistent_per_sm = 0;
+        // Thread-block cluster size along x (1: no cluster); grid[0] is a
+        // multiple of it.
+        uint32_t cluster_x = 1;
         // Per device, filled on first launch under the plan's resolve mutex
         // and read without it by every later launch (from any thread): the
         // function is published with release order after the grid.

@@ -2,7 +2,11 @@
 -> exp -> sum -> divide).
 
 Rows of up to 64 values per thread (16384 columns at 256 threads) are held
-in registers: one read and one write. Longer rows take two passes: an online
+in registers: one read and one write. When there are too few rows to fill
+the GPU, rows of up to 8 x 16384 columns are spread over a thread-block
+cluster of 2-8 CTAs, each holding its segment in registers, the CTAs'
+maxima and sums exchanged through distributed shared memory: still one read
+and one write. Otherwise longer rows take two passes: an online
 pass keeps a running (max, sum) per thread, rescaling the sum whenever the
 max grows, and the block combines the pairs; a second pass writes
 exp(x - m) / s. CPU: the plans. GPU: parity with the host oracle within the
@@ -17,10 +21,14 @@ from tolerances import assert_relative
 
 LONG = [
     # (rows, columns, distribution)
-    (64, 65536, "normal"),
-    (37, 20000, "rising"),    # the max grows at every step: a rescale each time
-    (10, 100003, "normal"),   # not a multiple of 4: scalar loads
-    (3, 16388, "falling"),    # just past the register limit; the first step holds the max
+    (64, 65536, "normal"),    # cluster of 4
+    (37, 20000, "rising"),    # cluster of 2; the max sits in the last CTA
+    (10, 100003, "normal"),   # cluster of 7, not a multiple of 4: scalar loads
+    (3, 16388, "falling"),    # cluster of 2, the second CTA holds 2 columns
+    (5, 131072, "rising"),    # cluster of 8
+    (600, 20000, "rising"),   # rows enough to fill the GPU: streaming
+    (4, 140000, "rising"),    # streaming: a rescale at every step
+    (2, 300001, "falling"),   # streaming, scalar loads
 ]
 
 
@@ -44,13 +52,18 @@ def _placeholder_plan(api, program, shapes):
     return [line for line in api.describe(e).splitlines() if line.startswith("kernel ")]
 
 
-def test_long_rows_plan_the_online_two_pass_kernel(api):
-    kernels = _placeholder_plan(api, "0 input 0\n1 softmax 0 1\n", [[64, 65536]])
-    assert len(kernels) == 1 and "online max/sum pass" in kernels[0], kernels
-    kernels = _placeholder_plan(api, "0 input 0\n1 softmax 0 1\n", [[1000, 16384]])
+def test_long_rows_plan_cluster_or_online_kernels(api):
+    prog = "0 input 0\n1 softmax 0 1\n"
+    kernels = _placeholder_plan(api, prog, [[1000, 16384]])
     assert len(kernels) == 1 and "row in registers" in kernels[0], kernels
-    kernels = _placeholder_plan(api, "0 input 0\n1 softmax 0 1\n", [[10, 100003]])
-    assert "V=1" in kernels[0] and "online" in kernels[0], kernels
+    kernels = _placeholder_plan(api, prog, [[64, 65536]])
+    assert len(kernels) == 1 and "cluster of 4 CTAs" in kernels[0] and "grid=256x" in kernels[0], kernels
+    kernels = _placeholder_plan(api, prog, [[10, 100003]])
+    assert "V=1" in kernels[0] and "cluster of 7 CTAs" in kernels[0], kernels
+    kernels = _placeholder_plan(api, prog, [[4, 140000]])
+    assert len(kernels) == 1 and "online max/sum pass" in kernels[0], kernels
+    kernels = _placeholder_plan(api, prog, [[600, 20000]])
+    assert len(kernels) == 1 and "online max/sum pass" in kernels[0], kernels
 
 
 @pytest.mark.parametrize("rows,cols,kind", LONG[:2])
