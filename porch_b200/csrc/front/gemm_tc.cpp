@@ -182,11 +182,11 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
                               const kernel_arg& B, int64_t M, int64_t N, int64_t K, int* nonfinite) {
         (void)id;
         if (tensor_cores_disabled()) return -1;
-        // Any M; N and K multiples of 4 (16-byte TMA row strides for the
-        // K-major hi/lo arrays and float4 epilogue stores). Edge tiles read
-        // zeros past M, N and K (TMA out-of-bounds fill) and mask their
-        // stores.
-        if (N % 4 != 0 || K % 4 != 0 || M < 1) return -1;
+        // Any M, N, K. The K-major hi/lo arrays have padded rows (16-byte
+        // TMA strides whatever K is); edge tiles read zeros past M, N and K
+        // (TMA out-of-bounds fill) and mask their stores; when N is not a
+        // multiple of 4 the epilogue loads and stores one float at a time.
+        if (M < 1 || N < 1 || K < 1) return -1;
         if (M * N * K < (int64_t{1} << 27)) return -1;
         if (M > (int64_t{1} << 30) || N > (int64_t{1} << 30) || K > (int64_t{1} << 30)) return -1;
         rank_ = 2;
@@ -235,10 +235,19 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
                 << "ull; i += (pb_u64)gridDim.x * 256u) {\n";
             if (Kp == K) {
                 src << "        const float4 v = pb_ld4(x + 4 * i);\n";
-            } else {
+            } else if (K % 4 == 0) {
                 src << "        const pb_u64 r = i / " << Kp / 4 << "ull, c = i % " << Kp / 4 << "ull;\n"
                     << "        const float4 v = c < " << K / 4 << "ull ? pb_ld4(x + r * " << K
                     << "ull + 4 * c) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);\n";
+            } else {
+                // Rows of A not 16-byte aligned: one float at a time.
+                src << "        const pb_u64 r = i / " << Kp / 4 << "ull, c = 4 * (i % " << Kp / 4 << "ull);\n"
+                    << "        const float* xr = x + r * " << K << "ull;\n"
+                    << "        float4 v;\n"
+                    << "        v.x = c < " << K << "ull ? pb_ld(xr + c) : 0.0f;\n"
+                    << "        v.y = c + 1 < " << K << "ull ? pb_ld(xr + c + 1) : 0.0f;\n"
+                    << "        v.z = c + 2 < " << K << "ull ? pb_ld(xr + c + 2) : 0.0f;\n"
+                    << "        v.w = c + 3 < " << K << "ull ? pb_ld(xr + c + 3) : 0.0f;\n";
             }
             src
                 << "        if (!(isfinite(v.x) && isfinite(v.y) && isfinite(v.z) && isfinite(v.w))) atomicOr(nf, 1);\n"
@@ -331,7 +340,7 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
         }
         const int64_t kb_unit = (raw_kb + split - 1) / split;
         const int64_t units = tiles * split;
-        const int part = split > 1 ? new_temp(static_cast<size_t>(split * M * N) * 4) : -1;
+        const int part = split > 1 ? new_temp(static_cast<size_t>(split * M * ((N + 3) / 4 * 4)) * 4) : -1;
         std::ostringstream src;
         src << kernel_prelude() << "#define PB_PERIOD " << period << "\n#define PB_SPLIT " << split << "\n"
             << gemm_device_source() << efn;
@@ -489,13 +498,17 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
         // Leaf loads by column stride: 1 and 16-byte aligned -> float4 per
         // 4 columns; 0 -> one load per row, hoisted out of the column loops;
         // otherwise one scalar per element.
+        // With N not a multiple of 4 a group of four columns can cross the
+        // end of a row: scalar loads, each behind a column check.
+        const bool vec_n = N % 4 == 0;
+        const int64_t Np = (N + 3) / 4 * 4;  // row pitch of the split-K partials
         std::vector<int> leaf_mode(order.size());
         for (size_t li = 0; li < order.size(); ++li) {
             const vnode& v = b.nodes[static_cast<size_t>(order[li])];
             const int64_t sr = v.map.st[0], sc = v.map.st[1];
             if (sc == 0)
                 leaf_mode[li] = 0;
-            else if (sc == 1 && v.map.off % 4 == 0 && sr % 4 == 0)
+            else if (vec_n && sc == 1 && v.map.off % 4 == 0 && sr % 4 == 0)
                 leaf_mode[li] = 1;
             else
                 leaf_mode[li] = 2;
@@ -513,6 +526,7 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
             }
             os << ind << "float y[4];\n" << ind << "#pragma unroll\n" << ind << "for (int e = 0; e < 4; ++e) {\n"
                << ind << "    const pb_u64 ce = cc + (pb_u64)e;\n" << ind << "    (void)ce;\n";
+            if (!vec_n) os << ind << "    y[e] = 0.0f;\n" << ind << "    if (ce >= " << N << "ull) continue;\n";
             for (size_t li = 0; li < order.size(); ++li) {
                 const vnode& v = b.nodes[static_cast<size_t>(order[li])];
                 if (leaf_mode[li] == 0)
@@ -545,10 +559,10 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
                  << "            #pragma unroll\n"
                  << "            for (int c = 0; c < PB_BN / 64; ++c) {\n"
                  << "                const int cbase = n0 + (int)half * (PB_BN / 2) + c * 32;\n"
-                 << "                float* orow = out + sp * " << M * N << "ull + rr * " << N << "ull + cbase;\n"
+                 << "                float* orow = out + sp * " << M * Np << "ull + rr * " << Np << "ull + cbase;\n"
                  << "                #pragma unroll\n"
                  << "                for (int j = 0; j < 32; j += 4)\n"
-                 << "                    if ((pb_u64)(cbase + j) < " << N << "ull)\n"
+                 << "                    if ((pb_u64)(cbase + j) < " << Np << "ull)\n"
                  << "                        pb_st4(orow + j, make_float4(acc[c * 32 + j], acc[c * 32 + j + 1], "
                     "acc[c * 32 + j + 2], acc[c * 32 + j + 3]));\n"
                  << "            }\n"
@@ -567,8 +581,13 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
                  << "                    const pb_u64 cc = (pb_u64)(cbase + j);\n"
                  << "                    if (cc >= " << N << "ull) continue;\n";
             emit_epilogue4(body, "                    ", "acc[c * 32 + j + e]");
-            body << "                    pb_st4(orow + j, make_float4(y[0], y[1], y[2], y[3]));\n"
-                 << "                }\n"
+            if (vec_n)
+                body << "                    pb_st4(orow + j, make_float4(y[0], y[1], y[2], y[3]));\n";
+            else
+                body << "                    #pragma unroll\n"
+                     << "                    for (int e = 0; e < 4; ++e) if (cc + (pb_u64)e < " << N
+                     << "ull) orow[j + e] = y[e];\n";
+            body << "                }\n"
                  << "            }\n"
                  << "            }\n";
         }
@@ -648,25 +667,29 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
 
         // ---- 4. split-K: sum the partials in split order + epilogue ---------
         {
-            const int64_t n4 = M * N / 4;
+            const int64_t n4 = M * Np / 4;
             std::ostringstream ks;
             ks << kernel_prelude() << efn;
             std::ostringstream kb;
             kb << "    if (*(const volatile int*)nf != 0) return;  // the CUDA-core GEMM writes out\n";
             kb << "    for (pb_u64 i = (pb_u64)blockIdx.x * 256u + threadIdx.x; i < " << n4
                << "ull; i += (pb_u64)gridDim.x * 256u) {\n"
-               << "        const pb_u64 o = 4u * i, rr = o / " << N << "ull, cc = o % " << N << "ull;\n"
+               << "        const pb_u64 o = 4u * i, rr = o / " << Np << "ull, cc = o % " << Np << "ull;\n"
                << "        (void)rr; (void)cc;\n"
                << "        float4 s = pb_ld4(part + o);\n"
                << "        #pragma unroll\n"
                << "        for (int p = 1; p < " << split << "; ++p) {\n"
-               << "            const float4 v = pb_ld4(part + (pb_u64)p * " << M * N << "ull + o);\n"
+               << "            const float4 v = pb_ld4(part + (pb_u64)p * " << M * Np << "ull + o);\n"
                << "            s.x = s.x + v.x; s.y = s.y + v.y; s.z = s.z + v.z; s.w = s.w + v.w;\n"
                << "        }\n"
                << "        const float sv[4] = {s.x, s.y, s.z, s.w};\n";
             emit_hoisted(kb, "        ");
             emit_epilogue4(kb, "        ", "sv[e]");
-            kb << "        pb_st4(out + o, make_float4(y[0], y[1], y[2], y[3]));\n    }\n";
+            if (vec_n)
+                kb << "        pb_st4(out + o, make_float4(y[0], y[1], y[2], y[3]));\n    }\n";
+            else
+                kb << "        #pragma unroll\n        for (int e = 0; e < 4; ++e) if (cc + (pb_u64)e < " << N
+                   << "ull) out[rr * " << N << "ull + cc + e] = y[e];\n    }\n";
             launch_spec r;
             r.name = "pb_splitk_" + hex8(ks.str() + kb.str());
             ks << "extern \"C\" __global__ void __launch_bounds__(256) " << r.name << "(";

@@ -22,7 +22,7 @@
 //  - the ops.hpp softmax shape over the last axis: one single-pass row kernel
 //    (row held in registers: one HBM read and one write), not four kernels.
 //  - matmul: the pending elementwise consumer is fused as the epilogue.
-//    Large aligned shapes use the tcgen05 3xTF32 path (gemm_tc.cpp); the rest
+//    Large shapes use the tcgen05 3xTF32 path (gemm_tc.cpp); the rest
 //    use a tiled CUDA-core kernel whose per-output FMA chain runs in k order,
 //    the same order as the reference's generated loop.
 #include "plan.hpp"

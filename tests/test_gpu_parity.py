@@ -175,13 +175,17 @@ TC_SHAPES = [(512, 512, 512), (256, 1024, 768), (1024, 768, 512), (384, 512, 102
              (1000, 520, 1004), (300, 4096, 772), (129, 4100, 260),
              # K past a multiple of 32: hi/lo rows padded with zeros to
              # 128-byte lines, the last accumulation period of a tile short
-             (128, 4100, 4096), (2048, 2052, 2048)]
+             (128, 4100, 4096), (2048, 2052, 2048),
+             # N or K not multiples of 4: scalar A loads, column-checked
+             # epilogue loads and stores, split-K partials on a padded pitch
+             (1000, 999, 1001), (513, 4097, 515), (129, 1030, 2050), (300, 771, 4096),
+             (2049, 515, 1027)]
 
 
 @pytest.mark.parametrize("m,k,n", TC_SHAPES)
 def test_tcgen05_3xtf32_matmul(gpu, m, k, n):
-    """Shapes eligible for the tcgen05 path (N, K multiples of 4 and
-    M*N*K >= 2^27): the plan must use it, and the result must hold fp32 accuracy: within the
+    """Shapes eligible for the tcgen05 path (M*N*K >= 2^27): the plan must
+    use it, and the result must hold fp32 accuracy: within the
     normalised 1e-5 bound, and within 4x the error of the reference's
     sequential fp32 accumulation (a plain one-pass TF32 product is about
     1000x worse than fp32 and fails this)."""
