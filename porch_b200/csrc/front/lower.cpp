@@ -1409,50 +1409,50 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
                 desc = "row reduction (CTA of " + std::to_string(threads) + " per row, 4 loads in flight) V=" +
                        std::to_string(V);
             } else {
-            body << "    const pb_u32 warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;\n";
-            body << "    const " << I << " row = (" << I << ")blockIdx.x * 8u + warp;\n";
-            body << "    if (row >= " << lit(outer, wide) << ") return;\n";
-            body << "    " << I << " t = row;\n";
-            for (int d = static_cast<int>(ax) - 1; d >= 0; --d) {
-                body << "    const " << I << " c" << d << " = t % " << lit(S[static_cast<size_t>(d)], wide) << "; t /= "
-                     << lit(S[static_cast<size_t>(d)], wide) << ";\n";
-            }
-            // Dimensions after the axis all have extent 1 here.
-            for (int d = static_cast<int>(ax) + 1; d < R; ++d)
-                body << "    const " << I << " c" << d << " = 0;\n";
-            body << "    float acc = " << init << ";\n";
-            body << "    for (" << I << " k = lane * " << V << "u; k < " << lit(A, wide) << "; k += " << 32 * V << "u) {\n";
-            body << "        const " << I << " c" << ax << " = k;\n";
-            for (size_t li = 0; li < order.size(); ++li) {
-                const vnode& v = r.b.nodes[static_cast<size_t>(order[li])];
-                const std::string base = "in" + std::to_string(v.buffer);
-                const std::string addr = address(v.map, cvar, wide, -1);
-                const int64_t sa = v.map.st[ax];
-                if (V == 4 && sa == 1)
-                    body << "        const float4 x" << li << " = pb_ld4(" << base << " + " << addr << ");\n";
-                else if (V == 4)
-                    body << "        const float s" << li << " = pb_ld(" << base << " + " << addr
-                         << "); const float4 x" << li << " = make_float4(s" << li << ", s" << li << ", s" << li
-                         << ", s" << li << ");\n";
-                else
-                    body << "        const float x" << li << " = pb_ld(" << base << " + " << addr << ");\n";
-            }
-            const char* comps[4] = {"x", "y", "z", "w"};
-            for (int e = 0; e < V; ++e) {
-                body << "        { const float v = pb_e0(";
-                for (size_t li = 0; li < order.size(); ++li) {
-                    if (li) body << ", ";
-                    body << "x" << li << (V == 4 ? std::string(".") + comps[e] : "");
+                body << "    const pb_u32 warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;\n";
+                body << "    const " << I << " row = (" << I << ")blockIdx.x * 8u + warp;\n";
+                body << "    if (row >= " << lit(outer, wide) << ") return;\n";
+                body << "    " << I << " t = row;\n";
+                for (int d = static_cast<int>(ax) - 1; d >= 0; --d) {
+                    body << "    const " << I << " c" << d << " = t % " << lit(S[static_cast<size_t>(d)], wide) << "; t /= "
+                         << lit(S[static_cast<size_t>(d)], wide) << ";\n";
                 }
-                body << "); " << combine("acc", "v") << " }\n";
-            }
-            body << "    }\n";
-            body << "    #pragma unroll\n    for (int o = 16; o > 0; o >>= 1) { const float v = __shfl_xor_sync(0xffffffffu, acc, o); "
-                 << combine("acc", "v") << " }\n";
-            body << "    if (lane == 0) out[row] = acc;\n";
-            const int64_t ctas = (outer + 7) / 8;
-            l.grid = {static_cast<uint32_t>(ctas), 1, 1};
-            desc = "row reduction (warp per row) V=" + std::to_string(V);
+                // Dimensions after the axis all have extent 1 here.
+                for (int d = static_cast<int>(ax) + 1; d < R; ++d)
+                    body << "    const " << I << " c" << d << " = 0;\n";
+                body << "    float acc = " << init << ";\n";
+                body << "    for (" << I << " k = lane * " << V << "u; k < " << lit(A, wide) << "; k += " << 32 * V << "u) {\n";
+                body << "        const " << I << " c" << ax << " = k;\n";
+                for (size_t li = 0; li < order.size(); ++li) {
+                    const vnode& v = r.b.nodes[static_cast<size_t>(order[li])];
+                    const std::string base = "in" + std::to_string(v.buffer);
+                    const std::string addr = address(v.map, cvar, wide, -1);
+                    const int64_t sa = v.map.st[ax];
+                    if (V == 4 && sa == 1)
+                        body << "        const float4 x" << li << " = pb_ld4(" << base << " + " << addr << ");\n";
+                    else if (V == 4)
+                        body << "        const float s" << li << " = pb_ld(" << base << " + " << addr
+                             << "); const float4 x" << li << " = make_float4(s" << li << ", s" << li << ", s" << li
+                             << ", s" << li << ");\n";
+                    else
+                        body << "        const float x" << li << " = pb_ld(" << base << " + " << addr << ");\n";
+                }
+                const char* comps[4] = {"x", "y", "z", "w"};
+                for (int e = 0; e < V; ++e) {
+                    body << "        { const float v = pb_e0(";
+                    for (size_t li = 0; li < order.size(); ++li) {
+                        if (li) body << ", ";
+                        body << "x" << li << (V == 4 ? std::string(".") + comps[e] : "");
+                    }
+                    body << "); " << combine("acc", "v") << " }\n";
+                }
+                body << "    }\n";
+                body << "    #pragma unroll\n    for (int o = 16; o > 0; o >>= 1) { const float v = __shfl_xor_sync(0xffffffffu, acc, o); "
+                     << combine("acc", "v") << " }\n";
+                body << "    if (lane == 0) out[row] = acc;\n";
+                const int64_t ctas = (outer + 7) / 8;
+                l.grid = {static_cast<uint32_t>(ctas), 1, 1};
+                desc = "row reduction (warp per row) V=" + std::to_string(V);
             }
         } else if (R == 2 && ax == 0 && S[1] % 4 == 0 && S[1] >= 64 && [&] {
                        for (int li : order) {
