@@ -137,6 +137,16 @@ int pbrt_function_attribute(pbrt_function function, int attribute,
 int pbrt_launch(int device, pbrt_function function, const uint32_t* grid,
                 const uint32_t* block, uint32_t dynamic_smem,
                 pbrt_stream stream, void** params, const uint32_t* cluster);
+/* pbrt_launch with flags. PBRT_LAUNCH_PDL: programmatic stream serialization
+ * -- the launch may begin while the stream's previous kernel finishes, so
+ * the kernel must execute `griddepcontrol.wait` before it touches memory
+ * that earlier work in the stream reads or writes (the generated kernels do
+ * so first thing). */
+#define PBRT_LAUNCH_PDL 1u
+int pbrt_launch_ex(int device, pbrt_function function, const uint32_t* grid,
+                   const uint32_t* block, uint32_t dynamic_smem,
+                   pbrt_stream stream, void** params, const uint32_t* cluster,
+                   unsigned flags);
 /* cuTensorMapEncodeTiled with plain integers; out must hold 128 bytes. */
 int pbrt_tensor_map_encode_tiled(void* out, int data_type, uint32_t rank,
                                  uint64_t global_address,

@@ -109,6 +109,8 @@ def _declare(L: ctypes.CDLL) -> None:
         "pbrt_mem_alloc_async": (c_int, [c_int, c_size_t, c_void_p, P(c_uint64)]),
         "pbrt_mem_free_async": (c_int, [c_int, c_uint64, c_void_p]),
         "pbrt_mem_alloc": (c_int, [c_int, c_size_t, P(c_uint64)]),
+        "pbrt_launch_ex": (c_int, [c_int, c_void_p, P(ctypes.c_uint32), P(ctypes.c_uint32), ctypes.c_uint32, c_void_p,
+                                   P(c_void_p), P(ctypes.c_uint32), ctypes.c_uint]),
         "pbrt_mem_free": (c_int, [c_int, c_uint64]),
         "pbrt_memcpy_h2d_async": (c_int, [c_int, c_uint64, c_void_p, c_size_t, c_void_p]),
         "pbrt_memcpy_d2h_async": (c_int, [c_int, c_void_p, c_uint64, c_size_t, c_void_p]),

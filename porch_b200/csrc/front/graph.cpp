@@ -451,8 +451,9 @@ namespace porch::detail {
                 if (pg != 0) grid[0] = pg;
             }
             const uint32_t cluster[3] = {l.cluster_x, 1, 1};
-            check(pbrt_launch(device, fn, grid.data(), l.block.data(), l.smem,
-                              stream->stream, params.data(), l.cluster_x > 1 ? cluster : nullptr));
+            check(pbrt_launch_ex(device, fn, grid.data(), l.block.data(), l.smem, stream->stream,
+                                 params.data(), l.cluster_x > 1 ? cluster : nullptr,
+                                 l.pdl ? PBRT_LAUNCH_PDL : 0u));
         }
         if (timing) t3 = now_ns();
 

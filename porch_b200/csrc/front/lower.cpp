@@ -900,7 +900,17 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
         return os.str();
     }
 
+    // Every generated kernel first waits for the stream's previous kernel
+    // (griddepcontrol.wait: returns at once when there is no programmatic
+    // dependency), so all of them can launch with programmatic stream
+    // serialization and their launch overlaps the previous kernel's tail.
     void lowerer::finish_kernel(launch_spec& l) {
+        const size_t g = l.source.find("__global__");
+        const size_t open = g == std::string::npos ? g : l.source.find('{', g);
+        if (open == std::string::npos || l.source.find("__global__", g + 10) != std::string::npos)
+            throw std::logic_error("generated source must define exactly one kernel: " + l.name);
+        l.source.insert(open + 1, "\n    asm volatile(\"griddepcontrol.wait;\" ::: \"memory\");");
+        l.pdl = true;
         const auto& opts = kernel_options();
         std::vector<const char*> o;
         for (const auto& s : opts) o.push_back(s.c_str());

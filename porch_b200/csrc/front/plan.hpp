@@ -84,6 +84,10 @@ namespace porch::detail {
         // Thread-block cluster size along x (1: no cluster); grid[0] is a
         // multiple of it.
         uint32_t cluster_x = 1;
+        // The kernel waits for the stream's previous kernel itself
+        // (griddepcontrol.wait first thing), so it may launch with
+        // programmatic stream serialization.
+        bool pdl = false;
         // Per device, filled on first launch under the plan's resolve mutex
         // and read without it by every later launch (from any thread): the
         // function is published with release order after the grid.

@@ -1151,6 +1151,12 @@ int pbrt_occupancy(int device, pbrt_function function, int block_threads, size_t
 int pbrt_launch(int device, pbrt_function function, const uint32_t* grid,
                 const uint32_t* block, uint32_t dynamic_smem, pbrt_stream stream,
                 void** params, const uint32_t* cluster) {
+    return pbrt_launch_ex(device, function, grid, block, dynamic_smem, stream, params, cluster, 0u);
+}
+
+int pbrt_launch_ex(int device, pbrt_function function, const uint32_t* grid,
+                   const uint32_t* block, uint32_t dynamic_smem, pbrt_stream stream,
+                   void** params, const uint32_t* cluster, unsigned flags) {
     if (function == nullptr || grid == nullptr || block == nullptr)
         return fail(PBRT_ERR_INVALID, "launch function, grid or block is null");
     environment* env = nullptr;
@@ -1166,14 +1172,23 @@ int pbrt_launch(int device, pbrt_function function, const uint32_t* grid,
     config.blockDimZ = block[2];
     config.sharedMemBytes = dynamic_smem;
     config.hStream = reinterpret_cast<CUstream>(stream);
-    CUlaunchAttribute attribute{};
+    CUlaunchAttribute attributes[2]{};
+    unsigned n_attr = 0;
     if (cluster != nullptr && cluster[0] * cluster[1] * cluster[2] > 1) {
-        attribute.id = CU_LAUNCH_ATTRIBUTE_CLUSTER_DIMENSION;
-        attribute.value.clusterDim.x = cluster[0];
-        attribute.value.clusterDim.y = cluster[1];
-        attribute.value.clusterDim.z = cluster[2];
-        config.attrs = &attribute;
-        config.numAttrs = 1;
+        attributes[n_attr].id = CU_LAUNCH_ATTRIBUTE_CLUSTER_DIMENSION;
+        attributes[n_attr].value.clusterDim.x = cluster[0];
+        attributes[n_attr].value.clusterDim.y = cluster[1];
+        attributes[n_attr].value.clusterDim.z = cluster[2];
+        ++n_attr;
+    }
+    if ((flags & PBRT_LAUNCH_PDL) != 0) {
+        attributes[n_attr].id = CU_LAUNCH_ATTRIBUTE_PROGRAMMATIC_STREAM_SERIALIZATION;
+        attributes[n_attr].value.programmaticStreamSerializationAllowed = 1;
+        ++n_attr;
+    }
+    if (n_attr > 0) {
+        config.attrs = attributes;
+        config.numAttrs = n_attr;
     }
     profiler& p = prof();
     const bool profiling = p.enabled;
