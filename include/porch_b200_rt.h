@@ -18,7 +18,9 @@
  *  - src/cuda_jit.cpp:437-528  cuda_environment (device 0 only) and thread-local
  *                              stream_handle; here: primary context per device,
  *                              stream per (thread, device)
- *  - src/cuda_jit.cpp:532-627  device_buffer_state cuMemAllocAsync/cuMemFreeAsync
+ *  - src/cuda_jit.cpp:532-627  device_buffer_state cuMemAllocAsync/cuMemFreeAsync;
+ *                              here: both kept, plus cuMemAlloc for the
+ *                              library's caching allocator (pbrt_mem_alloc)
  *  - src/cuda_jit.cpp:647-703  compile_to_ptx + ptx_cache (source-text keyed);
  *                              here: NVRTC -> sm_100a cubin keyed by a 64-bit hash
  *  - src/cuda_jit.cpp:705-761  copy_to_device / copy_to_host / synchronize

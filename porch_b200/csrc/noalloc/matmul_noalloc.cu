@@ -5,7 +5,8 @@
 // e.g. code running inside a custom memory arena or allocator hook, a
 // framework that forbids hidden allocations while it owns the device, or a
 // context where a cudaMalloc would synchronise or fail. The regular path
-// (pb_materialize) allocates its temporaries from the stream-ordered pool.
+// (pb_materialize) takes its temporaries from the library's caching
+// allocator, which calls cuMemAlloc when its cache has no block to reuse.
 //
 // The 3xTF32 split needs scratch for Ahi, Alo (M x K) and Bhi, Blo (N x K,
 // B transposed to K-major). Here that scratch is a file-scope device array
