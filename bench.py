@@ -396,6 +396,12 @@ def run_ours(args, rank, world, local, dist):
                     "how": "CUDA events around every launch over a second pass of the same K steps "
                            "(the timed region itself runs without them)",
                     "kernel_ms": round(per_launch_ms, 5)}
+        if bound == "tensor" and pk.get("bf16_tflops_sustained"):
+            # Context: the same ceiling from the power-capped figure (bf16
+            # GEMMs back to back for seconds); `frac` keeps the burst one.
+            sustained = round(pk["bf16_tflops_sustained"] / 6.0, 2)
+            roofline["peak_sustained"] = sustained
+            roofline["frac_sustained"] = round(achieved / sustained, 4)
 
     # End to end through the C-ABI with host buffers in pinned memory.
     pinned = [api.PinnedBuffer(a.size) for a in arrays]
