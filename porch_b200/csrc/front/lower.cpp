@@ -17,10 +17,16 @@
 //    both global reads and writes stay coalesced and shared memory is
 //    bank-conflict free). Graphs that are not affine (reshape of an
 //    unaligned slice and the like) fall back to a per-element gather kernel.
-//  - sum/max along an axis: warp-per-row (contiguous axis) or
-//    thread-per-output (strided axis) with the operand expression fused in.
-//  - the ops.hpp softmax shape over the last axis: one single-pass row kernel
-//    (row held in registers: one HBM read and one write), not four kernels.
+//  - sum/max along an axis, the operand expression fused in: a warp per row
+//    (contiguous axis), a CTA per row for few long rows, 128-column tiles
+//    for axis 0 of a 2-D operand with aligned rows, else a thread per
+//    output (strided axis); tall inputs split into row chunks whose
+//    partials a second pass combines in a fixed order.
+//  - the ops.hpp softmax shape over the last axis: one row kernel, not four
+//    kernels -- rows held in registers (one HBM read and one write); for few
+//    long rows a thread-block cluster per row exchanging max and sum through
+//    distributed shared memory; otherwise an online max/sum pass and a write
+//    pass.
 //  - matmul: the pending elementwise consumer is fused as the epilogue.
 //    Large shapes use the tcgen05 3xTF32 path (gemm_tc.cpp); the rest
 //    use a tiled CUDA-core kernel whose per-output FMA chain runs in k order,
