@@ -28,17 +28,30 @@ DISTRIBUTIONS = {
 }
 # Inputs whose leading dimension is the graph's row axis (cut by --rows).
 ROW_INPUTS = {"c3a_softmax": {"x"}, "c3b_relu_logistic": {"x"}, "c4_matmul": {"a"}, "c5_mlp": {"x"}}
-# Reductions outside the benchmark configs: (shape, axis) of sum(x, axis).
+# Row graphs outside the benchmark configs: (shape, axis) of sum(x, axis),
+# and long-row softmax shapes (streaming two-pass; a cluster per row).
 REDUCTIONS = {"sum_axis0": ([262144, 256], 0), "sum_axis1": ([4096, 16384], 1)}
+SOFTMAX = {"softmax_long": [4096, 32768], "softmax_cluster": [64, 65536]}
 
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("workload", choices=sorted(api.CONFIG_SHAPES) + sorted(REDUCTIONS))
+    ap.add_argument("workload", choices=sorted(api.CONFIG_SHAPES) + sorted(REDUCTIONS) + sorted(SOFTMAX))
     ap.add_argument("--rows", type=int, default=0)
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--device", type=int, default=0)
     args = ap.parse_args()
+    if args.workload in SOFTMAX:
+        shape = list(SOFTMAX[args.workload])
+        if args.rows:
+            shape[0] = args.rows
+        arr = np.empty(int(np.prod(shape)), dtype=np.float32)
+        api.fill_synthetic(arr, 20261201, "normal", 0, 2)
+        x = api.tensor(shape, arr, device=args.device)
+        outs = [api.materialize(api.softmax(x, 1)) for _ in range(max(1, args.steps))]
+        api.device_synchronize(args.device)
+        print(f"{args.workload}: {len(outs)} realisations of shape {outs[-1].shape()}")
+        return
     if args.workload in REDUCTIONS:
         shape, axis = REDUCTIONS[args.workload]
         shape = list(shape)
