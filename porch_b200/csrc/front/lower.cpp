@@ -1949,28 +1949,36 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
                 pair_combine("om", "os", "            ");
                 body << "        }\n        __syncthreads();  // red_m/red_s are rewritten by the next row\n";
             }
+            // The write pass walks the row from its end: the online pass
+            // read the end last, so that part is the likeliest still in L2.
             body << "        const float rs = 1.0f / s;\n";
-            body << "        k = threadIdx.x * " << V << "u;\n";
-            body << "        for (; k + " << 3 * step << "u < " << lit(A, wide) << "; k += " << 4 * step << "u) {\n";
-            body << "            float xv[4][" << V << "];\n";
+            body << "        {\n";
+            body << "            const " << I << " k0 = threadIdx.x * " << V << "u;\n";
+            body << "            long long j = k0 < " << lit(A, wide) << " ? (long long)((" << lit(A, wide)
+                 << " - 1u - k0) / " << step << "u) : -1;\n";
+            body << "            for (; j >= 3; j -= 4) {\n";
+            body << "                float xv[4][" << V << "];\n";
             for (int u = 0; u < 4; ++u)
-                emit_load("k + " + std::to_string(u * step) + "u", "xv[" + std::to_string(u) + "]", "            ");
+                emit_load("k0 + (" + I + ")(j - " + std::to_string(u) + ") * " + std::to_string(step) + "u",
+                          "xv[" + std::to_string(u) + "]", "                ");
             for (int u = 0; u < 4; ++u) {
-                const std::string kk = "k + " + std::to_string(u * step) + "u";
+                const std::string kk = "k0 + (" + I + ")(j - " + std::to_string(u) + ") * " + std::to_string(step) + "u";
                 if (V == 4)
-                    body << "            pb_st4(out + " << orow << " + " << kk << ", make_float4(__expf(xv[" << u
+                    body << "                pb_st4(out + " << orow << " + " << kk << ", make_float4(__expf(xv[" << u
                          << "][0] - m) * rs, __expf(xv[" << u << "][1] - m) * rs, __expf(xv[" << u
                          << "][2] - m) * rs, __expf(xv[" << u << "][3] - m) * rs));\n";
                 else
-                    body << "            out[" << orow << " + " << kk << "] = __expf(xv[" << u << "][0] - m) * rs;\n";
+                    body << "                out[" << orow << " + " << kk << "] = __expf(xv[" << u
+                         << "][0] - m) * rs;\n";
             }
-            body << "        }\n";
-            body << "        for (; k < " << lit(A, wide) << "; k += " << step << "u) {\n";
-            body << "            float xv[" << V << "];\n";
-            emit_load("k", "xv", "            ");
-            body << "            #pragma unroll\n            for (int e = 0; e < " << V << "; ++e) out[" << orow
-                 << " + k + e] = __expf(xv[e] - m) * rs;\n";
-            body << "        }\n";
+            body << "            }\n";
+            body << "            for (; j >= 0; --j) {\n";
+            body << "                const " << I << " kj = k0 + (" << I << ")j * " << step << "u;\n";
+            body << "                float xv[" << V << "];\n";
+            emit_load("kj", "xv", "                ");
+            body << "                #pragma unroll\n                for (int e = 0; e < " << V << "; ++e) out["
+                 << orow << " + kj + e] = __expf(xv[e] - m) * rs;\n";
+            body << "            }\n        }\n";
         }
         body << "    }\n";
         launch_spec l;
