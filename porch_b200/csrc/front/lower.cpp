@@ -1470,7 +1470,7 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
                 l.grid = {static_cast<uint32_t>(ctas), 1, 1};
                 desc = "row reduction (warp per row) V=" + std::to_string(V);
             }
-        } else if (R == 2 && ax == 0 && S[1] % 4 == 0 && S[1] >= 64 && [&] {
+        } else if (R == 2 && ax == 0 && S[1] % 4 == 0 && S[1] >= 16 && [&] {
                        for (int li : order) {
                            const vnode& v = r.b.nodes[static_cast<size_t>(li)];
                            const int64_t sc = v.map.st[1];
@@ -1483,15 +1483,25 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
             // and 16-byte aligned: column tiles of 128 (a float4 per lane);
             // the 8 warps of a CTA take every 8th row of the CTA's row chunk
             // (eight float4 loads in flight per lane), then combine their
-            // partials in warp order through shared memory. Row chunks fill
-            // the GPU as in the strided form; chunk partials are combined in
-            // chunk order, so results do not depend on scheduling.
+            // partials in warp order through shared memory. Rows narrower
+            // than 128 columns pack several rows into one warp load: LPR
+            // lanes per row (a power of two covering the row), RPW = 32 / LPR
+            // rows per warp; lanes holding the same columns are combined in
+            // (warp, row) order. Row chunks fill the GPU as in the strided
+            // form; chunk partials are combined in chunk order, so results
+            // do not depend on scheduling.
             const int64_t C = S[1];
             const int64_t col_tiles = (C + 127) / 128;
+            int lpr = 32;
+            if (C < 128) {
+                lpr = 4;
+                while (lpr * 4 < C) lpr *= 2;
+            }
+            const int rpw = 32 / lpr;
             // Four CTAs per SM already keep 128 KB of loads in flight per SM;
             // more row chunks would only lengthen pass 2.
             const int64_t target = 148 * 4;
-            int64_t chunks = std::max<int64_t>(1, std::min<int64_t>((target + col_tiles - 1) / col_tiles, A / 64));
+            int64_t chunks = std::max<int64_t>(1, std::min<int64_t>((target + col_tiles - 1) / col_tiles, A / (64 * rpw)));
             const int64_t per = (A + chunks - 1) / chunks;
             chunks = (A + per - 1) / per;
             const int part = chunks > 1 ? new_temp(static_cast<size_t>(chunks * C) * sizeof(float)) : out;
@@ -1526,28 +1536,31 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
             std::ostringstream b1;
             b1 << "    __shared__ float4 red[8][32];\n";
             b1 << "    const pb_u32 warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;\n";
-            b1 << "    const " << I << " c1 = (" << I << ")blockIdx.x * 128u + lane * 4u;\n";
+            b1 << "    const pb_u32 sub = lane / " << lpr << "u, lc = lane % " << lpr << "u;\n";
+            b1 << "    (void)sub;\n";
+            b1 << "    const " << I << " c1 = (" << I << ")blockIdx.x * 128u + lc * 4u;\n";
             b1 << "    const bool active = c1 < " << lit(C, wide) << ";\n";
             b1 << "    const " << I << " k0 = (" << I << ")blockIdx.y * " << lit(per, wide) << ";\n";
             b1 << "    const " << I << " k1 = k0 + " << lit(per, wide) << " < " << lit(A, wide) << " ? k0 + "
                << lit(per, wide) << " : " << lit(A, wide) << ";\n";
             b1 << "    float4 acc = make_float4(" << init << ", " << init << ", " << init << ", " << init << ");\n";
             b1 << "    if (active) {\n";
-            b1 << "        " << I << " k = k0 + warp;\n";
-            b1 << "        for (; k + 56u < k1; k += 64u) {\n            float4 vv[8];\n";
+            b1 << "        " << I << " k = k0 + warp * " << rpw << "u + sub;\n";
+            b1 << "        for (; k + " << 56 * rpw << "u < k1; k += " << 64 * rpw << "u) {\n            float4 vv[8];\n";
             b1 << "            #pragma unroll\n            for (int u = 0; u < 8; ++u)\n";
-            value4(b1, "k + 8u * (" + I + ")u", "vv[u]", "            ");
+            value4(b1, "k + " + std::to_string(8 * rpw) + "u * (" + I + ")u", "vv[u]", "            ");
             b1 << "            #pragma unroll\n            for (int u = 0; u < 8; ++u) {\n";
             combine4(b1, "acc", "vv[u]", "                ");
             b1 << "            }\n        }\n";
-            b1 << "        for (; k < k1; k += 8u) {\n            float4 v;\n";
+            b1 << "        for (; k < k1; k += " << 8 * rpw << "u) {\n            float4 v;\n";
             value4(b1, "k", "v", "            ");
             combine4(b1, "acc", "v", "            ");
             b1 << "        }\n    }\n";
             b1 << "    red[warp][lane] = acc;\n    __syncthreads();\n";
-            b1 << "    if (warp == 0 && active) {\n";
-            b1 << "        float4 s = red[0][lane];\n";
-            b1 << "        #pragma unroll\n        for (int w = 1; w < 8; ++w) {\n            const float4 v = red[w][lane];\n";
+            b1 << "    if (warp == 0 && sub == 0u && active) {\n";
+            b1 << "        float4 s = red[0][lc];\n";
+            b1 << "        #pragma unroll\n        for (int q = 1; q < " << 8 * rpw << "; ++q) {\n"
+               << "            const float4 v = red[q / " << rpw << "][(q % " << rpw << ") * " << lpr << " + lc];\n";
             combine4(b1, "s", "v", "            ");
             b1 << "        }\n";
             b1 << "        pb_st4(" << (chunks > 1 ? "part" : "out") << " + (" << PI << ")blockIdx.y * " << lit(C, pwide)
@@ -1560,7 +1573,8 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
             s1 << "float* __restrict__ " << (chunks > 1 ? "part" : "out") << ") {\n" << b1.str() << "}\n";
             l1.source = s1.str();
             l1.schedule = std::string(is_sum ? "sum " : "max ") + "column reduction (128-column tiles, 8 warps on " +
-                          "interleaved rows, " + std::to_string(chunks) + " row chunks of " + std::to_string(per) + ")";
+                          "interleaved rows" + (rpw > 1 ? ", " + std::to_string(rpw) + " rows per warp load" : "") +
+                          ", " + std::to_string(chunks) + " row chunks of " + std::to_string(per) + ")";
             l1.grid = {static_cast<uint32_t>(col_tiles), static_cast<uint32_t>(chunks), 1};
             l1.block = {256, 1, 1};
             l1.args = r.k.leaves;

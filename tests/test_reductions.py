@@ -30,7 +30,12 @@ CASES = [
     ([1000, 260], 0, False, "sum", "exp"),
     ([1003, 128], 0, True, "max", None),
     ([64, 128], 0, False, "max", "relu"),
-    # Narrow or transposed columns keep the thread-per-output form:
+    # Narrow rows: several rows per warp load (2, 4 and 8 rows).
+    ([1048576, 64], 0, False, "sum", None),
+    ([100000, 32], 0, True, "max", "relu"),
+    ([65536, 16], 0, False, "sum", "exp"),
+    ([333, 20], 0, False, "max", None),
+    # Narrower or transposed columns keep the thread-per-output form:
     ([100000, 4], 0, False, "sum", None),
     ([300, 8], 0, False, "max", None),
     ([2048, 384], 0, False, "sum", "transpose"),
