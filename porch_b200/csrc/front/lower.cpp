@@ -19,7 +19,8 @@
 //    unaligned slice and the like) fall back to a per-element gather kernel.
 //  - sum/max along an axis, the operand expression fused in: a warp per row
 //    (contiguous axis), a CTA per row for few long rows, 128-column tiles
-//    for axis 0 of a 2-D operand with aligned rows, else a thread per
+//    for the second-to-last axis of an operand with aligned rows (axis 0
+//    of [A, C], the middle axis of [B, A, C]), else a thread per
 //    output (strided axis); tall inputs split into row chunks whose
 //    partials a second pass combines in a fixed order.
 //  - the ops.hpp softmax shape over the last axis: one row kernel, not four
@@ -1470,17 +1471,23 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
                 l.grid = {static_cast<uint32_t>(ctas), 1, 1};
                 desc = "row reduction (warp per row) V=" + std::to_string(V);
             }
-        } else if (R == 2 && ax == 0 && S[1] % 4 == 0 && S[1] >= 16 && [&] {
+        } else if (R >= 2 && static_cast<int>(ax) == R - 2 && S[static_cast<size_t>(R - 1)] % 4 == 0 &&
+                   S[static_cast<size_t>(R - 1)] >= 16 && outer <= 65535 && [&] {
                        for (int li : order) {
                            const vnode& v = r.b.nodes[static_cast<size_t>(li)];
-                           const int64_t sc = v.map.st[1];
-                           if (sc == 1 && (affine_at(v.map, r.b.lo) % 4 != 0 || v.map.st[0] % 4 != 0)) return false;
+                           const int64_t sc = v.map.st[static_cast<size_t>(R - 1)];
                            if (sc != 0 && sc != 1) return false;
+                           if (sc == 0) continue;
+                           if (affine_at(v.map, r.b.lo) % 4 != 0) return false;
+                           for (int d = 0; d < R - 1; ++d)
+                               if (v.map.st[static_cast<size_t>(d)] % 4 != 0 && S[static_cast<size_t>(d)] > 1) return false;
                        }
                        return true;
                    }()) {
-            // Column reduction of a [A, C] operand whose rows are unit-stride
-            // and 16-byte aligned: column tiles of 128 (a float4 per lane);
+            // Reduction over the second-to-last axis of an [..., A, C]
+            // operand whose rows are unit-stride and 16-byte aligned (axis 0
+            // of a 2-D operand; the middle axis of [B, A, C], one batch per
+            // blockIdx.z): column tiles of 128 (a float4 per lane);
             // the 8 warps of a CTA take every 8th row of the CTA's row chunk
             // (eight float4 loads in flight per lane), then combine their
             // partials in warp order through shared memory. Rows narrower
@@ -1490,7 +1497,7 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
             // (warp, row) order. Row chunks fill the GPU as in the strided
             // form; chunk partials are combined in chunk order, so results
             // do not depend on scheduling.
-            const int64_t C = S[1];
+            const int64_t C = S[static_cast<size_t>(R - 1)];
             const int64_t col_tiles = (C + 127) / 128;
             int lpr = 32;
             if (C < 128) {
@@ -1501,11 +1508,13 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
             // Four CTAs per SM already keep 128 KB of loads in flight per SM;
             // more row chunks would only lengthen pass 2.
             const int64_t target = 148 * 4;
-            int64_t chunks = std::max<int64_t>(1, std::min<int64_t>((target + col_tiles - 1) / col_tiles, A / (64 * rpw)));
+            int64_t chunks = std::max<int64_t>(
+                1, std::min<int64_t>((target + col_tiles * outer - 1) / (col_tiles * outer), A / (64 * rpw)));
             const int64_t per = (A + chunks - 1) / chunks;
             chunks = (A + per - 1) / per;
-            const int part = chunks > 1 ? new_temp(static_cast<size_t>(chunks * C) * sizeof(float)) : out;
-            const bool pwide = wide || chunks * C >= (int64_t{1} << 31) - 4096;
+            const int part = chunks > 1 ? new_temp(static_cast<size_t>(chunks * outputs) * sizeof(float)) : out;
+            const bool pwide = wide || chunks * outputs >= (int64_t{1} << 31) - 4096;
+            const std::string cax = "c" + std::to_string(ax), ccol = "c" + std::to_string(R - 1);
             const std::string PI = pwide ? "pb_u64" : "pb_u32";
             const char* comps[4] = {"x", "y", "z", "w"};
             auto combine4 = [&](std::ostringstream& os, const std::string& acc, const std::string& v,
@@ -1515,11 +1524,11 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
             };
             auto value4 = [&](std::ostringstream& os, const std::string& k, const std::string& dst,
                               const std::string& ind) {
-                os << ind << "{\n" << ind << "    const " << I << " c0 = " << k << ";\n";
+                os << ind << "{\n" << ind << "    const " << I << " " << cax << " = " << k << ";\n";
                 for (size_t li = 0; li < order.size(); ++li) {
                     const vnode& v = r.b.nodes[static_cast<size_t>(order[li])];
                     const std::string addr = address(v.map, cvar, wide, -1);
-                    if (v.map.st[1] == 1)
+                    if (v.map.st[static_cast<size_t>(R - 1)] == 1)
                         os << ind << "    const float4 x" << li << " = pb_ld4(in" << v.buffer << " + " << addr << ");\n";
                     else
                         os << ind << "    const float s" << li << " = pb_ld(in" << v.buffer << " + " << addr
@@ -1538,8 +1547,13 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
             b1 << "    const pb_u32 warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;\n";
             b1 << "    const pb_u32 sub = lane / " << lpr << "u, lc = lane % " << lpr << "u;\n";
             b1 << "    (void)sub;\n";
-            b1 << "    const " << I << " c1 = (" << I << ")blockIdx.x * 128u + lc * 4u;\n";
-            b1 << "    const bool active = c1 < " << lit(C, wide) << ";\n";
+            b1 << "    const " << I << " " << ccol << " = (" << I << ")blockIdx.x * 128u + lc * 4u;\n";
+            b1 << "    const bool active = " << ccol << " < " << lit(C, wide) << ";\n";
+            // Batch coordinates (the dimensions before the reduced axis).
+            b1 << "    " << I << " bt = blockIdx.z;\n    (void)bt;\n";
+            for (int d = static_cast<int>(ax) - 1; d >= 0; --d)
+                b1 << "    const " << I << " c" << d << " = bt % " << lit(S[static_cast<size_t>(d)], wide) << "; bt /= "
+                   << lit(S[static_cast<size_t>(d)], wide) << ";\n";
             b1 << "    const " << I << " k0 = (" << I << ")blockIdx.y * " << lit(per, wide) << ";\n";
             b1 << "    const " << I << " k1 = k0 + " << lit(per, wide) << " < " << lit(A, wide) << " ? k0 + "
                << lit(per, wide) << " : " << lit(A, wide) << ";\n";
@@ -1563,8 +1577,9 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
                << "            const float4 v = red[q / " << rpw << "][(q % " << rpw << ") * " << lpr << " + lc];\n";
             combine4(b1, "s", "v", "            ");
             b1 << "        }\n";
-            b1 << "        pb_st4(" << (chunks > 1 ? "part" : "out") << " + (" << PI << ")blockIdx.y * " << lit(C, pwide)
-               << " + (" << PI << ")c1, s);\n    }\n";
+            b1 << "        pb_st4(" << (chunks > 1 ? "part" : "out") << " + (" << PI << ")blockIdx.y * "
+               << lit(outputs, pwide) << " + (" << PI << ")blockIdx.z * " << lit(C, pwide) << " + (" << PI << ")"
+               << ccol << ", s);\n    }\n";
             launch_spec l1;
             l1.name = "pb_reduce_cols_" + hex64(hash_string(src.str() + b1.str())).substr(0, 8);
             std::ostringstream s1;
@@ -1575,7 +1590,7 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
             l1.schedule = std::string(is_sum ? "sum " : "max ") + "column reduction (128-column tiles, 8 warps on " +
                           "interleaved rows" + (rpw > 1 ? ", " + std::to_string(rpw) + " rows per warp load" : "") +
                           ", " + std::to_string(chunks) + " row chunks of " + std::to_string(per) + ")";
-            l1.grid = {static_cast<uint32_t>(col_tiles), static_cast<uint32_t>(chunks), 1};
+            l1.grid = {static_cast<uint32_t>(col_tiles), static_cast<uint32_t>(chunks), static_cast<uint32_t>(outer)};
             l1.block = {256, 1, 1};
             l1.args = r.k.leaves;
             kernel_arg pa;

@@ -35,6 +35,11 @@ CASES = [
     ([100000, 32], 0, True, "max", "relu"),
     ([65536, 16], 0, False, "sum", "exp"),
     ([333, 20], 0, False, "max", None),
+    # The middle axis of [B, A, C]: column tiles, one batch per blockIdx.z.
+    ([32, 2048, 1024], 1, False, "sum", None),
+    ([7, 300, 260], 1, True, "max", "exp"),
+    ([64, 4096, 64], 1, False, "sum", "relu"),
+    ([2, 3, 5, 40], 2, False, "max", None),
     # Narrower or transposed columns keep the thread-per-output form:
     ([100000, 4], 0, False, "sum", None),
     ([300, 8], 0, False, "max", None),
@@ -109,6 +114,12 @@ def test_few_long_rows_plan_a_cta_per_row(api):
     e = _placeholder_expr(api, _program([65536, 1024], 1, False, "sum", None), [65536, 1024])
     kernels = [line for line in api.describe(e).splitlines() if line.startswith("kernel ")]
     assert "warp per row" in kernels[0], kernels
+
+
+def test_middle_axis_plans_batched_column_tiles(api):
+    e = _placeholder_expr(api, _program([32, 2048, 1024], 1, False, "sum", None), [32, 2048, 1024])
+    kernels = [line for line in api.describe(e).splitlines() if line.startswith("kernel ")]
+    assert "column reduction (128-column tiles" in kernels[0] and "x32 block" in kernels[0], kernels
 
 
 def test_wide_row_reduction_stays_one_pass(api):
