@@ -1472,7 +1472,7 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
                 desc = "row reduction (warp per row) V=" + std::to_string(V);
             }
         } else if (R >= 2 && static_cast<int>(ax) == R - 2 && S[static_cast<size_t>(R - 1)] % 4 == 0 &&
-                   S[static_cast<size_t>(R - 1)] >= 16 && outer <= 65535 && [&] {
+                   S[static_cast<size_t>(R - 1)] >= 4 && outer <= 65535 && [&] {
                        for (int li : order) {
                            const vnode& v = r.b.nodes[static_cast<size_t>(li)];
                            const int64_t sc = v.map.st[static_cast<size_t>(R - 1)];
@@ -1491,7 +1491,8 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
             // the 8 warps of a CTA take every 8th row of the CTA's row chunk
             // (eight float4 loads in flight per lane), then combine their
             // partials in warp order through shared memory. Rows narrower
-            // than 128 columns pack several rows into one warp load: LPR
+            // than 128 columns (down to 4) pack several rows into one warp
+            // load: LPR
             // lanes per row (a power of two covering the row), RPW = 32 / LPR
             // rows per warp; lanes holding the same columns are combined in
             // (warp, row) order. Row chunks fill the GPU as in the strided
@@ -1501,7 +1502,7 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
             const int64_t col_tiles = (C + 127) / 128;
             int lpr = 32;
             if (C < 128) {
-                lpr = 4;
+                lpr = 1;
                 while (lpr * 4 < C) lpr *= 2;
             }
             const int rpw = 32 / lpr;
@@ -1573,7 +1574,7 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
             b1 << "    red[warp][lane] = acc;\n    __syncthreads();\n";
             b1 << "    if (warp == 0 && sub == 0u && active) {\n";
             b1 << "        float4 s = red[0][lc];\n";
-            b1 << "        #pragma unroll\n        for (int q = 1; q < " << 8 * rpw << "; ++q) {\n"
+            b1 << "        #pragma unroll 8\n        for (int q = 1; q < " << 8 * rpw << "; ++q) {\n"
                << "            const float4 v = red[q / " << rpw << "][(q % " << rpw << ") * " << lpr << " + lc];\n";
             combine4(b1, "s", "v", "            ");
             b1 << "        }\n";

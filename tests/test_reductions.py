@@ -40,9 +40,12 @@ CASES = [
     ([7, 300, 260], 1, True, "max", "exp"),
     ([64, 4096, 64], 1, False, "sum", "relu"),
     ([2, 3, 5, 40], 2, False, "max", None),
-    # Narrower or transposed columns keep the thread-per-output form:
+    # 4 and 8 columns: 32 and 16 rows per warp load.
     ([100000, 4], 0, False, "sum", None),
     ([300, 8], 0, False, "max", None),
+    ([64, 4096, 8], 1, True, "sum", "exp"),
+    # Columns not a multiple of 4, or transposed: thread per output.
+    ([100000, 6], 0, False, "sum", None),
     ([2048, 384], 0, False, "sum", "transpose"),
     # Few long rows: a CTA per row (8 warps share it).
     ([4096, 16384], 1, False, "sum", None),
@@ -91,7 +94,7 @@ def test_tall_leading_axis_reduction_plans_two_passes(api):
     kernels = [line for line in plan.splitlines() if line.startswith("kernel ")]
     assert len(kernels) == 2, plan
     assert "column reduction (128-column tiles" in kernels[0] and "pass 2" in kernels[1], plan
-    e = _placeholder_expr(api, _program([100000, 4], 0, False, "sum", None), [100000, 4])
+    e = _placeholder_expr(api, _program([100000, 6], 0, False, "sum", None), [100000, 6])
     kernels = [line for line in api.describe(e).splitlines() if line.startswith("kernel ")]
     assert len(kernels) == 2 and "pass 1" in kernels[0] and "pass 2" in kernels[1], kernels
 
