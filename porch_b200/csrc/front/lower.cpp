@@ -21,7 +21,8 @@
 //    (contiguous axis), a CTA per row for few long rows, 128-column tiles
 //    for the second-to-last axis of an operand with aligned rows (axis 0
 //    of [A, C], the middle axis of [B, A, C]), else a thread per
-//    output (strided axis); tall inputs split into row chunks whose
+//    output (strided axis); dimensions after the axis that every load
+//    walks contiguously merge first; tall inputs split into row chunks whose
 //    partials a second pass combines in a fixed order.
 //  - the ops.hpp softmax shape over the last axis: one row kernel, not four
 //    kernels -- rows held in registers (one HBM read and one write); for few
@@ -1223,6 +1224,38 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
         const gnode& n = g_.nodes[static_cast<size_t>(id)];
         const bool is_sum = n.kind == expr_kind::sum;
         row_operand r = row_prologue(n.a, n.axis);
+        // Dimensions after the reduced axis that every load walks
+        // contiguously (or not at all) merge into one: [A, B, C] over axis
+        // 0 becomes [A, B*C], which the column-tile schedule reads as
+        // float4. The outputs keep their order, so nothing else changes.
+        if (n.axis + 2 < r.shape.size()) {
+            const size_t a0 = n.axis + 1, last = r.shape.size() - 1;
+            bool ok = true;
+            for (size_t d = a0; d <= last && ok; ++d)
+                ok = r.b.lo[d] == 0 && r.b.hi[d] == r.shape[d];
+            for (const vnode& v : r.b.nodes) {
+                if (!ok) break;
+                if (v.kind != vnode::op::load) continue;
+                for (size_t d = a0; d < last && ok; ++d)
+                    ok = r.shape[d] == 1 || v.map.st[d] == v.map.st[d + 1] * r.shape[d + 1];
+            }
+            if (ok) {
+                int64_t merged = 1;
+                for (size_t d = a0; d <= last; ++d) merged *= r.shape[d];
+                for (vnode& v : r.b.nodes)
+                    if (v.kind == vnode::op::load) {
+                        const int64_t st_last = v.map.st[last];
+                        v.map.st.resize(a0);
+                        v.map.st.push_back(st_last);
+                    }
+                r.shape.resize(a0);
+                r.shape.push_back(merged);
+                r.b.lo.resize(a0);
+                r.b.lo.push_back(0);
+                r.b.hi.resize(a0);
+                r.b.hi.push_back(merged);
+            }
+        }
         const std::vector<index_t>& S = r.shape;
         rank_ = static_cast<int>(S.size());
         const int R = rank_;

@@ -40,6 +40,11 @@ CASES = [
     ([7, 300, 260], 1, True, "max", "exp"),
     ([64, 4096, 64], 1, False, "sum", "relu"),
     ([2, 3, 5, 40], 2, False, "max", None),
+    # Contiguous trailing dimensions merge: [A, B, C] over axis 0 reads as
+    # [A, B*C]; [64, 32, 16, 8] over axis 1 as a batch of [32, 128].
+    ([4096, 64, 256], 0, False, "sum", None),
+    ([64, 32, 16, 8], 1, True, "max", "relu"),
+    ([8, 3, 5, 7], 0, False, "sum", "exp"),
     # 4 and 8 columns: 32 and 16 rows per warp load.
     ([100000, 4], 0, False, "sum", None),
     ([300, 8], 0, False, "max", None),
@@ -162,3 +167,25 @@ def test_cuda_reductions_match_oracle(gpu, case):
         x = _host_prologue(ins[0].astype(np.float64), prologue)
         abs_sum = np.abs(x).sum(axis=axis, keepdims=keepdim)
         assert_sum_close(got, want, abs_sum, x.shape[axis], REL_TOL, str(case))
+
+
+def test_trailing_dimensions_merge_only_when_contiguous(api):
+    e = _placeholder_expr(api, _program([4096, 64, 256], 0, False, "sum", None), [4096, 64, 256])
+    kernels = [line for line in api.describe(e).splitlines() if line.startswith("kernel ")]
+    assert "column reduction (128-column tiles" in kernels[0] and "grid=128x" in kernels[0], kernels
+    x = api.placeholder([64, 16, 300])
+    kernels = [line for line in api.describe(api.sum(x[:, :, 0:256], 0)).splitlines() if line.startswith("kernel ")]
+    assert "strided reduction" in kernels[0], kernels
+
+
+@pytest.mark.gpu
+def test_sliced_trailing_dimensions_match_oracle(gpu):
+    """A slice breaks the contiguity of the trailing dimensions: no merge,
+    thread per output; same results as the oracle."""
+    rng = np.random.default_rng(17)
+    x = rng.normal(0, 1, (512, 16, 300)).astype(np.float32)
+    program = "0 input 0\n1 tensor 0\n2 index 1 s0:512:1;s0:16:1;s3:259:1\n3 sum 2 0 0\n"
+    got = graphs.evaluate_product(gpu, program, [x])
+    want = graphs.evaluate_oracle(program, [x])
+    abs_sum = np.abs(x[:, :, 3:259].astype(np.float64)).sum(axis=0)
+    assert_sum_close(got, want, abs_sum, 512, REL_TOL, "sliced sum over axis 0")
