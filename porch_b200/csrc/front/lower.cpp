@@ -1794,8 +1794,8 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
         body << "    __shared__ float red_m[32], red_s[32];\n";
         body << "    const pb_u32 warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;\n";
         // Declares the row coordinates c0..c(ax-1) of row `r` in a scope.
-        auto emit_row_coords = [&](const std::string& r, const std::string& indent) {
-            body << indent << I << " t = " << r << ";\n";
+        auto emit_row_coords = [&](const std::string& row_expr, const std::string& indent) {
+            body << indent << I << " t = " << row_expr << ";\n";
             for (int d = static_cast<int>(ax) - 1; d >= 0; --d)
                 body << indent << "const " << I << " c" << d << " = t % " << lit(S[static_cast<size_t>(d)], wide)
                      << "; t /= " << lit(S[static_cast<size_t>(d)], wide) << ";\n";
@@ -1847,9 +1847,9 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
             // Software pipeline over the CTA's rows: the next row's loads are
             // issued before this row's reductions, so HBM stays busy while
             // the block waits at its barriers.
-            auto emit_row_loads = [&](const std::string& r, const std::string& dst, const std::string& indent) {
+            auto emit_row_loads = [&](const std::string& row_expr, const std::string& dst, const std::string& indent) {
                 body << indent << "{\n";
-                emit_row_coords(r, indent + "    ");
+                emit_row_coords(row_expr, indent + "    ");
                 body << indent << "    #pragma unroll\n" << indent << "    for (int it = 0; it < " << NI << "; ++it) {\n";
                 body << indent << "        const " << I << " k = ((" << I << ")it * " << T << "u + threadIdx.x) * " << V
                      << "u;\n";
