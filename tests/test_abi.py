@@ -142,6 +142,27 @@ def test_fuzz_plans_compile_for_sm100a(api, seed):
     assert "kernel pb_" in api.describe(node)
 
 
+def test_every_generated_kernel_waits_for_its_predecessor(api):
+    """Kernels launch with programmatic stream serialization, so each must
+    execute griddepcontrol.wait before anything else: every kernel of the
+    benchmark plans and of the long-row, column and GEMM schedules."""
+    exprs = list(api.benchmark_graphs(placeholder=True).values())
+    x = api.placeholder([64, 65536])
+    exprs += [api.softmax(x, 1), api.sum(api.placeholder([262144, 256]), 0),
+              api.softmax(api.placeholder([4096, 32768]), 1),
+              api.matmul(api.placeholder([128, 4100]), api.placeholder([4100, 4096]))]
+    seen = 0
+    for e in exprs:
+        text = api.describe(e, True)
+        for block in re.split(r"^kernel \S+ .*$", text, flags=re.M)[1:]:
+            body = block[block.index("__global__"):]
+            first = body[body.index("{") + 1:].lstrip()
+            assert first.startswith('asm volatile("griddepcontrol.wait;"'), first[:120]
+            assert body.count("__global__") == 1
+            seen += 1
+    assert seen >= 20
+
+
 def test_placeholders_refuse_to_compute(api):
     p = api.placeholder([4])
     with pytest.raises(RuntimeError):
