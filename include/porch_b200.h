@@ -225,6 +225,11 @@ int pb_comm_wait(pb_comm* comm);
  * owns the device, or an allocation would synchronise or fail where they
  * call). A, B, C are row-major device arrays on the current device:
  * A [M,K], B [K,N], C [M,N]; M % 128 == 0, N % 256 == 0, K % 64 == 0.
+ * A and C must be 16-byte aligned (they are read and written in float4s),
+ * B 4-byte aligned; all three must be device (or managed) memory of the
+ * current device. Misaligned, host or other-device pointers, and buffers
+ * that end before their shape does within one allocation, are rejected
+ * with PB_ERR_INVALID_ARGUMENT before anything is enqueued.
  * The split operands live in a fixed 64 MiB device array that every GPU
  * loading this library holds until exit; calls needing more than that
  * (2 * (M*K + N*K) floats) are rejected with PB_ERR_INVALID_ARGUMENT.

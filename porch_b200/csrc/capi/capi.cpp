@@ -97,10 +97,9 @@ int pb_tensor_create(const int64_t* shape, size_t rank, const float* values, siz
         if (count != 0) require(values, "values");
         int ndev = 0;
         porch::detail::check(pbrt_device_count(&ndev));
-        if (device < 0) throw std::invalid_argument("CUDA device ordinal must be non-negative");
         auto storage = std::make_shared<porch::detail::realized_storage>();
         storage->count = count;
-        storage->device = device % ndev;
+        storage->device = porch::detail::checked_ordinal(device, ndev);
         auto stream = porch::detail::current_stream(storage->device);
         storage->device_values =
             porch::detail::allocate(storage->device, count * sizeof(float), stream);

@@ -219,6 +219,9 @@ namespace porch::detail {
 
     size_t checked_numel(std::span<const index_t> shape);
     std::vector<index_t> contiguous_strides(std::span<const index_t> shape);
+    // `ordinal` as a device index among `count` visible devices; throws
+    // std::invalid_argument when it is negative or not present.
+    int checked_ordinal(int ordinal, int count);
 
     // Lower, compile and launch `root`; the result is a realised tensor on the
     // graph's device (src/tensor.cpp:1002-1066 is the reference's driver).

@@ -76,6 +76,16 @@ namespace porch {
             return count;
         }
 
+        int checked_ordinal(int ordinal, int count) {
+            if (ordinal < 0)
+                throw std::invalid_argument("CUDA device ordinal must be non-negative");
+            if (ordinal >= count)
+                throw std::invalid_argument("CUDA device ordinal " + std::to_string(ordinal) +
+                                            " is not present (" + std::to_string(count) +
+                                            " visible devices)");
+            return ordinal;
+        }
+
         std::vector<index_t> contiguous_strides(std::span<const index_t> shape) {
             std::vector<index_t> strides(shape.size(), 1);
             index_t stride = 1;
@@ -295,12 +305,8 @@ namespace porch {
                 check(pbrt_device_count(&count));
                 // The reference treats the ordinal as metadata and always runs on
                 // device 0 (src/cuda_jit.cpp:446-450). Here ordinals address real
-                // devices; ordinals beyond the visible count wrap around so
-                // programs written for larger machines still run.
-                const int ordinal = placement.ordinal();
-                if (ordinal < 0)
-                    throw std::invalid_argument("CUDA device ordinal must be non-negative");
-                return ordinal % count;
+                // devices, so one that is not present is an argument error.
+                return checked_ordinal(placement.ordinal(), count);
             }
         } // namespace
 

@@ -260,3 +260,19 @@ def test_strided_axis_and_inner_softmax_match_oracle(gpu, case):
         assert_sum_close(got, want, x.sum(axis=1), 100, 1e-5, program)
     else:
         assert_relative(got, want, 1e-5, program)
+
+
+@pytest.mark.gpu
+def test_device_ordinal_not_present_is_an_argument_error(gpu):
+    """device{n} addresses GPU n; an ordinal past the visible devices is an
+    std::invalid_argument (it used to wrap around to n % count)."""
+    api = gpu
+    count = api.device_count()
+    values = np.arange(4, dtype=np.float32)
+    with pytest.raises(ValueError, match="is not present"):
+        api.tensor([4], values, device=count)
+    with pytest.raises(ValueError, match="non-negative"):
+        api.tensor([4], values, device=-1)
+    # The last present device still works.
+    t = api.tensor([4], values, device=count - 1)
+    assert_bitwise(api.materialize(t + 1.0).cpu(), values + 1.0, "last device")
