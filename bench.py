@@ -1,23 +1,29 @@
 """Benchmark: porch lazy-graph hot path on B200.
 
-Default workload (N=1): config 2 of the baseline, the fused view/indexing
-graph concat(transpose(X[0::2, 1024:7168]) + broadcast(b), Y, 0) ->
-[12288, 4096] fp32, metric "fused-graph HBM GB/s" (algorithmic bytes per
-realisation / time). Other workloads: --workload c1_elementwise |
-c3a_softmax | c3b_relu_logistic | c4_matmul | c5_mlp.
+Headline workload: config 5 of the baseline, the two-layer MLP realised as
+one lazy graph P = softmax(logistic(X@W1 + b1)@W2 + b2, 1) with
+X [16384,4096], W1 [4096,16384], W2 [16384,4096] in fp32 (tcgen05 3xTF32
+GEMMs with fused epilogues), metric "fp32 matmul TFLOP/s". The same run
+times every other configuration of the baseline and reports each under
+"extra" with its own value, roofline, e2e and cpu_baseline: config 1
+((a+b)*2-1), config 2 (slice/transpose/bias/concat), configs 3a/3b (softmax,
+logistic(relu)) and config 4 (relu(A@B + bias)); --no-extra skips them and
+--workload picks another headline.
 
-Multi-GPU (python -m torch.distributed.run ... bench.py --gpus N): the
-default graph does not shard, so every rank realises its own replica on its
-own GPU (weak scaling, no data-path collective); torch.distributed (gloo)
-carries only the barrier and the max-over-ranks timing. Row-shardable
-workloads (c3a/c3b/c5) split their rows across ranks in contiguous blocks
-(strong scaling): each rank realises its block on its own GPU; c5's output P
-is then gathered whole on every rank with one ncclAllGather over NVLink per
-step (porch_b200 Communicator.allgather_rows), inside the timed region.
+Multi-GPU (python -m torch.distributed.run ... bench.py --gpus N): config 5
+splits X's rows across ranks in contiguous blocks (W1, W2 replicated, strong
+scaling); each rank realises its block on its own GPU and P is gathered
+whole on every rank with one ncclAllGather over NVLink per step (porch_b200
+Communicator.allgather_rows), inside the timed region. Configs 3a/3b are
+reported row-sharded too (no exchange: no consumer needs them whole); the
+single-GPU configs 1, 2 and 4 are reported at N=1 only. torch.distributed
+(gloo) carries only barriers and the max-over-ranks timing.
 
 --impl reference runs the reference's own implementation of the path
 (oracle/_ref/ref_runner: AkhilSamavedam/porch compiled from its sources,
-NVRTC JIT on the same GPU) on rank 0 and prints the same metric.
+NVRTC JIT on the same GPU) on rank 0 and prints the same metric for the same
+workloads. It has no multi-GPU path: its one-GPU number is the baseline at
+every N.
 """
 
 from __future__ import annotations
@@ -198,10 +204,7 @@ def make_host_inputs(api, workload: str, rank: int, world: int):
     return arrays
 
 
-CPU_SECONDS = 10.0
-
-
-def cpu_baseline(workload: str, arrays) -> dict:
+def cpu_baseline(workload: str, arrays, seconds: float = 10.0) -> dict:
     """The host oracle on a bounded sample of the same workload."""
     from oracle.graph import Program
 
@@ -252,14 +255,14 @@ def cpu_baseline(workload: str, arrays) -> dict:
             nbytes = 4 * rows * arrays[1].shape[0] * arrays[1].shape[1]
         sample = f"{rows} output rows"
     # The sample is evaluated again and again (the oracle keeps no results
-    # between evaluations) until about CPU_SECONDS of host work are timed.
+    # between evaluations) until about `seconds` of host work are timed.
     reps = 0
     t0 = time.perf_counter()
     while True:
         P.evaluate(node)
         reps += 1
         dt = time.perf_counter() - t0
-        if dt >= CPU_SECONDS or dt / reps * (reps + 1) > 3 * CPU_SECONDS:
+        if dt >= seconds or dt / reps * (reps + 1) > 3 * seconds:
             break
     unit = "GFLOP/s" if CONFIGS[workload][2] == "tensor" else "GB/s"
     value = nbytes * reps / dt / 1e9
@@ -267,10 +270,20 @@ def cpu_baseline(workload: str, arrays) -> dict:
             "sample": f"{sample}, evaluated {reps} times", "seconds": round(dt, 3)}
 
 
-def run_ours(args, rank, world, local, dist):
-    from porch_b200 import api
+def _config_keys(workload: str, world: int) -> dict:
+    specs = CONFIGS[workload][0]
+    return {"workload": workload,
+            "shapes": {k: s for k, (s, *_) in zip(KEYS[workload], specs)},
+            "parallelism": (f"row-shard x{world}" if workload in ROW_SHARDED and world > 1
+                            else (f"replicas x{world}" if world > 1 else "single GPU"))}
 
-    workload = args.workload
+
+def measure(api, workload: str, args, rank, world, local, dist, cpu_seconds: float | None,
+            two_threads: bool) -> dict:
+    """Times `args.steps` steps of `workload` after `args.warmup` warm-up
+    steps on this rank's GPU (max over ranks), then the same steps with
+    events around every launch (roofline), then end to end through the
+    C-ABI from pinned host memory; returns the record."""
     specs, work, bound = CONFIGS[workload]
     keys = KEYS[workload]
     device = local
@@ -440,7 +453,7 @@ def run_ours(args, rank, world, local, dist):
     # Skipped when a step holds a collective: threads would interleave the
     # ranks' collectives in different orders.
     e2e_threads = None
-    if comm is None:
+    if comm is None and two_threads:
         n_threads = 2
         per_thread = max(1, e2e_steps // n_threads)
         t_bufs = [api.PinnedBuffer(out_count) for _ in range(n_threads)]
@@ -479,45 +492,73 @@ def run_ours(args, rank, world, local, dist):
                        "unit": unit, "ms_per_step": round(thr_ms, 4), "errors": errors or None}
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and cpu_seconds:
         try:
-            cpu = cpu_baseline(workload, arrays)
+            cpu = cpu_baseline(workload, arrays, cpu_seconds)
         except Exception as exc:  # the baseline must not sink the bench line
             cpu = {"error": str(exc)}
 
     if comm is not None:
         outs.clear()
         comm.close()
+    outs.clear()
+    del graphs, sets
+    config = _config_keys(workload, world)
+    return {
+        "metric": CONFIG_METRIC[workload], "value": round(value, 3), "unit": unit,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 5), "higher_is_better": True,
+        "scaling": "strong" if workload in ROW_SHARDED else "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic (seeded; distributions as the baseline config)",
+        "config": config,
+        "setup": {"l2": f"inputs rotated over {n_sets} device-resident sets, each larger than L2",
+                  "collective": (f"ncclAllGather of the output rows ({total_rows} rows whole on every "
+                                 "rank) inside every step, on its own stream (overlapping the next "
+                                 "step's GEMMs), all complete before the timed region ends"
+                                 if comm is not None else None)},
+        "e2e": {"value": round(e2e_value, 3), "unit": unit, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4),
+                "copy_bound": {"h2d_gbs": round(bw["h2d_gbs"], 2), "d2h_gbs": round(bw["d2h_gbs"], 2),
+                               "ms": round((h2d / bw["h2d_gbs"] + d2h / bw["d2h_gbs"]) / 1e6, 4),
+                               "frac": round((h2d / bw["h2d_gbs"] + d2h / bw["d2h_gbs"]) / 1e6 / e2e_ms, 4),
+                               "how": "pinned 256 MiB H2D and D2H copies timed alone (best of 3)"},
+                "two_threads": e2e_threads,
+                "path": "pb_tensor_create from pinned host -> pb_materialize -> pb_tensor_read"
+                        + (" (after pb_allgather_rows)" if comm is not None else "")},
+        "gpu_launches": launches,
+        "roofline": roofline,
+        "cpu_baseline": cpu,
+        "clocks": clock_summary,
+        "kernels": {k: {"launches": n, "ms": round(t, 4)} for k, (n, t) in prof.items()},
+        "host_us_per_materialize": {k: round(v, 2) for k, v in host.items()},
+    }
+
+
+# Reported beside the headline in the same run: single-GPU configurations at
+# N = 1 only, the row-sharded ones at every N.
+EXTRA_SINGLE = ["c1_elementwise", "c2_view", "c4_matmul"]
+EXTRA_SHARDED = ["c3a_softmax", "c3b_relu_logistic"]
+
+
+def run_ours(args, rank, world, local, dist):
+    from porch_b200 import api
+
+    line = measure(api, args.workload, args, rank, world, local, dist,
+                   None if args.no_cpu_baseline else 10.0, two_threads=True)
+    extra = {}
+    if not args.no_extra:
+        names = (EXTRA_SINGLE if world == 1 else []) + EXTRA_SHARDED
+        for name in sorted(n for n in names if n != args.workload):
+            api.empty_cache(local)
+            r = measure(api, name, args, rank, world, local, dist,
+                        None if args.no_cpu_baseline else 5.0, two_threads=False)
+            extra[name] = {k: r[k] for k in ("metric", "value", "unit", "ms_per_step", "scaling", "config",
+                                              "e2e", "gpu_launches", "roofline", "cpu_baseline", "clocks",
+                                              "kernels")}
+        api.empty_cache(local)
     if rank == 0:
-        line = {
-            "metric": CONFIG_METRIC[workload], "value": round(value, 3), "unit": unit,
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(ms, 5), "higher_is_better": True,
-            "scaling": "strong" if workload in ROW_SHARDED else "weak", "vs_baseline": None,
-            "dtype": "f32", "data": "synthetic (seeded; distributions as the baseline config)",
-            "config": {"workload": workload, "shapes": {k: s for k, (s, *_) in zip(keys, specs)},
-                       "parallelism": (f"row-shard x{world}" if workload in ROW_SHARDED and world > 1
-                                       else (f"replicas x{world}" if world > 1 else "single GPU")),
-                       "l2": f"inputs rotated over {n_sets} device-resident sets, each larger than L2",
-                       "collective": (f"ncclAllGather of the output rows ({total_rows} rows whole on every "
-                                      "rank) inside every step, on its own stream (overlapping the next "
-                                      "step's GEMMs), all complete before the timed region ends"
-                                      if comm is not None else None)},
-            "e2e": {"value": round(e2e_value, 3), "unit": unit, "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4),
-                    "copy_bound": {"h2d_gbs": round(bw["h2d_gbs"], 2), "d2h_gbs": round(bw["d2h_gbs"], 2),
-                                   "ms": round((h2d / bw["h2d_gbs"] + d2h / bw["d2h_gbs"]) / 1e6, 4),
-                                   "frac": round((h2d / bw["h2d_gbs"] + d2h / bw["d2h_gbs"]) / 1e6 / e2e_ms, 4),
-                                   "how": "pinned 256 MiB H2D and D2H copies timed alone (best of 3)"},
-                    "two_threads": e2e_threads,
-                    "path": "pb_tensor_create from pinned host -> pb_materialize -> pb_tensor_read"},
-            "gpu_launches": launches,
-            "roofline": roofline,
-            "cpu_baseline": cpu,
-            "clocks": clock_summary,
-            "kernels": {k: {"launches": n, "ms": round(t, 4)} for k, (n, t) in prof.items()},
-            "host_us_per_materialize": {k: round(v, 2) for k, v in host.items()},
-        }
+        if extra:
+            line["extra"] = extra
         print(json.dumps(line), flush=True)
 
 
@@ -531,45 +572,79 @@ CONFIG_METRIC = {
 }
 
 
-def run_reference(args, rank, world, dist):
-    workload = args.workload
+def reference_record(workload: str, args, world: int) -> dict:
+    """The reference's own implementation of `workload` (its NVRTC-JIT GPU
+    path, one GPU) through oracle/_ref/ref_runner, with the same steps and
+    warm-up as this library's arm."""
     specs, work, bound = CONFIGS[workload]
-    if rank != 0:
-        return
     exe = ROOT / "oracle" / "_ref" / "ref_runner"
     unit = "GB/s" if bound == "hbm" else "TFLOP/s"
     scale = 1e9 if bound == "hbm" else 1e12
-    if not exe.exists():
-        print(json.dumps({"impl": "reference", "unavailable":
-                          "oracle/_ref/ref_runner was not built (reference sources absent)"}))
-        return
-    steps = args.steps if bound == "hbm" else max(1, min(args.steps, 2))
-    warm = max(1, min(args.warmup, 3))
-    cmd = [str(exe), "bench", workload, str(steps), str(warm), "e2e"]
+    cmd = [str(exe), "bench", workload, str(args.steps), str(args.warmup), "e2e"]
     res = subprocess.run(cmd, capture_output=True, text=True, timeout=1800)
     if res.returncode != 0:
-        print(json.dumps({"impl": "reference", "unavailable": f"ref_runner failed: {res.stderr[-300:]}"}))
-        return
+        raise RuntimeError(f"ref_runner failed: {res.stderr[-300:]}")
     r = json.loads(res.stdout.strip().splitlines()[-1])
     value = work / (r["warm_ms"] * 1e-3) / scale
     e2e_value = work / (r["e2e_ms"] * 1e-3) / scale
-    line = {
+    # Kernel-only time of the reference's launches (ncu launch list,
+    # committed under profiles/): its warm step also holds a module load per
+    # launch and host-side zero fills.
+    kernels = None
+    kfile = ROOT / "profiles" / "ref_kernels.json"
+    if kfile.exists():
+        k = json.loads(kfile.read_text()).get(workload)
+        if k:
+            kernels = dict(k)
+            kernels["value"] = round(work / (k["kernel_ms_per_step"] * 1e-3) / scale, 4)
+            kernels["unit"] = unit
+    config = _config_keys(workload, 1)
+    return {
         "impl": "reference", "metric": CONFIG_METRIC[workload], "value": round(value, 4),
-        "unit": unit, "n_gpus": world, "steps": steps, "warmup": warm,
+        "unit": unit, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(r["warm_ms"], 4), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "scaling": "strong" if workload in ROW_SHARDED else "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (same seeds and generator as the porch_b200 arm)",
-        "config": {"workload": workload, "reference": "AkhilSamavedam/porch compiled from source",
-                   "path": "materialize(expr) + synchronize() through the reference's C++ API "
-                           "(NVRTC JIT, one GPU)",
-                   "staged": r.get("staged") if workload == "c5_mlp" else None},
+        "config": config,
+        "setup": {"reference": "AkhilSamavedam/porch compiled from source",
+                  "path": "materialize(expr) + synchronize() through the reference's C++ API "
+                          "(NVRTC JIT, one GPU: the reference has no multi-GPU path)",
+                  "staged": r.get("staged") if workload == "c5_mlp" else None},
         "e2e": {"value": round(e2e_value, 4), "unit": unit, "h2d_bytes_per_step": r["h2d_bytes"],
                 "d2h_bytes_per_step": r["d2h_bytes"], "ms_per_step": round(r["e2e_ms"], 4)},
         "cpu_baseline": {"value": round(value, 4), "unit": unit, "cores": 1, "kind": "reference",
                          "sample": "the reference has no CPU implementation of the path; "
                                    "this is its own NVRTC-JIT GPU path, timed on the same box"},
+        "kernel_only": kernels,
         "cold_ms": r["cold_ms"],
     }
+
+
+def run_reference(args, rank, world, dist):
+    if rank != 0:
+        return
+    exe = ROOT / "oracle" / "_ref" / "ref_runner"
+    if not exe.exists():
+        print(json.dumps({"impl": "reference", "unavailable":
+                          "oracle/_ref/ref_runner was not built (reference sources absent)"}))
+        return
+    try:
+        line = reference_record(args.workload, args, world)
+    except RuntimeError as exc:
+        print(json.dumps({"impl": "reference", "unavailable": str(exc)}))
+        return
+    if not args.no_extra and world == 1:
+        extra = {}
+        for name in sorted(EXTRA_SINGLE + EXTRA_SHARDED):
+            if name == args.workload:
+                continue
+            try:
+                r = reference_record(name, args, world)
+                extra[name] = {k: r[k] for k in ("metric", "value", "unit", "ms_per_step", "config", "e2e",
+                                                  "kernel_only", "cold_ms")}
+            except RuntimeError as exc:
+                extra[name] = {"unavailable": str(exc)}
+        line["extra"] = extra
     print(json.dumps(line), flush=True)
 
 
@@ -608,8 +683,10 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="porch_b200", choices=["porch_b200", "reference"])
-    ap.add_argument("--workload", default="c2_view", choices=sorted(CONFIGS))
+    ap.add_argument("--workload", default="c5_mlp", choices=sorted(CONFIGS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="time the headline workload only (not the other configurations)")
     args = ap.parse_args()
     rank, world, local, dist = dist_setup(args.gpus)
     try:

@@ -547,6 +547,14 @@ def device_synchronize(device: int = 0) -> None:
     _check(lib().pb_device_synchronize(int(device)))
 
 
+def empty_cache(device: int = 0) -> int:
+    """Returns every cached device block of `device` to the driver; the
+    bytes released."""
+    released = c_size_t()
+    _check(lib().pb_empty_cache(int(device), byref(released)))
+    return int(released.value)
+
+
 class PinnedBuffer:
     """Page-locked host memory viewed as a float32 numpy array."""
 

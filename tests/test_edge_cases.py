@@ -11,8 +11,10 @@ as IEEE says (the 3xTF32 path hands such operands to the same chain).
 import numpy as np
 import pytest
 
+import error_bounds
 import graphs
-from tolerances import assert_bitwise, assert_relative, assert_sum_close
+from tolerances import (MATMUL_TOL, REL_TOL, assert_bitwise, assert_relative, assert_sum_close,
+                        matmul_error)
 
 ZERO_SIZE = [
     ("0 input 0\n1 exp 0\n", [[0, 5]]),
@@ -122,15 +124,19 @@ def test_nonfinite_matmul_operands_match_the_reference(gpu):
     assert np.array_equal(np.isnan(got), np.isnan(want))
     assert np.array_equal(np.isposinf(got), np.isposinf(want))
     assert np.array_equal(np.isneginf(got), np.isneginf(want))
-    fin = np.isfinite(want)
-    assert np.max(np.abs(got[fin] - want[fin])) <= 1e-4
+    # Finite entries: 1e-5 relative or, where they cancel, within the fp32
+    # forward error bound (both sides are fp32 evaluations).
+    _, bound = error_bounds.evaluate(prog, [a, b])
+    error_bounds.check(got, want, bound, REL_TOL, "non-finite operands")
     # And with finite operands the same plan takes the tensor-core path: the
     # CUDA-core kernel returns at once (results equal to the reference's
     # within the 3xTF32 tolerance).
     a2, b2 = np.nan_to_num(a, posinf=1.0, neginf=-1.0), np.nan_to_num(b, posinf=1.0, neginf=-1.0)
     got2 = graphs.evaluate_product(gpu, prog, [a2, b2])
     want2 = ref._run_reference(prog, [a2, b2])
-    assert np.max(np.abs(got2 - want2)) <= 1e-4
+    _, bound2 = error_bounds.evaluate(prog, [a2, b2])
+    error_bounds.check(got2, want2, bound2, REL_TOL, "finite operands")
+    assert matmul_error(got2, a2.astype(np.float64) @ b2.astype(np.float64), k) <= MATMUL_TOL
 
 
 BIG = (1 << 31) + 8

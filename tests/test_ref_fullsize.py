@@ -12,7 +12,8 @@ get the same seeded inputs (the bench's generator and distributions):
   (src/tensor.cpp:684-721) against fp64 on sampled rows: both within the
   1e-5 sqrt(K) bound, ours within 4x the reference's own error, and the two
   within that bound of each other;
-- config 5 (staged, as the reference must run it): within tolerance.
+- config 5 as one lazy graph (what the benchmark realises) against fp64 on
+  sampled rows and against the reference's staged run on every row.
 """
 
 from __future__ import annotations
@@ -25,6 +26,7 @@ from pathlib import Path
 import numpy as np
 import pytest
 
+import error_bounds
 import graphs
 from tolerances import MATMUL_TOL, REL_TOL, assert_bitwise, assert_relative, matmul_error
 
@@ -90,7 +92,8 @@ def test_c3b_equals_reference(gpu):
 
 @pytest.mark.gpu
 def test_c3a_softmax_matches_reference(gpu):
-    ins = _inputs(gpu, [([16384, 4096], "normal", 0, 2)])
+    """All 65536 rows of config 3a against the reference's output."""
+    ins = _inputs(gpu, [([65536, 4096], "normal", 0, 2)])
     assert_relative(graphs.evaluate_product(gpu, C3A, ins), _run_reference(C3A, ins), REL_TOL,
                     "config 3a vs reference")
 
@@ -121,20 +124,78 @@ def test_c4_matmul_against_reference_and_fp64(gpu):
     assert matmul_error(ours_full[rows], ref_full[rows].astype(np.float64), n) <= MATMUL_TOL
 
 
+def _softmax64(z: np.ndarray) -> np.ndarray:
+    z = z.astype(np.float64)
+    e = np.exp(z - z.max(axis=1, keepdims=True))
+    return e / e.sum(axis=1, keepdims=True)
+
+
 @pytest.mark.gpu
-def test_c5_staged_matches_reference(gpu):
-    m, d, h = 4096, 4096, 16384
-    ins = _inputs(gpu, [([m, d], "normal", 0, 1), ([d, h], "normal", 0, 1 / 64), ([h], "uniform", -0.1, 0.1),
+def test_c5_one_graph_full_size_against_fp64_and_reference(gpu):
+    """Config 5 exactly as the benchmark realises it: one lazy graph
+    P = softmax(logistic(X@W1 + b1)@W2 + b2, 1) (api.config_graph) at the
+    full [16384,4096] x [4096,16384] x [16384,4096] shape, with the bench's
+    seeded inputs. Bars:
+    - each GEMM within the sqrt(K)-normalised 1e-5 of fp64 (GEMM1 realised
+      as X@W1 + b1, GEMM2 as H@W2 + b2 on our own H, each against fp64 of its
+      own fp32 operands) on 256 sampled rows;
+    - softmax within 1e-5 relative: the one-graph P against the fp64
+      softmax of our realised Z on the sampled rows;
+    - end to end, P against the fp64 MLP within 1e-5 plus the GEMM bar
+      carried through the softmax (|d log P| <= 2 max|dZ|), and no further
+      from fp64 than the reference's own staged output (its FMA chains,
+      src/tensor.cpp:684-721; staged because as one graph the reference
+      re-evaluates the inner matmul inside the outer one's K loop);
+    - all 16384 rows against the reference's staged output within the sum
+      of both sides' end-to-end bars."""
+    api = gpu
+    m, d, h = 16384, 4096, 16384
+    ins = _inputs(api, [([m, d], "normal", 0, 1), ([d, h], "normal", 0, 1 / 64), ([h], "uniform", -0.1, 0.1),
                         ([h, d], "normal", 0, 1 / 128), ([d], "uniform", -0.1, 0.1)])
-    prog = (f"0 input 0\n1 input 1\n2 input 2\n3 input 3\n4 input 4\n5 matmul 0 1\n6 broadcast 2 {m},{h}\n"
-            f"7 add 5 6\n8 logistic 7\n9 materialize 8\n10 matmul 9 3\n11 broadcast 4 {m},{d}\n"
-            "12 add 10 11\n13 materialize 12\n14 softmax 13 1\n")
-    ours = graphs.evaluate_product(gpu, prog, ins)
-    ref = _run_reference(prog, ins)
-    # P's rows sum to 1 with entries ~1/4096: compare each element against
-    # the row scale (the matmuls' sqrt(K)-normalised error carries through).
-    err = np.abs(ours.astype(np.float64) - ref.astype(np.float64)) / np.abs(ref).max(axis=1, keepdims=True)
-    assert float(err.max()) <= 1e-4, float(err.max())
+    x, w1, b1, w2, b2 = ins
+    t = {k: api.tensor(list(a.shape), a) for k, a in zip(["x", "w1", "b1", "w2", "b2"], ins)}
+    p_graph = api.materialize(api.config_graph("c5_mlp", t)).cpu().reshape(m, d)
+    g1 = api.materialize(api.matmul(t["x"], t["w1"]) + api.broadcast_to(t["b1"], [m, h]))
+    hid = api.materialize(api.logistic(g1))
+    z = api.materialize(api.matmul(hid, t["w2"]) + api.broadcast_to(t["b2"], [m, d]))
+    rows = np.linspace(0, m - 1, 256).astype(int)
+    g1r = g1.cpu().reshape(m, h)[rows]
+    hr = hid.cpu().reshape(m, h)[rows]
+    zr = z.cpu().reshape(m, d)[rows]
+    del g1, hid
+    w1_64, w2_64 = w1.astype(np.float64), w2.astype(np.float64)
+    g1_64 = x[rows].astype(np.float64) @ w1_64 + b1.astype(np.float64)
+    e_g1 = matmul_error(g1r, g1_64, d)
+    z_own64 = hr.astype(np.float64) @ w2_64 + b2.astype(np.float64)
+    e_z = matmul_error(zr, z_own64, h)
+    print(f"config 5 GEMM errors (sqrt(K)-normalised): GEMM1 {e_g1:.3e}, GEMM2 {e_z:.3e}")
+    assert e_g1 <= MATMUL_TOL and e_z <= MATMUL_TOL, (e_g1, e_z)
+    # Softmax bar on the graph's own P.
+    assert_relative(p_graph[rows], _softmax64(zr), REL_TOL, "config 5 softmax vs fp64 of our Z")
+    # End to end against the fp64 MLP.
+    h64 = 1.0 / (1.0 + np.exp(-g1_64))
+    z64 = h64 @ w2_64 + b2.astype(np.float64)
+    p64 = _softmax64(z64)
+    zscale = np.maximum(np.abs(z64), np.sqrt(np.mean(z64 * z64)))
+    gemm_abs = MATMUL_TOL * np.sqrt(h) * zscale.max(axis=1, keepdims=True)
+    bar = REL_TOL + 2 * gemm_abs
+    rel_ours = np.abs(p_graph[rows] - p64) / p64
+    ref = _run_reference(
+        f"0 input 0\n1 input 1\n2 input 2\n3 input 3\n4 input 4\n5 matmul 0 1\n6 broadcast 2 {m},{h}\n"
+        f"7 add 5 6\n8 logistic 7\n9 materialize 8\n10 matmul 9 3\n11 broadcast 4 {m},{d}\n"
+        "12 add 10 11\n13 materialize 12\n14 softmax 13 1\n", ins).reshape(m, d)
+    rel_ref = np.abs(ref[rows] - p64) / p64
+    print(f"config 5 P vs fp64 (max relative): porch_b200 {rel_ours.max():.3e}, reference {rel_ref.max():.3e}, "
+          f"bar {bar.max():.3e}")
+    assert np.all(rel_ours <= bar), float((rel_ours / bar).max())
+    assert rel_ours.max() <= rel_ref.max(), (rel_ours.max(), rel_ref.max())
+    # Every row against the reference: both sides within their bars of the
+    # exact result; the row scale of Z from our own realised Z.
+    zall = z.cpu().reshape(m, d).astype(np.float64)
+    zs_all = np.maximum(np.abs(zall).max(axis=1, keepdims=True), np.sqrt(np.mean(zall * zall)))
+    bar_all = 2 * (REL_TOL + 2 * MATMUL_TOL * np.sqrt(h) * zs_all) + 2 * (rel_ref.max() + REL_TOL)
+    rel_all = np.abs(p_graph.astype(np.float64) - ref) / ref
+    assert np.all(rel_all <= bar_all), float((rel_all / bar_all).max())
 
 
 LARGE_SEEDS = list(range(7000, 7040))
@@ -168,9 +229,8 @@ def test_large_random_programs_match_reference(gpu, seed):
         # The same __expf on both sides, in the same operation order.
         assert_bitwise(got, ref, f"seed {seed}")
     else:
-        g64, r64 = got.astype(np.float64), ref.astype(np.float64)
-        fin = np.isfinite(r64)
-        assert np.array_equal(np.isfinite(g64), fin), f"seed {seed}"
-        scale = np.maximum(np.abs(r64), np.sqrt(np.mean(r64[fin] ** 2)) if fin.any() else 1.0)
-        err = np.abs(g64 - r64)[fin] / np.where(scale[fin] == 0, 1.0, scale[fin])
-        assert err.size == 0 or float(err.max()) <= 1e-4, (f"seed {seed}", float(err.max()))
+        # Both are fp32 evaluations: within 1e-5 relative, or where the
+        # result cancels, within the forward error bound of fp32 evaluation
+        # (tests/error_bounds.py).
+        _, bound = error_bounds.evaluate(text, ins)
+        error_bounds.check(got, ref, bound, REL_TOL, f"seed {seed}")
