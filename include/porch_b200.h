@@ -127,6 +127,13 @@ int pb_expr_broadcast(const pb_expr* value, const int64_t* shape, size_t rank,
 int pb_expr_unsqueeze(const pb_expr* value, size_t axis, pb_expr** out);
 int pb_expr_concat(const pb_expr* lhs, const pb_expr* rhs, size_t axis,
                    pb_expr** out);
+/* N-D permutation of the axes: output axis d is input axis perm[d]. No
+ * counterpart in the reference, whose transpose is rank 2 only
+ * (src/tensor.cpp:430-437); PB_TRANSPOSE keeps that rule. Realised alone
+ * (or with slices and unsqueezes) it is a strided view: no copy until the
+ * values are read out. */
+int pb_expr_permute(const pb_expr* value, const int64_t* perm, size_t rank,
+                    pb_expr** out);
 /* sum / max with keepdim (PB_SUM, PB_MAX) */
 int pb_expr_reduce(int op, const pb_expr* value, size_t axis, int keepdim,
                    pb_expr** out);

@@ -439,6 +439,16 @@ def unsqueeze(a, axis: int) -> Expr:
     return Expr(out.value)
 
 
+def permute(a, perm: Sequence[int]) -> Expr:
+    """N-D axis permutation (output axis d = input axis perm[d]); an
+    extension, the reference's transpose is rank 2 only."""
+    ea = _expr(a)
+    arr, n = _shape_arg(perm)
+    out = c_void_p()
+    _check(lib().pb_expr_permute(ea._h, arr, n, byref(out)))
+    return Expr(out.value)
+
+
 def concat(a, b, axis: int) -> Expr:
     ea, eb = _expr(a), _expr(b)
     out = c_void_p()

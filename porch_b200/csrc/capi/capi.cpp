@@ -218,6 +218,7 @@ int pb_tensor_read(const pb_tensor* t, float* values, size_t count) {
         }
         if (storage->placeholder)
             throw std::runtime_error("placeholder tensors hold no values");
+        porch::detail::make_contiguous(storage);
         porch::cuda_jit::copy_to_host(storage->device_values, std::span<float>(values, count));
     });
 }
@@ -342,6 +343,21 @@ int pb_expr_unsqueeze(const pb_expr* value, size_t axis, pb_expr** out) {
         require(value, "value");
         require(out, "out");
         *out = wrap(porch::unsqueeze(value->value, axis));
+    });
+}
+
+int pb_expr_permute(const pb_expr* value, const int64_t* perm, size_t rank, pb_expr** out) {
+    return guarded([&] {
+        require(value, "value");
+        require(out, "out");
+        if (rank != 0) require(perm, "perm");
+        auto n = std::make_shared<porch::tensor_expr::node>();
+        n->kind = porch::detail::expr_kind::permute;
+        n->lhs = porch::expr_access::root(value->value);
+        n->shape.assign(perm, perm + rank);
+        porch::tensor_expr e = porch::expr_access::make(std::move(n));
+        (void)porch::detail::infer(*porch::expr_access::root(e)); // validates now, as the builders do
+        *out = wrap(std::move(e));
     });
 }
 

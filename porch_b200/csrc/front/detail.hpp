@@ -110,15 +110,56 @@ namespace porch::detail {
     // mirror (the reference zero-fills a host vector of numel floats twice per
     // materialisation, src/tensor.cpp:1019 and :1073-1076; here the mirror is
     // allocated only when data()/cpu() is called).
+    //
+    // A storage may instead be a strided view of another storage's device
+    // values: materialising a graph that only slices, transposes,
+    // unsqueezes or (contiguously) reshapes one realised tensor launches
+    // nothing and records element (i0, i1, ...) at
+    // view_offset + sum_d i_d * view_strides[d] of `view_base`. Later graphs
+    // read the view in place (canonicalised as a slice over the base); the
+    // public accessors still see a contiguous tensor, copied out on the
+    // first request for its values (make_contiguous). A view is a snapshot:
+    // before a raw handle to a base's values is handed out (device_data()),
+    // its live views are copied out, and no view is made of a storage whose
+    // handle has been handed out.
     struct realized_storage {
-        cuda_jit::device_buffer device_values;
+        cuda_jit::device_buffer device_values; // a view: the base's buffer
         size_t count = 0;
         int device = 0;
         std::mutex host_mutex;
         std::vector<float32_t> host;
         bool host_current = false;
         bool placeholder = false; // shape-only tensor for plan inspection
+
+        std::mutex view_mutex;
+        std::shared_ptr<realized_storage> view_base; // null: contiguous values
+        std::vector<index_t> view_shape;
+        std::vector<index_t> view_strides;
+        index_t view_offset = 0;
+        // Bumped when a view turns into contiguous values (bound graphs that
+        // read it through its base are then rebuilt).
+        std::atomic<uint32_t> layout_epoch{0};
+        bool escaped = false; // a handle to device_values was handed out
+        std::vector<std::weak_ptr<realized_storage>> views;
     };
+
+    // A strided layout over a storage's linear values.
+    struct strided_layout {
+        std::vector<index_t> shape;
+        std::vector<index_t> strides;
+        index_t offset = 0;
+    };
+
+    // The view fields of `s` under its view_mutex: false when `s` holds
+    // contiguous values.
+    bool view_of(realized_storage& s, std::shared_ptr<realized_storage>& base, strided_layout& layout);
+    // Turns a view into contiguous values of its own (one copy kernel);
+    // no-op for contiguous storage.
+    void make_contiguous(const std::shared_ptr<realized_storage>& s);
+    // Before a handle to `s`'s device values leaves the library: copies out
+    // its live views (so they stay snapshots), makes `s` itself contiguous
+    // and marks it so that no new view is made of it.
+    void escape(const std::shared_ptr<realized_storage>& s);
 
     enum class expr_kind : uint8_t {
         input,
@@ -140,6 +181,10 @@ namespace porch::detail {
         minimum,
         exp,
         reciprocal,
+        // Internal N-D permutation (no reference counterpart: its transpose
+        // is rank 2 only, src/tensor.cpp:430-437); `shape` holds the
+        // permutation, output dim d = input dim perm[d].
+        permute,
     };
 
     const char* kind_name(expr_kind kind);
@@ -149,8 +194,9 @@ namespace porch::detail {
 namespace porch {
 
     // IR node. Same 19 kinds and parameters as the reference
-    // (src/tensor.cpp:26-60), except that an input holds shared ownership of
-    // the realised storage instead of a raw `const tensor*`.
+    // (src/tensor.cpp:26-60) plus the internal permute, except that an input
+    // holds shared ownership of the realised storage instead of a raw
+    // `const tensor*`.
     struct tensor_expr::node {
         detail::expr_kind kind = detail::expr_kind::scalar;
         std::shared_ptr<detail::realized_storage> storage; // input

@@ -9,8 +9,12 @@
 // ~2^-22 relative, is dropped).
 //
 // Launches:
-//  1. pb_split_rows:      A [M,K]  -> Ahi, Alo [M,K]      (K-major as is)
-//  2. pb_split_transpose: B [K,N]  -> Bhi, Blo [N,K]      (to K-major)
+//  1-2. pb_split_rows / pb_split_transpose: each operand, read in place with
+//     its strides (inputs, slices and strided views of them, transposes),
+//     -> hi, lo in K-major rows of K padded to 32: A [M,K] -> [M,Kp] and
+//     B [K,N] -> [N,Kp]. An operand contiguous along K takes the row pass,
+//     one contiguous along M or N (B as stored, a transposed A) the tile
+//     transpose.
 //  3. pb_gemm_tc:         one 128x256 output tile per CTA, 320 threads.
 //     warp 0 lane 0 issues TMA loads (64B swizzle, BK = 16 fp32 = one 64-byte
 //     swizzle row) into a 4-stage ring of {Ahi, Alo, Bhi, Blo} tiles (48 KB
@@ -178,8 +182,8 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
 
     } // namespace
 
-    int lowerer::emit_gemm_tc(int id, const box& b, kernel& k, const kernel_arg& A,
-                              const kernel_arg& B, int64_t M, int64_t N, int64_t K, int* nonfinite) {
+    int lowerer::emit_gemm_tc(int id, const box& b, kernel& k, const gemm_operand& A,
+                              const gemm_operand& B, int64_t M, int64_t N, int64_t K, int* nonfinite) {
         (void)id;
         if (tensor_cores_disabled()) return -1;
         // Any M, N, K. The K-major hi/lo arrays have padded rows (16-byte
@@ -224,78 +228,83 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
             p_.launches.push_back(std::move(l));
         }
 
-        // ---- 1. split A rows (contiguous, float4) --------------------------
-        {
-            const int64_t n4 = M * Kp / 4;
+        // ---- 1-2. split A and B into K-major hi/lo ---------------------------
+        // Each operand is read in place as a K-major source: rows r (A: its
+        // M rows; B: its N columns), element (r, k) at off + r * sr + k * sk.
+        // Contiguous along k: a row pass (float4 when rows start 16-byte
+        // aligned); contiguous along r (a transposed operand, or B as
+        // stored): 64 x 64 tiles through shared memory so both the loads
+        // and the K-major stores stay coalesced; otherwise the same tiles
+        // with strided loads.
+        auto emit_split = [&](const std::string& what, const gemm_operand& X, int64_t R, int64_t sr, int64_t sk,
+                              int hi_t, int lo_t) {
             std::ostringstream src;
             src << kernel_prelude() << gemm_device_source();
-            src << "extern \"C\" __global__ void __launch_bounds__(256) pb_split_rows(const float* __restrict__ x, "
-                   "float* __restrict__ hi, float* __restrict__ lo, int* __restrict__ nf) {\n"
-                << "    for (pb_u64 i = (pb_u64)blockIdx.x * 256u + threadIdx.x; i < " << n4
-                << "ull; i += (pb_u64)gridDim.x * 256u) {\n";
-            if (Kp == K) {
-                src << "        const float4 v = pb_ld4(x + 4 * i);\n";
-            } else if (K % 4 == 0) {
-                src << "        const pb_u64 r = i / " << Kp / 4 << "ull, c = i % " << Kp / 4 << "ull;\n"
-                    << "        const float4 v = c < " << K / 4 << "ull ? pb_ld4(x + r * " << K
-                    << "ull + 4 * c) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);\n";
+            launch_spec l;
+            if (sk == 1) {
+                const int64_t n4 = R * Kp / 4;
+                src << "extern \"C\" __global__ void __launch_bounds__(256) pb_split_rows(const float* __restrict__ x, "
+                       "float* __restrict__ hi, float* __restrict__ lo, int* __restrict__ nf) {\n"
+                    << "    for (pb_u64 i = (pb_u64)blockIdx.x * 256u + threadIdx.x; i < " << n4
+                    << "ull; i += (pb_u64)gridDim.x * 256u) {\n";
+                if (Kp == K && sr == K && X.off == 0) {
+                    src << "        const float4 v = pb_ld4(x + 4 * i);\n";
+                } else if (K % 4 == 0 && sr % 4 == 0 && X.off % 4 == 0) {
+                    src << "        const pb_u64 r = i / " << Kp / 4 << "ull, c = i % " << Kp / 4 << "ull;\n"
+                        << "        const float4 v = c < " << K / 4 << "ull ? pb_ld4(x + " << X.off << "ull + r * " << sr
+                        << "ull + 4 * c) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);\n";
+                } else {
+                    // Rows not 16-byte aligned: one float at a time.
+                    src << "        const pb_u64 r = i / " << Kp / 4 << "ull, c = 4 * (i % " << Kp / 4 << "ull);\n"
+                        << "        const float* xr = x + " << X.off << "ull + r * " << sr << "ull;\n"
+                        << "        float4 v;\n"
+                        << "        v.x = c < " << K << "ull ? pb_ld(xr + c) : 0.0f;\n"
+                        << "        v.y = c + 1 < " << K << "ull ? pb_ld(xr + c + 1) : 0.0f;\n"
+                        << "        v.z = c + 2 < " << K << "ull ? pb_ld(xr + c + 2) : 0.0f;\n"
+                        << "        v.w = c + 3 < " << K << "ull ? pb_ld(xr + c + 3) : 0.0f;\n";
+                }
+                src << "        if (!(isfinite(v.x) && isfinite(v.y) && isfinite(v.z) && isfinite(v.w))) atomicOr(nf, 1);\n"
+                    << "        float4 h, l;\n"
+                    << "        h.x = pb_tf32_hi(v.x); l.x = pb_tf32_rn(v.x - h.x);\n"
+                    << "        h.y = pb_tf32_hi(v.y); l.y = pb_tf32_rn(v.y - h.y);\n"
+                    << "        h.z = pb_tf32_hi(v.z); l.z = pb_tf32_rn(v.z - h.z);\n"
+                    << "        h.w = pb_tf32_hi(v.w); l.w = pb_tf32_rn(v.w - h.w);\n"
+                    << "        pb_st4(hi + 4 * i, h);\n        pb_st4(lo + 4 * i, l);\n    }\n}\n";
+                l.name = "pb_split_rows";
+                l.schedule = "3xTF32 split of " + what + " (hi = rn(x), lo = rn(x - hi))";
+                l.grid = {static_cast<uint32_t>(std::min<int64_t>((n4 + 255) / 256, 148 * 16)), 1, 1};
             } else {
-                // Rows of A not 16-byte aligned: one float at a time.
-                src << "        const pb_u64 r = i / " << Kp / 4 << "ull, c = 4 * (i % " << Kp / 4 << "ull);\n"
-                    << "        const float* xr = x + r * " << K << "ull;\n"
-                    << "        float4 v;\n"
-                    << "        v.x = c < " << K << "ull ? pb_ld(xr + c) : 0.0f;\n"
-                    << "        v.y = c + 1 < " << K << "ull ? pb_ld(xr + c + 1) : 0.0f;\n"
-                    << "        v.z = c + 2 < " << K << "ull ? pb_ld(xr + c + 2) : 0.0f;\n"
-                    << "        v.w = c + 3 < " << K << "ull ? pb_ld(xr + c + 3) : 0.0f;\n";
+                // Tile (k0.., r0..): loads walk r (coalesced when sr == 1),
+                // stores walk k of the K-major output.
+                src << "extern \"C\" __global__ void __launch_bounds__(256) pb_split_transpose(const float* __restrict__ x, "
+                       "float* __restrict__ hi, float* __restrict__ lo, int* __restrict__ nf) {\n"
+                    << "    __shared__ float t[64][65];\n"
+                    << "    const pb_u64 k0 = (pb_u64)blockIdx.y * 64u, n0 = (pb_u64)blockIdx.x * 64u;\n"
+                    << "    #pragma unroll\n    for (int u = 0; u < 16; ++u) {\n"
+                    << "        const pb_u32 r = threadIdx.x / 64u + 4u * u, c = threadIdx.x % 64u;\n"
+                    << "        t[r][c] = (k0 + r < " << K << "ull && n0 + c < " << R << "ull) ? pb_ld(x + " << X.off
+                    << "ull + (k0 + r) * " << sk << "ull + (n0 + c)" << (sr == 1 ? std::string{} : " * " + std::to_string(sr) + "ull")
+                    << ") : 0.0f;\n    }\n"
+                    << "    __syncthreads();\n"
+                    << "    #pragma unroll\n    for (int u = 0; u < 16; ++u) {\n"
+                    << "        const pb_u32 r = threadIdx.x / 64u + 4u * u, c = threadIdx.x % 64u;\n"
+                    << "        if (n0 + r >= " << R << "ull || k0 + c >= " << Kp << "ull) continue;\n"
+                    << "        const float v = t[c][r];\n"
+                    << "        if (!isfinite(v)) atomicOr(nf, 1);\n"
+                    << "        const float h = pb_tf32_hi(v);\n"
+                    << "        const pb_u64 o = (n0 + r) * " << Kp << "ull + k0 + c;\n"
+                    << "        hi[o] = h;\n        lo[o] = pb_tf32_rn(v - h);\n    }\n}\n";
+                l.name = "pb_split_transpose";
+                l.schedule = "3xTF32 split of " + what + " with transpose to K-major";
+                l.grid = {static_cast<uint32_t>((R + 63) / 64), static_cast<uint32_t>((Kp + 63) / 64), 1};
             }
-            src
-                << "        if (!(isfinite(v.x) && isfinite(v.y) && isfinite(v.z) && isfinite(v.w))) atomicOr(nf, 1);\n"
-                << "        float4 h, l;\n"
-                << "        h.x = pb_tf32_hi(v.x); l.x = pb_tf32_rn(v.x - h.x);\n"
-                << "        h.y = pb_tf32_hi(v.y); l.y = pb_tf32_rn(v.y - h.y);\n"
-                << "        h.z = pb_tf32_hi(v.z); l.z = pb_tf32_rn(v.z - h.z);\n"
-                << "        h.w = pb_tf32_hi(v.w); l.w = pb_tf32_rn(v.w - h.w);\n"
-                << "        pb_st4(hi + 4 * i, h);\n        pb_st4(lo + 4 * i, l);\n    }\n}\n";
-            launch_spec l;
-            l.name = "pb_split_rows";
             l.source = src.str();
-            l.schedule = "3xTF32 split of A (hi = rn(x), lo = rn(x - hi))";
-            l.grid = {static_cast<uint32_t>(std::min<int64_t>((n4 + 255) / 256, 148 * 16)), 1, 1};
-            l.args = {A, temp_arg(a_hi), temp_arg(a_lo), temp_arg(nf)};
+            l.args = {X.arg, temp_arg(hi_t), temp_arg(lo_t), temp_arg(nf)};
             finish_kernel(l);
             p_.launches.push_back(std::move(l));
-        }
-        // ---- 2. split + transpose B (64x64 tiles through shared memory) -----
-        {
-            std::ostringstream src;
-            src << kernel_prelude() << gemm_device_source();
-            src << "extern \"C\" __global__ void __launch_bounds__(256) pb_split_transpose(const float* __restrict__ x, "
-                   "float* __restrict__ hi, float* __restrict__ lo, int* __restrict__ nf) {\n"
-                << "    __shared__ float t[64][65];\n"
-                << "    const pb_u64 k0 = (pb_u64)blockIdx.y * 64u, n0 = (pb_u64)blockIdx.x * 64u;\n"
-                << "    #pragma unroll\n    for (int u = 0; u < 16; ++u) {\n"
-                << "        const pb_u32 r = threadIdx.x / 64u + 4u * u, c = threadIdx.x % 64u;\n"
-                << "        t[r][c] = (k0 + r < " << K << "ull && n0 + c < " << N << "ull) ? pb_ld(x + (k0 + r) * " << N
-                << "ull + n0 + c) : 0.0f;\n    }\n"
-                << "    __syncthreads();\n"
-                << "    #pragma unroll\n    for (int u = 0; u < 16; ++u) {\n"
-                << "        const pb_u32 r = threadIdx.x / 64u + 4u * u, c = threadIdx.x % 64u;\n"
-                << "        if (n0 + r >= " << N << "ull || k0 + c >= " << Kp << "ull) continue;\n"
-                << "        const float v = t[c][r];\n"
-                << "        if (!isfinite(v)) atomicOr(nf, 1);\n"
-                << "        const float h = pb_tf32_hi(v);\n"
-                << "        const pb_u64 o = (n0 + r) * " << Kp << "ull + k0 + c;\n"
-                << "        hi[o] = h;\n        lo[o] = pb_tf32_rn(v - h);\n    }\n}\n";
-            launch_spec l;
-            l.name = "pb_split_transpose";
-            l.source = src.str();
-            l.schedule = "3xTF32 split of B with transpose to K-major";
-            l.grid = {static_cast<uint32_t>((N + 63) / 64), static_cast<uint32_t>((Kp + 63) / 64), 1};
-            l.args = {B, temp_arg(b_hi), temp_arg(b_lo), temp_arg(nf)};
-            finish_kernel(l);
-            p_.launches.push_back(std::move(l));
-        }
+        };
+        emit_split("A", A, M, A.s0, A.s1, a_hi, a_lo);
+        emit_split("B", B, N, B.s1, B.s0, b_hi, b_lo);
         // ---- 3. tcgen05 GEMM + epilogue -------------------------------------
         std::vector<int> order;
         const std::string efn = emit_expr_function(b, "0", order);

@@ -30,81 +30,10 @@ namespace porch::detail {
             std::map<std::string, int> numbering;
             std::unordered_map<const realized_storage*, int> slot_of;
 
-            int visit(const tensor_expr::node& n) {
-                auto it = memo.find(&n);
-                if (it != memo.end()) return it->second;
-                gnode gn;
-                gn.kind = n.kind;
-                if (n.lhs) gn.a = visit(*n.lhs);
-                if (n.rhs) gn.b = visit(*n.rhs);
-                std::string key;
-                key.reserve(64);
-                auto put = [&](const void* p, size_t s) {
-                    key.append(static_cast<const char*>(p), s);
-                };
-                auto put_i = [&](int64_t v) { put(&v, sizeof v); };
-                auto put_v = [&](const std::vector<index_t>& v) {
-                    put_i(static_cast<int64_t>(v.size()));
-                    for (index_t x : v) put_i(x);
-                };
-                put_i(static_cast<int64_t>(n.kind));
-                put_i(gn.a);
-                put_i(gn.b);
-                switch (n.kind) {
-                    case expr_kind::input: {
-                        auto s = slot_of.find(n.storage.get());
-                        if (s == slot_of.end()) {
-                            const int slot = static_cast<int>(g.slots.size());
-                            slot_of.emplace(n.storage.get(), slot);
-                            g.slots.push_back(n.storage);
-                            g.slot_shapes.push_back(n.input_shape);
-                            gn.slot = slot;
-                        } else {
-                            gn.slot = s->second;
-                        }
-                        put_i(gn.slot);
-                        put_v(n.input_shape);
-                        gn.shape = n.input_shape;
-                        break;
-                    }
-                    case expr_kind::scalar: {
-                        gn.scalar = n.scalar;
-                        gn.is_scalar = true;
-                        uint32_t bits = 0;
-                        std::memcpy(&bits, &n.scalar, 4);
-                        put_i(bits);
-                        break;
-                    }
-                    case expr_kind::slice:
-                        gn.p_shape = n.slice_shape;
-                        gn.p_strides = n.slice_strides;
-                        gn.p_offset = n.slice_offset;
-                        put_v(gn.p_shape);
-                        put_v(gn.p_strides);
-                        put_i(gn.p_offset);
-                        break;
-                    case expr_kind::reshape:
-                    case expr_kind::broadcast:
-                        gn.p_shape = n.shape;
-                        put_v(gn.p_shape);
-                        break;
-                    case expr_kind::unsqueeze:
-                    case expr_kind::concat:
-                    case expr_kind::sum:
-                    case expr_kind::max:
-                        gn.axis = n.axis;
-                        gn.keepdim = n.keepdim;
-                        put_i(static_cast<int64_t>(n.axis));
-                        put_i(n.keepdim ? 1 : 0);
-                        break;
-                    default:
-                        break;
-                }
+            // Interns a node under its structural key (value numbering).
+            int intern(gnode gn, std::string key) {
                 auto num = numbering.find(key);
-                if (num != numbering.end()) {
-                    memo.emplace(&n, num->second);
-                    return num->second;
-                }
+                if (num != numbering.end()) return num->second;
                 shape_of(gn);
                 const int id = static_cast<int>(g.nodes.size());
                 g.nodes.push_back(std::move(gn));
@@ -114,6 +43,132 @@ namespace porch::detail {
                 g.hash = mix(g.hash, std::hash<std::string>{}(key));
                 g.key += key;
                 numbering.emplace(std::move(key), id);
+                return id;
+            }
+
+            static void put_i(std::string& key, int64_t v) { key.append(reinterpret_cast<const char*>(&v), sizeof v); }
+            static void put_v(std::string& key, const std::vector<index_t>& v) {
+                put_i(key, static_cast<int64_t>(v.size()));
+                for (index_t x : v) put_i(key, x);
+            }
+
+            int slot_for(const std::shared_ptr<realized_storage>& s, const std::vector<index_t>& shape) {
+                auto it = slot_of.find(s.get());
+                if (it != slot_of.end()) return it->second;
+                const int slot = static_cast<int>(g.slots.size());
+                slot_of.emplace(s.get(), slot);
+                g.slots.push_back(s);
+                g.slot_shapes.push_back(shape);
+                return slot;
+            }
+
+            // A strided view read in place: slice(input(base as [count]), layout).
+            int view_node(const std::shared_ptr<realized_storage>& base, const strided_layout& l) {
+                gnode in;
+                in.kind = expr_kind::input;
+                in.shape = {static_cast<index_t>(base->count)};
+                in.slot = slot_for(base, in.shape);
+                std::string ik;
+                put_i(ik, static_cast<int64_t>(expr_kind::input));
+                put_i(ik, -1);
+                put_i(ik, -1);
+                put_i(ik, in.slot);
+                put_v(ik, in.shape);
+                const int bi = intern(std::move(in), std::move(ik));
+                gnode sl;
+                sl.kind = expr_kind::slice;
+                sl.a = bi;
+                sl.p_shape = l.shape;
+                sl.p_strides = l.strides;
+                sl.p_offset = l.offset;
+                std::string sk;
+                put_i(sk, static_cast<int64_t>(expr_kind::slice));
+                put_i(sk, bi);
+                put_i(sk, -1);
+                put_v(sk, sl.p_shape);
+                put_v(sk, sl.p_strides);
+                put_i(sk, sl.p_offset);
+                return intern(std::move(sl), std::move(sk));
+            }
+
+            int visit(const tensor_expr::node& n) {
+                auto it = memo.find(&n);
+                if (it != memo.end()) return it->second;
+                // Inputs that are strided views (and slices of them) read the
+                // base storage in place.
+                if (n.kind == expr_kind::input || (n.kind == expr_kind::slice && n.lhs &&
+                                                   n.lhs->kind == expr_kind::input)) {
+                    const tensor_expr::node& in = n.kind == expr_kind::input ? n : *n.lhs;
+                    std::shared_ptr<realized_storage> base;
+                    strided_layout l;
+                    if (in.storage && view_of(*in.storage, base, l)) {
+                        g.view_inputs.emplace_back(in.storage, in.storage->layout_epoch.load());
+                        int id = -1;
+                        if (n.kind == expr_kind::input) {
+                            id = view_node(base, l);
+                        } else {
+                            strided_layout c;
+                            if (compose_slice(l, n.slice_offset, n.slice_strides, n.slice_shape, c))
+                                id = view_node(base, c);
+                        }
+                        if (id >= 0) {
+                            memo.emplace(&n, id);
+                            return id;
+                        }
+                    }
+                }
+                gnode gn;
+                gn.kind = n.kind;
+                if (n.lhs) gn.a = visit(*n.lhs);
+                if (n.rhs) gn.b = visit(*n.rhs);
+                std::string key;
+                key.reserve(64);
+                put_i(key, static_cast<int64_t>(n.kind));
+                put_i(key, gn.a);
+                put_i(key, gn.b);
+                switch (n.kind) {
+                    case expr_kind::input: {
+                        gn.slot = slot_for(n.storage, n.input_shape);
+                        put_i(key, gn.slot);
+                        put_v(key, n.input_shape);
+                        gn.shape = n.input_shape;
+                        break;
+                    }
+                    case expr_kind::scalar: {
+                        gn.scalar = n.scalar;
+                        gn.is_scalar = true;
+                        uint32_t bits = 0;
+                        std::memcpy(&bits, &n.scalar, 4);
+                        put_i(key, bits);
+                        break;
+                    }
+                    case expr_kind::slice:
+                        gn.p_shape = n.slice_shape;
+                        gn.p_strides = n.slice_strides;
+                        gn.p_offset = n.slice_offset;
+                        put_v(key, gn.p_shape);
+                        put_v(key, gn.p_strides);
+                        put_i(key, gn.p_offset);
+                        break;
+                    case expr_kind::reshape:
+                    case expr_kind::broadcast:
+                    case expr_kind::permute:
+                        gn.p_shape = n.shape;
+                        put_v(key, gn.p_shape);
+                        break;
+                    case expr_kind::unsqueeze:
+                    case expr_kind::concat:
+                    case expr_kind::sum:
+                    case expr_kind::max:
+                        gn.axis = n.axis;
+                        gn.keepdim = n.keepdim;
+                        put_i(key, static_cast<int64_t>(n.axis));
+                        put_i(key, n.keepdim ? 1 : 0);
+                        break;
+                    default:
+                        break;
+                }
+                const int id = intern(std::move(gn), std::move(key));
                 memo.emplace(&n, id);
                 return id;
             }
@@ -161,6 +216,11 @@ namespace porch::detail {
                         return;
                     case expr_kind::transpose:
                         n.shape = {a->shape[1], a->shape[0]};
+                        return;
+                    case expr_kind::permute:
+                        n.shape.resize(a->shape.size());
+                        for (size_t d = 0; d < n.p_shape.size(); ++d)
+                            n.shape[d] = a->shape[static_cast<size_t>(n.p_shape[d])];
                         return;
                     case expr_kind::concat:
                         n.shape = a->shape;
@@ -230,7 +290,22 @@ namespace porch::detail {
             std::shared_ptr<plan> p;
             shape_info info;
             int device = 0;
+            // A pure view builds its (copy) plan only if a view cannot be
+            // made when it is materialised.
+            mutable std::once_flag plan_once;
+            mutable std::shared_ptr<plan> view_copy_plan;
+            plan* get_plan() const {
+                if (p) return p.get();
+                std::call_once(plan_once, [&] { view_copy_plan = lookup_plan(g); });
+                return view_copy_plan.get();
+            }
         };
+
+        bool stale(const bound_graph& b) {
+            for (const auto& [s, epoch] : b.g.view_inputs)
+                if (s->layout_epoch.load(std::memory_order_acquire) != epoch) return true;
+            return false;
+        }
 
         struct host_profiler {
             std::atomic<bool> on{false};
@@ -253,7 +328,7 @@ namespace porch::detail {
 
         std::shared_ptr<const bound_graph> bind(const tensor_expr::node& root) {
             auto cached = std::static_pointer_cast<const bound_graph>(std::atomic_load(&root.bound));
-            if (cached) return cached;
+            if (cached && !stale(*cached)) return cached;
             auto b = std::make_shared<bound_graph>();
             b->info = infer(root);
             if (!b->info.has_input)
@@ -268,7 +343,8 @@ namespace porch::detail {
                 if (device < 0) device = s->device;
             }
             b->device = device < 0 ? 0 : device;
-            if (checked_numel(b->info.shape) != 0) b->p = lookup_plan(b->g);
+            b->g.pure_view = pure_view(b->g, b->g.view_slot, b->g.view_layout);
+            if (checked_numel(b->info.shape) != 0 && !b->g.pure_view) b->p = lookup_plan(b->g);
             std::shared_ptr<const void> erased = b;
             std::atomic_store(&root.bound, erased);
             return b;
@@ -323,7 +399,15 @@ namespace porch::detail {
         return "CUDA elementwise input is empty";
     }
 
-    tensor materialize_graph(const tensor_expr::node& root) {
+    namespace {
+        tensor materialize_impl(const tensor_expr::node& root, bool allow_view);
+    }
+
+    tensor materialize_graph(const tensor_expr::node& root) { return materialize_impl(root, true); }
+    tensor materialize_graph_copy(const tensor_expr::node& root) { return materialize_impl(root, false); }
+
+    namespace {
+    tensor materialize_impl(const tensor_expr::node& root, bool allow_view) {
         host_profiler& hp = hprof();
         const bool timing = hp.on.load(std::memory_order_relaxed);
         uint64_t t0 = timing ? now_ns() : 0, t1 = 0, t2 = 0, t3 = 0, ta = 0, tb = 0;
@@ -345,7 +429,15 @@ namespace porch::detail {
             return tensor_access::from_storage(b->info.shape, std::move(storage),
                                                b->info.placement);
         }
-        plan* p = b->p.get();
+        if (allow_view && g.pure_view &&
+            make_view(g.slots[static_cast<size_t>(g.view_slot)], g.view_layout, storage)) {
+            // Data movement of one realised tensor: a strided view, no kernel.
+            storage->count = count;
+            storage->device = device;
+            host_count("materialize_view");
+            return tensor_access::from_storage(b->info.shape, std::move(storage), b->info.placement);
+        }
+        plan* p = b->get_plan();
         if (timing) ta = now_ns();
 
         for (size_t si = 0; si < g.slots.size(); ++si) {
@@ -474,6 +566,7 @@ namespace porch::detail {
         }
         return result;
     }
+    } // namespace
 
     std::string describe_plan(const tensor_expr::node& root, bool with_source) {
         shape_info info = infer(root);

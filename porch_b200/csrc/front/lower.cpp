@@ -246,6 +246,45 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
         return a;
     }
 
+    gemm_operand lowerer::as_gemm_operand(int id) {
+        const gnode& n = g_.nodes[static_cast<size_t>(id)];
+        gemm_operand o;
+        // Peel one transpose (it swaps the strides), then a slice of an
+        // input or the input itself.
+        bool transposed = false;
+        int v = id;
+        if (n.kind == expr_kind::transpose) {
+            transposed = true;
+            v = n.a;
+        }
+        const gnode& m = g_.nodes[static_cast<size_t>(v)];
+        bool in_place = false;
+        if (m.kind == expr_kind::input && m.shape.size() == 2) {
+            o.arg.kind = arg_kind::slot;
+            o.arg.index = m.slot;
+            o.s0 = m.shape[1];
+            o.s1 = 1;
+            in_place = true;
+        } else if (m.kind == expr_kind::slice && m.shape.size() == 2 &&
+                   g_.nodes[static_cast<size_t>(m.a)].kind == expr_kind::input && m.p_strides[0] >= 0 &&
+                   m.p_strides[1] >= 0) {
+            o.arg.kind = arg_kind::slot;
+            o.arg.index = g_.nodes[static_cast<size_t>(m.a)].slot;
+            o.off = m.p_offset;
+            o.s0 = m.p_strides[0];
+            o.s1 = m.p_strides[1];
+            in_place = true;
+        }
+        if (!in_place) {
+            o.arg = as_buffer(id);
+            o.s0 = n.shape[1];
+            o.s1 = 1;
+            return o;
+        }
+        if (transposed) std::swap(o.s0, o.s1);
+        return o;
+    }
+
     // ================================================= affine analysis ==
     std::string lowerer::pos_key(const position& p) {
         std::string k = p.linear ? "L" : "C";
@@ -415,6 +454,15 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
                 const std::vector<affine> c = to_coords(pos, n.shape, b);
                 position child;
                 child.coords = {c[1], c[0]};
+                out = build(k, b, n.a, child, acc_id, memo);
+                break;
+            }
+            case expr_kind::permute: {
+                // Output dim d is input dim perm[d].
+                const std::vector<affine> c = to_coords(pos, n.shape, b);
+                position child;
+                child.coords.resize(c.size());
+                for (size_t d = 0; d < c.size(); ++d) child.coords[static_cast<size_t>(n.p_shape[d])] = c[d];
                 out = build(k, b, n.a, child, acc_id, memo);
                 break;
             }
@@ -1091,6 +1139,16 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
             case expr_kind::reshape:
             case expr_kind::unsqueeze:
                 return gen_value(k, n.a, idx, stmts, counter);
+            case expr_kind::permute: {
+                const gnode& src = g_.nodes[static_cast<size_t>(n.a)];
+                const std::vector<index_t> scs = contiguous_strides(src.shape);
+                std::string s = "0ull";
+                for (size_t d = 0; d < n.shape.size(); ++d)
+                    s += " + " + coord(n.shape, d) + " * " + std::to_string(scs[static_cast<size_t>(n.p_shape[d])]) + "ull";
+                const std::string v = "x" + std::to_string(counter++);
+                stmts << "    const pb_u64 " << v << " = " << s << ";\n";
+                return gen_value(k, n.a, v, stmts, counter);
+            }
             case expr_kind::transpose: {
                 const gnode& src = g_.nodes[static_cast<size_t>(n.a)];
                 const std::string v = "x" + std::to_string(counter++);
@@ -2095,8 +2153,8 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
             return -1;
         }
         if (boxes.size() != 1) return -1;
-        const kernel_arg A = as_buffer(m.a);
-        const kernel_arg B = as_buffer(m.b);
+        const gemm_operand A = as_gemm_operand(m.a);
+        const gemm_operand B = as_gemm_operand(m.b);
         int nonfinite = -1;
         if (const int t = emit_gemm_tc(id, boxes[0], k, A, B, M, N, K, &nonfinite); t >= 0) {
             // Inf or NaN in an operand: the 3xTF32 expansion turns inf * 0
@@ -2110,12 +2168,26 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
         return emit_gemm_simt(boxes[0], k, A, B, M, N, K);
     }
 
-    int lowerer::emit_gemm_simt(const box& b, kernel& k, const kernel_arg& A, const kernel_arg& B,
+    int lowerer::emit_gemm_simt(const box& b, kernel& k, const gemm_operand& A, const gemm_operand& B,
                                 int64_t M, int64_t N, int64_t K, int out_temp, int guard_temp) {
         const int out = out_temp >= 0 ? out_temp : new_temp(static_cast<size_t>(M * N) * sizeof(float));
         rank_ = 2;
         const bool wide = M * N >= (int64_t{1} << 31) - 4096 || M * K >= (int64_t{1} << 31) - 4096 ||
-                          K * N >= (int64_t{1} << 31) - 4096;
+                          K * N >= (int64_t{1} << 31) - 4096 ||
+                          A.off + (M - 1) * A.s0 + (K - 1) * A.s1 >= (int64_t{1} << 31) - 4096 ||
+                          B.off + (K - 1) * B.s0 + (N - 1) * B.s1 >= (int64_t{1} << 31) - 4096;
+        // Operand element addresses: the contiguous forms keep their
+        // original text; strided operands add offset and strides.
+        auto a_at = [&](const std::string& r, const std::string& c) {
+            if (A.contiguous(K)) return "A + (" + r + ") * " + lit(K, wide) + " + " + c;
+            return "A + " + lit(A.off, wide) + " + (" + r + ") * " + lit(A.s0, wide) + " + (" + c + ") * " +
+                   lit(A.s1, wide);
+        };
+        auto b_at = [&](const std::string& r, const std::string& c) {
+            if (B.contiguous(N)) return "B + (" + r + ") * " + lit(N, wide) + " + " + c;
+            return "B + " + lit(B.off, wide) + " + (" + r + ") * " + lit(B.s0, wide) + " + (" + c + ") * " +
+                   lit(B.s1, wide);
+        };
         const std::string I = wide ? "pb_u64" : "pb_u32";
         std::vector<int> order;
         std::ostringstream src;
@@ -2140,10 +2212,10 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
         body << "            const pb_u32 f = threadIdx.x + 256u * u;\n";
         body << "            const pb_u32 ar = f >> 4, ak = f & 15u;\n";
         body << "            As[ak][ar] = (row0 + ar < " << lit(M, wide) << " && k0 + ak < " << lit(K, wide)
-             << ") ? pb_ld(A + (row0 + ar) * " << lit(K, wide) << " + k0 + ak) : 0.0f;\n";
+             << ") ? pb_ld(" << a_at("row0 + ar", "k0 + ak") << ") : 0.0f;\n";
         body << "            const pb_u32 bk = f >> 6, bc = f & 63u;\n";
         body << "            Bs[bk][bc] = (k0 + bk < " << lit(K, wide) << " && col0 + bc < " << lit(N, wide)
-             << ") ? pb_ld(B + (k0 + bk) * " << lit(N, wide) << " + col0 + bc) : 0.0f;\n";
+             << ") ? pb_ld(" << b_at("k0 + bk", "col0 + bc") << ") : 0.0f;\n";
         body << "        }\n        __syncthreads();\n";
         body << "        const pb_u32 kmax = (" << lit(K, wide) << " - k0) < 16u ? (pb_u32)(" << lit(K, wide)
              << " - k0) : 16u;\n";
@@ -2177,8 +2249,8 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
         l.block = {256, 1, 1};
         l.schedule = "gemm CUDA-core 64x64x16 tiles, k-ordered FMA chain, fused epilogue";
         if (guard_temp >= 0) l.schedule += " (runs only for non-finite operands)";
-        l.args.push_back(A);
-        l.args.push_back(B);
+        l.args.push_back(A.arg);
+        l.args.push_back(B.arg);
         for (const kernel_arg& a : k.leaves) l.args.push_back(a);
         kernel_arg o;
         o.kind = arg_kind::temp;

@@ -53,6 +53,16 @@ namespace porch::detail {
 
     const char* kernel_prelude();
 
+    // A matmul operand [rows, cols] read in place: element (i, j) at
+    // off + i * s0 + j * s1 of `arg` (an input slot, or a contiguous temp).
+    struct gemm_operand {
+        kernel_arg arg;
+        int64_t off = 0;
+        int64_t s0 = 0;
+        int64_t s1 = 1;
+        bool contiguous(int64_t cols) const { return off == 0 && s1 == 1 && s0 == cols; }
+    };
+
     class lowerer {
       public:
         lowerer(const graph& g, plan& p);
@@ -75,6 +85,10 @@ namespace porch::detail {
         bool is_barrier(int id) const;
         int match_gemm(int id) const;
         kernel_arg as_buffer(int id);
+        // A rank-2 matmul operand: an input, a slice of an input (e.g. a
+        // strided view), or a transpose of either, read in place with
+        // strides; anything else is materialised into a contiguous temp.
+        gemm_operand as_gemm_operand(int id);
 
         static std::string pos_key(const position& p);
         affine to_linear(const position& p, const std::vector<index_t>& shape) const;
@@ -108,13 +122,13 @@ namespace porch::detail {
         int emit_gemm(int id, int mm);
         // CUDA-core GEMM (fp32 FMA chain in k order). out_temp >= 0 writes
         // into that temp; guard_temp >= 0 runs only when its first int is set.
-        int emit_gemm_simt(const box& b, kernel& k, const kernel_arg& A, const kernel_arg& B,
+        int emit_gemm_simt(const box& b, kernel& k, const gemm_operand& A, const gemm_operand& B,
                            int64_t M, int64_t N, int64_t K, int out_temp = -1, int guard_temp = -1);
         // tcgen05 3xTF32 path; returns -1 when the shape is not eligible. On
         // success *nonfinite receives a temp whose first int is set when an
         // operand holds Inf or NaN (the tensor-core result is then skipped).
-        int emit_gemm_tc(int id, const box& b, kernel& k, const kernel_arg& A,
-                         const kernel_arg& B, int64_t M, int64_t N, int64_t K, int* nonfinite);
+        int emit_gemm_tc(int id, const box& b, kernel& k, const gemm_operand& A,
+                         const gemm_operand& B, int64_t M, int64_t N, int64_t K, int* nonfinite);
 
         const graph& g_;
         plan& p_;

@@ -40,9 +40,37 @@ namespace porch::detail {
         std::vector<int> uses; // number of parents per node
         uint64_t hash = 0;
         std::string key; // full structural key (verifies plan-cache hash hits)
+        // Inputs that were strided views, read through their base, with the
+        // layout epoch seen: a bound graph is rebuilt once one of them has
+        // turned into contiguous values.
+        std::vector<std::pair<std::shared_ptr<realized_storage>, uint32_t>> view_inputs;
+        // The root is a strided view of one input slot (slice, transpose,
+        // unsqueeze, contiguous reshape and permute only): materialising it
+        // needs no kernel.
+        bool pure_view = false;
+        int view_slot = -1;
+        strided_layout view_layout;
     };
 
     graph canonicalize(const tensor_expr::node& root);
+
+    // ------------------------------------------------------ strided views --
+    // The layout of slicing `src`'s logical (contiguous) index space with
+    // (offset, strides, shape) -- the parameters tensor::operator[] records --
+    // over src's own storage; false when a stride does not step along one of
+    // src's dimensions without carrying into the next.
+    bool compose_slice(const strided_layout& src, index_t offset, const std::vector<index_t>& strides,
+                       const std::vector<index_t>& shape, strided_layout& out);
+    // True when `g`'s root only moves the data of one input slot (slice,
+    // transpose, permute, unsqueeze, reshape of a contiguous layout):
+    // `layout` is then the root over that slot's values.
+    bool pure_view(const graph& g, int& slot, strided_layout& layout);
+    // Makes `view` a view of `base` (false when base's values have been
+    // handed out or base is itself a view or a placeholder).
+    bool make_view(const std::shared_ptr<realized_storage>& base, const strided_layout& layout,
+                   const std::shared_ptr<realized_storage>& view);
+    // materialize_graph that always writes a new contiguous result.
+    tensor materialize_graph_copy(const tensor_expr::node& root);
 
     // ---------------------------------------------------------- launches --
     enum class arg_kind : uint8_t {

@@ -75,6 +75,7 @@ namespace porch::detail {
         const size_t out_count = checked_numel(out_shape);
 
         auto storage_in = tensor_access::storage(shard); // realises a lazy shard
+        make_contiguous(storage_in);                      // a view: its rows copied out
         if (asynchronous && c.stream == nullptr) {
             pbrt_stream s = nullptr;
             check(pbrt_stream_create(c.device, &s));

@@ -62,6 +62,7 @@ namespace porch {
                 case expr_kind::minimum: return "minimum";
                 case expr_kind::exp: return "exp";
                 case expr_kind::reciprocal: return "reciprocal";
+                case expr_kind::permute: return "permute";
             }
             return "?";
         }
@@ -234,6 +235,23 @@ namespace porch {
                             throw std::invalid_argument("unsqueeze axis is out of bounds");
                         std::vector<index_t> shape = s.shape;
                         shape.insert(shape.begin() + static_cast<ptrdiff_t>(n.axis), 1);
+                        return {std::move(shape), false};
+                    }
+                    case expr_kind::permute: {
+                        info s = infer_rec(*n.lhs, c);
+                        if (s.scalar)
+                            throw std::invalid_argument("permute operand must be a tensor");
+                        if (n.shape.size() != s.shape.size())
+                            throw std::invalid_argument("permutation length must equal the tensor rank");
+                        std::vector<bool> seen(s.shape.size(), false);
+                        std::vector<index_t> shape(s.shape.size());
+                        for (size_t d = 0; d < n.shape.size(); ++d) {
+                            const index_t p = n.shape[d];
+                            if (p < 0 || static_cast<size_t>(p) >= s.shape.size() || seen[static_cast<size_t>(p)])
+                                throw std::invalid_argument("permute needs a permutation of the tensor's axes");
+                            seen[static_cast<size_t>(p)] = true;
+                            shape[d] = s.shape[static_cast<size_t>(p)];
+                        }
                         return {std::move(shape), false};
                     }
                     case expr_kind::transpose: {
@@ -431,6 +449,7 @@ namespace porch {
 
     std::span<const float32_t> tensor::data() const {
         std::shared_ptr<detail::realized_storage> storage = state_->storage();
+        detail::make_contiguous(storage);
         std::scoped_lock lock{storage->host_mutex};
         if (!storage->host_current) {
             if (storage->placeholder)
@@ -448,7 +467,11 @@ namespace porch {
     }
 
     const cuda_jit::device_buffer& tensor::device_data() const {
-        return state_->storage()->device_values;
+        // The handle may be written through: contiguous values of its own,
+        // and its live views copied out first.
+        const std::shared_ptr<detail::realized_storage>& storage = state_->storage();
+        detail::escape(storage);
+        return storage->device_values;
     }
 
     const tensor& tensor::realize() const {

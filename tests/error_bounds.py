@@ -218,9 +218,10 @@ def check(got: np.ndarray, want: np.ndarray, bound: np.ndarray, rel: float, what
     cancellation makes that bar unattainable, within 2 x the forward error
     bound of fp32 evaluation. Non-finite results must agree in class.
     Returns how many elements needed the second bar."""
+    want = np.asarray(want, np.float64)
+    bound = np.broadcast_to(np.asarray(bound, np.float64), want.shape).reshape(-1)
     got = np.asarray(got, np.float64).reshape(-1)
-    want = np.asarray(want, np.float64).reshape(-1)
-    bound = np.broadcast_to(np.asarray(bound, np.float64), np.shape(want)).reshape(-1)
+    want = want.reshape(-1)
     fin = np.isfinite(want)
     assert np.array_equal(np.isfinite(got), fin), f"{what}: finite/non-finite pattern differs"
     nan_w, nan_g = np.isnan(want), np.isnan(got)

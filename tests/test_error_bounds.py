@@ -51,3 +51,13 @@ def test_bound_is_tight_enough_to_fail_a_wrong_sum(oracle_lib):
     v, e = error_bounds.evaluate(text, [x])
     wrong = x[:, :-1].astype(np.float64).sum(axis=1)
     assert np.all(np.abs(wrong - v) > 2 * e)
+
+
+def test_check_accepts_shaped_arrays():
+    want = np.arange(12, dtype=np.float64).reshape(3, 4) + 1
+    bound = np.full((3, 4), 1e-9)
+    got = want.astype(np.float32)
+    out = error_bounds.check(got, want, bound, 1e-5, "shaped")
+    assert out["elements"] == 12
+    with pytest.raises(AssertionError):
+        error_bounds.check(got + 1, want, bound, 1e-5, "shaped")
