@@ -152,6 +152,16 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
     return isinf(r) && !isinf(x) ? __uint_as_float(__float_as_uint(x) & 0xFFFFE000u) : r;
 }
 
+// Named barrier 1 over the 256 drain/epilogue threads (warps 0-7), with and
+// without an AND of a predicate.
+static __device__ __forceinline__ void pb_bar_drain() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+static __device__ __forceinline__ bool pb_bar_all(bool v) {
+    pb_u32 r;
+    asm volatile("{\n .reg .pred p, q;\n setp.ne.u32 q, %1, 0;\n bar.red.and.pred p, 1, 256, q;\n selp.u32 %0, 1, 0, p;\n}\n"
+                 : "=r"(r) : "r"((pb_u32)v) : "memory");
+    return r != 0;
+}
+
 #define PB_TMEM_LD32(taddr, v)                                                                   \
     asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15," \
                  "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"       \
@@ -183,7 +193,9 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
     } // namespace
 
     int lowerer::emit_gemm_tc(int id, const box& b, kernel& k, const gemm_operand& A,
-                              const gemm_operand& B, int64_t M, int64_t N, int64_t K, int* nonfinite) {
+                              const gemm_operand& B, int64_t M, int64_t N, int64_t K, int* nonfinite,
+                              int* row_partials) {
+        const bool softmax = row_partials != nullptr;
         (void)id;
         if (tensor_cores_disabled()) return -1;
         // Any M, N, K. The K-major hi/lo arrays have padded rows (16-byte
@@ -335,7 +347,7 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
         // a part-filled last wave runs at a higher clock.
         const int64_t tiles = tiles_m * tiles_n;
         int64_t split = 1;
-        if (tiles < 74) {
+        if (tiles < 74 && !softmax) {
             double best = static_cast<double>(tiles) / 148.0;
             for (int64_t s = 2; s <= 16; s *= 2) {
                 if (raw_kb / s < 16) break;
@@ -350,6 +362,8 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
         const int64_t kb_unit = (raw_kb + split - 1) / split;
         const int64_t units = tiles * split;
         const int part = split > 1 ? new_temp(static_cast<size_t>(split * M * ((N + 3) / 4 * 4)) * 4) : -1;
+        const int stats = softmax ? new_temp(static_cast<size_t>(M * tiles_n) * 8) : -1;
+        if (softmax) *row_partials = stats;
         std::ostringstream src;
         src << kernel_prelude() << "#define PB_PERIOD " << period << "\n#define PB_SPLIT " << split << "\n"
             << gemm_device_source() << efn;
@@ -381,6 +395,7 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
              << "    __shared__ pb_u32 tmem_slot;\n"
              << "    __shared__ int abort_flag;\n"
              << "    __shared__ int issued, consumed;\n"
+             << (softmax ? "    __shared__ float sm_max[2][PB_BM], sm_sum[2][PB_BM];\n" : "")
              << "    const pb_u32 warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;\n"
              << "    const pb_u32 base = (pb_smem(pb_dyn_smem) + 1023u) & ~1023u;\n"
              << "    const pb_u32 tiles = " << units << "u;  // work units: tiles x K splits\n"
@@ -500,6 +515,9 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
              << "                __syncwarp();\n"
              << "                if (lane == 0) pb_mbar_arrive(pb_smem(&acce[buf]));\n"
              << "            }\n"
+             << (softmax ? "            // The softmax epilogue exchanges row statistics between the\n"
+                           "            // column halves: all 256 drain threads agree on going on.\n"
+                           "            ok = pb_bar_all(ok);\n" : "")
              << "            if (!ok) break;\n"
              << "            const int r = m0 + (int)(quad * 32u + lane);\n"
              << "            const pb_u64 rr = (pb_u64)r;\n"
@@ -560,7 +578,73 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
                    << ");\n";
             }
         };
-        if (split > 1) {
+        if (softmax) {
+            // Softmax over the output row, per tile: y = tree(acc) (columns
+            // past N count as -inf), m = the tile row's maximum (the two
+            // column halves meet in shared memory), E = exp(y - m) stored in
+            // place of y, and (m, sum E) stored per (row, column tile) for
+            // the normalising pass.
+            body << "            const float pb_ninf = __int_as_float(0xff800000);\n"
+                 << "            float mx = pb_ninf;\n"
+                 << "            if (rr < " << M << "ull) {\n";
+            emit_hoisted(body, "            ");
+            body << "            #pragma unroll\n"
+                 << "            for (int c = 0; c < PB_BN / 64; ++c) {\n"
+                 << "                const int cbase = n0 + (int)half * (PB_BN / 2) + c * 32;\n"
+                 << "                #pragma unroll\n"
+                 << "                for (int j = 0; j < 32; j += 4) {\n"
+                 << "                    const pb_u64 cc = (pb_u64)(cbase + j);\n"
+                 << "                    if (cc >= " << N << "ull) {\n"
+                 << "                        acc[c * 32 + j] = pb_ninf; acc[c * 32 + j + 1] = pb_ninf;\n"
+                 << "                        acc[c * 32 + j + 2] = pb_ninf; acc[c * 32 + j + 3] = pb_ninf;\n"
+                 << "                        continue;\n"
+                 << "                    }\n";
+            emit_epilogue4(body, "                    ", "acc[c * 32 + j + e]");
+            body << "                    #pragma unroll\n"
+                 << "                    for (int e = 0; e < 4; ++e) acc[c * 32 + j + e] = cc + (pb_u64)e < " << N
+                 << "ull ? y[e] : pb_ninf;\n"
+                 << "                }\n"
+                 << "            }\n"
+                 << "            #pragma unroll\n"
+                 << "            for (int j = 0; j < PB_BN / 2; ++j) mx = acc[j] > mx ? acc[j] : mx;\n"
+                 << "            }\n"
+                 << "            const pb_u32 row = quad * 32u + lane;\n"
+                 << "            sm_max[half][row] = mx;\n"
+                 << "            pb_bar_drain();\n"
+                 << "            mx = sm_max[0][row] > sm_max[1][row] ? sm_max[0][row] : sm_max[1][row];\n"
+                 << "            float sum = 0.0f;\n"
+                 << "            if (rr < " << M << "ull) {\n"
+                 << "            #pragma unroll\n"
+                 << "            for (int j = 0; j < PB_BN / 2; ++j) {\n"
+                 << "                const float e = __expf(acc[j] - mx);\n"
+                 << "                acc[j] = e;\n"
+                 << "                sum = sum + e;\n"
+                 << "            }\n"
+                 << "            }\n"
+                 << "            sm_sum[half][row] = sum;\n"
+                 << "            pb_bar_drain();\n"
+                 << "            sum = sm_sum[0][row] + sm_sum[1][row];\n"
+                 << "            if (rr < " << M << "ull) {\n"
+                 << "            if (half == 0u) stats[rr * " << tiles_n << "ull + (pb_u64)(n0 / PB_BN)] = make_float2(mx, sum);\n"
+                 << "            #pragma unroll\n"
+                 << "            for (int c = 0; c < PB_BN / 64; ++c) {\n"
+                 << "                const int cbase = n0 + (int)half * (PB_BN / 2) + c * 32;\n"
+                 << "                float* orow = out + rr * " << N << "ull + cbase;\n"
+                 << "                #pragma unroll\n"
+                 << "                for (int j = 0; j < 32; j += 4) {\n"
+                 << "                    const pb_u64 cc = (pb_u64)(cbase + j);\n"
+                 << "                    if (cc >= " << N << "ull) continue;\n";
+            if (vec_n)
+                body << "                    pb_st4(orow + j, make_float4(acc[c * 32 + j], acc[c * 32 + j + 1], "
+                        "acc[c * 32 + j + 2], acc[c * 32 + j + 3]));\n";
+            else
+                body << "                    #pragma unroll\n"
+                     << "                    for (int e = 0; e < 4; ++e) if (cc + (pb_u64)e < " << N
+                     << "ull) orow[j + e] = acc[c * 32 + j + e];\n";
+            body << "                }\n"
+                 << "            }\n"
+                 << "            }\n";
+        } else if (split > 1) {
             // Raw partial tile of this K split; the split-K kernel below
             // sums the partials and applies the epilogue.
             body << "            const pb_u64 sp = (pb_u64)(t % PB_SPLIT);\n"
@@ -629,8 +713,8 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
             << "(const __grid_constant__ pb_tmap tm_ahi, const __grid_constant__ pb_tmap tm_alo, "
                "const __grid_constant__ pb_tmap tm_bhi, const __grid_constant__ pb_tmap tm_blo, ";
         for (size_t i = 0; i < k.leaves.size(); ++i) src << "const float* __restrict__ in" << i << ", ";
-        src << "float* __restrict__ out, int* __restrict__ err, const int* __restrict__ nf) {\n" << body.str()
-            << "}\n";
+        src << "float* __restrict__ out, " << (softmax ? "float2* __restrict__ stats, " : "")
+            << "int* __restrict__ err, const int* __restrict__ nf) {\n" << body.str() << "}\n";
         l.source = src.str();
         l.schedule = "gemm tcgen05 3xTF32 128x256x16, 4-stage TMA ring (64B swizzle, no multicast), "
                      "two TMEM accumulators drained per period into fp32 registers, fused epilogue, "
@@ -649,6 +733,7 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
             l.schedule += ", persistent CTAs (epilogue overlaps the next tile)";
         }
         if (split > 1) l.schedule += ", split-K x" + std::to_string(split) + " (raw partial tiles)";
+        if (softmax) l.schedule += ", softmax epilogue (exp(y - tile row max) and per-tile row (max, sum))";
         l.block = {320, 1, 1};
         l.smem = kStages * (2 * kBM * kBK * 4 + 2 * kBN * kBK * 4) + 1024;
         auto tmap_arg = [&](int temp, int64_t rows, int box_rows) {
@@ -666,6 +751,7 @@ static __device__ __forceinline__ float pb_tf32_hi(float x) {
                   tmap_arg(b_lo, N, kBN)};
         for (const kernel_arg& a : k.leaves) l.args.push_back(a);
         l.args.push_back(temp_arg(split > 1 ? part : out));
+        if (softmax) l.args.push_back(temp_arg(stats));
         kernel_arg e;
         e.kind = arg_kind::error_word;
         l.args.push_back(e);

@@ -220,7 +220,11 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
         int x = 0;
         size_t axis = 0;
         if (match_softmax(id, x, axis) && axis + 1 == n.shape.size()) {
-            t = emit_softmax(id, x);
+            if (n.shape.size() == 2) {
+                const int mm = match_gemm(x);
+                if (mm >= 0) t = emit_gemm_softmax(id, x, mm);
+            }
+            if (t < 0) t = emit_softmax(id, x);
         } else if (n.kind == expr_kind::sum || n.kind == expr_kind::max) {
             t = emit_reduce(id);
         } else {
@@ -2166,6 +2170,131 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
             return t;
         }
         return emit_gemm_simt(boxes[0], k, A, B, M, N, K);
+    }
+
+    int lowerer::emit_gemm_softmax(int id, int x, int mm) {
+        (void)id;
+        const gnode& m = g_.nodes[static_cast<size_t>(mm)];
+        const gnode& xv = g_.nodes[static_cast<size_t>(x)];
+        if (m.shape != xv.shape) return -1;
+        const int64_t M = m.shape[0], N = m.shape[1];
+        const int64_t K = g_.nodes[static_cast<size_t>(m.a)].shape[1];
+        const int64_t T = (N + 255) / 256; // column tiles of the GEMM
+        if (T > 1536) return -1;           // the pass keeps a row's T factors in shared memory
+        kernel k;
+        std::vector<box> boxes;
+        try {
+            boxes = build_boxes(k, x, xv.shape, mm);
+        } catch (const not_fusable&) {
+            return -1;
+        } catch (const not_affine&) {
+            return -1;
+        }
+        if (boxes.size() != 1) return -1;
+        const gemm_operand A = as_gemm_operand(m.a);
+        const gemm_operand B = as_gemm_operand(m.b);
+        int nonfinite = -1, stats = -1;
+        const int out = emit_gemm_tc(x, boxes[0], k, A, B, M, N, K, &nonfinite, &stats);
+        if (out < 0) return -1;
+        auto temp = [](int t) {
+            kernel_arg a;
+            a.kind = arg_kind::temp;
+            a.index = t;
+            return a;
+        };
+        // Inf or NaN in an operand: the CUDA-core GEMM writes y = tree(A@B)
+        // into the output, then a row softmax with the reference's own
+        // steps (max with -FLT_MAX as seed and (l > r ? l : r), exp(y - max)
+        // summed, then divided; src/ops.cpp:7-14) runs in place. Both return
+        // at once for finite operands.
+        emit_gemm_simt(boxes[0], k, A, B, M, N, K, out, nonfinite);
+        {
+            std::ostringstream src;
+            src << kernel_prelude();
+            std::ostringstream body;
+            body << "    if (*(const volatile int*)nf == 0) return;\n"
+                 << "    __shared__ float red[256];\n"
+                 << "    for (pb_u64 r = blockIdx.x; r < " << M << "ull; r += gridDim.x) {\n"
+                 << "        float* row = p + r * " << N << "ull;\n"
+                 << "        float m = -3.40282347e+38f;\n"
+                 << "        for (pb_u64 c = threadIdx.x; c < " << N << "ull; c += 256u) { const float v = row[c]; m = v > m ? v : m; }\n"
+                 << "        red[threadIdx.x] = m;\n        __syncthreads();\n"
+                 << "        for (pb_u32 h = 128u; h > 0u; h >>= 1) {\n"
+                 << "            if (threadIdx.x < h) { const float a = red[threadIdx.x], b = red[threadIdx.x + h]; red[threadIdx.x] = a > b ? a : b; }\n"
+                 << "            __syncthreads();\n        }\n"
+                 << "        m = red[0];\n        __syncthreads();\n"
+                 << "        float s = 0.0f;\n"
+                 << "        for (pb_u64 c = threadIdx.x; c < " << N << "ull; c += 256u) s = s + __expf(row[c] - m);\n"
+                 << "        red[threadIdx.x] = s;\n        __syncthreads();\n"
+                 << "        for (pb_u32 h = 128u; h > 0u; h >>= 1) {\n"
+                 << "            if (threadIdx.x < h) red[threadIdx.x] = red[threadIdx.x] + red[threadIdx.x + h];\n"
+                 << "            __syncthreads();\n        }\n"
+                 << "        s = red[0];\n        __syncthreads();\n"
+                 << "        for (pb_u64 c = threadIdx.x; c < " << N << "ull; c += 256u) row[c] = __expf(row[c] - m) / s;\n"
+                 << "        __syncthreads();\n    }\n";
+            launch_spec l;
+            l.name = "pb_softmax_rows_nonfinite";
+            src << "extern \"C\" __global__ void __launch_bounds__(256) " << l.name
+                << "(float* __restrict__ p, const int* __restrict__ nf) {\n" << body.str() << "}\n";
+            l.source = src.str();
+            l.schedule = "row softmax in place (runs only for non-finite matmul operands)";
+            l.grid = {static_cast<uint32_t>(std::min<int64_t>(M, 148 * 8)), 1, 1};
+            l.block = {256, 1, 1};
+            l.args = {temp(out), temp(nonfinite)};
+            finish_kernel(l);
+            p_.launches.push_back(std::move(l));
+        }
+        // The normalising pass, in place: per row, M = max of the tiles'
+        // maxima, S = sum_t s_t exp(m_t - M), and each tile's values times
+        // f_t = exp(m_t - M) * (1 / S). A warp per row; the row's T factors
+        // in shared memory.
+        {
+            const bool vec = N % 4 == 0;
+            std::ostringstream src;
+            src << kernel_prelude();
+            std::ostringstream body;
+            body << "    if (*(const volatile int*)nf != 0) return;  // the fallback above wrote the rows\n"
+                 << "    __shared__ float f[8][" << T << "];\n"
+                 << "    const pb_u32 warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;\n"
+                 << "    for (pb_u64 r = (pb_u64)blockIdx.x * 8u + warp; r < " << M << "ull; r += (pb_u64)gridDim.x * 8u) {\n"
+                 << "        const float2* st = stats + r * " << T << "ull;\n"
+                 << "        float m = __int_as_float(0xff800000);\n"
+                 << "        for (pb_u32 t = lane; t < " << T << "u; t += 32u) { const float v = st[t].x; m = v > m ? v : m; }\n"
+                 << "        #pragma unroll\n"
+                 << "        for (int o = 16; o > 0; o >>= 1) { const float v = __shfl_xor_sync(0xffffffffu, m, o); m = v > m ? v : m; }\n"
+                 << "        float s = 0.0f;\n"
+                 << "        for (pb_u32 t = lane; t < " << T << "u; t += 32u) s = s + st[t].y * __expf(st[t].x - m);\n"
+                 << "        #pragma unroll\n"
+                 << "        for (int o = 16; o > 0; o >>= 1) s = s + __shfl_xor_sync(0xffffffffu, s, o);\n"
+                 << "        const float inv = 1.0f / s;\n"
+                 << "        for (pb_u32 t = lane; t < " << T << "u; t += 32u) f[warp][t] = __expf(st[t].x - m) * inv;\n"
+                 << "        __syncwarp();\n"
+                 << "        float* row = p + r * " << N << "ull;\n";
+            if (vec)
+                body << "        for (pb_u32 c = lane; c < " << N / 4 << "u; c += 32u) {\n"
+                     << "            float4 v = pb_ld4(row + 4u * c);\n"
+                     << "            const float g = f[warp][(4u * c) >> 8];\n"
+                     << "            v.x = v.x * g; v.y = v.y * g; v.z = v.z * g; v.w = v.w * g;\n"
+                     << "            pb_st4(row + 4u * c, v);\n"
+                     << "        }\n";
+            else
+                body << "        for (pb_u32 c = lane; c < " << N << "u; c += 32u) row[c] = row[c] * f[warp][c >> 8];\n";
+            body << "        __syncwarp();\n    }\n";
+            launch_spec l;
+            l.name = "pb_softmax_norm_" + hex64(hash_string(body.str())).substr(0, 8);
+            src << "extern \"C\" __global__ void __launch_bounds__(256) " << l.name
+                << "(float* __restrict__ p, const float2* __restrict__ stats, const int* __restrict__ nf) {\n"
+                << body.str() << "}\n";
+            l.source = src.str();
+            l.schedule = "softmax normalising pass over the GEMM's exp tiles: a warp per row, " +
+                         std::to_string(T) + " tile factors per row";
+            l.grid = {static_cast<uint32_t>(std::min<int64_t>((M + 7) / 8, 148 * 16)), 1, 1};
+            l.block = {256, 1, 1};
+            l.args = {temp(out), temp(stats), temp(nonfinite)};
+            finish_kernel(l);
+            p_.launches.push_back(std::move(l));
+        }
+        return out;
     }
 
     int lowerer::emit_gemm_simt(const box& b, kernel& k, const gemm_operand& A, const gemm_operand& B,

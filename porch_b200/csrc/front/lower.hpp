@@ -127,8 +127,17 @@ namespace porch::detail {
         // tcgen05 3xTF32 path; returns -1 when the shape is not eligible. On
         // success *nonfinite receives a temp whose first int is set when an
         // operand holds Inf or NaN (the tensor-core result is then skipped).
+        // With row_partials != nullptr the epilogue is a softmax over each
+        // output row: the result temp receives exp(y - m) per 128 x 256 tile
+        // and *row_partials a temp of [M, ceil(N / 256)] float2 (m, sum) --
+        // the tile's row maximum and its sum of exp(y - m).
         int emit_gemm_tc(int id, const box& b, kernel& k, const gemm_operand& A,
-                         const gemm_operand& B, int64_t M, int64_t N, int64_t K, int* nonfinite);
+                         const gemm_operand& B, int64_t M, int64_t N, int64_t K, int* nonfinite,
+                         int* row_partials = nullptr);
+        // softmax(x, last axis) where x is an elementwise tree over one
+        // rank-2 matmul `mm`: the GEMM's softmax epilogue plus a normalising
+        // pass; -1 when the tensor-core GEMM does not apply.
+        int emit_gemm_softmax(int id, int x, int mm);
 
         const graph& g_;
         plan& p_;
