@@ -163,9 +163,11 @@ int pb_timer_begin(int device, void** timer);
 int pb_timer_end(void* timer, float* milliseconds);
 /* Synchronise this thread's porch stream on `device`. */
 int pb_device_synchronize(int device);
-/* Returns every cached device block of `device` to the driver's pool
- * (*released receives the bytes; may be NULL). Blocks freed by porch stay
- * cached per stream for reuse without a driver call until then. */
+/* Drops every cached device block of `device` (*released receives the
+ * bytes; may be NULL). Blocks freed by porch stay cached per stream for
+ * reuse without a driver call until then; they are carved from 256 MiB
+ * slabs (a larger block has a slab of its own), and a slab goes back to the
+ * driver once every block carved from it has been dropped. */
 int pb_empty_cache(int device, size_t* released);
 /* Kernel launches issued by this library since process start. */
 uint64_t pb_launch_count(void);
@@ -224,6 +226,16 @@ int pb_allgather_rows_async(pb_comm* comm, const pb_tensor* shard, int64_t total
 /* Waits, bounded by the communicator's timeout, until every asynchronous
  * gather issued so far has completed. */
 int pb_comm_wait(pb_comm* comm);
+
+/* ---- failure-detection test hook ---------------------------------------- */
+/* No counterpart in the reference, which has no device-side waits. While
+ * enabled (it is off by default), tensor-core GEMM plans built from then on
+ * (a plan key of their own) make one CTA wait on an mbarrier that nothing
+ * arrives on: its bounded wait gives up (about two seconds), the kernel
+ * records code 0x7c07 in the device error word, waits for its own copies in
+ * flight, frees its tensor memory and returns; the next synchronisation
+ * raises PB_ERR_RUNTIME. Only for tests of that path. */
+int pb_test_gemm_stall(int enable);
 
 /* ---- matmul without allocation ------------------------------------------ */
 /* C = A @ B in fp32 (3xTF32 on tcgen05), on raw device pointers, allocating

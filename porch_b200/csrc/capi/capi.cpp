@@ -1,5 +1,6 @@
 // Flat C-ABI over the porch C++ API (include/porch_b200.h).
 #include "porch_b200.h"
+#include "lower.hpp"
 
 #include "../front/detail.hpp"
 #include "porch/backend.hpp"
@@ -344,6 +345,10 @@ int pb_expr_unsqueeze(const pb_expr* value, size_t axis, pb_expr** out) {
         require(out, "out");
         *out = wrap(porch::unsqueeze(value->value, axis));
     });
+}
+
+int pb_test_gemm_stall(int enable) {
+    return guarded([&] { porch::detail::set_test_gemm_stall(enable != 0); });
 }
 
 int pb_expr_permute(const pb_expr* value, const int64_t* perm, size_t rank, pb_expr** out) {

@@ -94,8 +94,12 @@ namespace porch::detail {
     // `events` -- recorded behind reads on other streams -- has completed.
     void defer_recycle(int device, uint64_t ptr, size_t capacity, std::shared_ptr<stream_ref> stream,
                        std::vector<std::pair<int, pbrt_event>> events);
-    // Gives every cached block of `device` back to the driver; returns bytes.
+    // Drops every cached block of `device` (slabs left with no block go back
+    // to the driver); returns the bytes dropped.
     size_t release_cached_blocks(int device);
+    // Gives one block back (a slab block: to its slab; any other: to the
+    // driver). The caller has ordered it after every use.
+    void release_block(int device, uint64_t ptr, size_t capacity);
     // Makes `stream` wait for the buffer's producer when they differ, and
     // records `stream` as a reader so the eventual free is ordered after it.
     void order_read(

@@ -41,6 +41,7 @@
 // No TMA multicast is used anywhere.
 #include "lower.hpp"
 
+#include <atomic>
 #include <cmath>
 #include <cstdlib>
 #include <sstream>
@@ -185,12 +186,17 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
             return b;
         }
 
+        std::atomic<bool> g_test_stall{false};
+
         bool tensor_cores_disabled() {
             const char* v = std::getenv("PORCH_B200_GEMM");
             return v != nullptr && std::string{v} == "simt";
         }
 
     } // namespace
+
+    void set_test_gemm_stall(bool on) { g_test_stall.store(on); }
+    bool test_gemm_stall() { return g_test_stall.load(); }
 
     int lowerer::emit_gemm_tc(int id, const box& b, kernel& k, const gemm_operand& A,
                               const gemm_operand& B, int64_t M, int64_t N, int64_t K, int* nonfinite,
@@ -365,7 +371,8 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
         const int stats = softmax ? new_temp(static_cast<size_t>(M * tiles_n) * 8) : -1;
         if (softmax) *row_partials = stats;
         std::ostringstream src;
-        src << kernel_prelude() << "#define PB_PERIOD " << period << "\n#define PB_SPLIT " << split << "\n"
+        src << kernel_prelude() << (test_gemm_stall() ? "#define PB_TEST_STALL 1\n" : "") << "#define PB_PERIOD "
+            << period << "\n#define PB_SPLIT " << split << "\n"
             << gemm_device_source() << efn;
         // Tile t -> output origin, tiles ordered in groups of group_m M-tiles
         // that sweep N (consecutive tiles, run at the same time by the
@@ -395,6 +402,7 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
              << "    __shared__ pb_u32 tmem_slot;\n"
              << "    __shared__ int abort_flag;\n"
              << "    __shared__ int issued, consumed;\n"
+             << "#ifdef PB_TEST_STALL\n    __shared__ __align__(8) unsigned long long stall_bar;\n#endif\n"
              << (softmax ? "    __shared__ float sm_max[2][PB_BM], sm_sum[2][PB_BM];\n" : "")
              << "    const pb_u32 warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;\n"
              << "    const pb_u32 base = (pb_smem(pb_dyn_smem) + 1023u) & ~1023u;\n"
@@ -406,6 +414,7 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
              << "        for (int s = 0; s < PB_STAGES; ++s) { pb_mbar_init(pb_smem(&full_bar[s]), 1); pb_mbar_init(pb_smem(&empty_bar[s]), 1); }\n"
              << "        for (int b = 0; b < 2; ++b) { pb_mbar_init(pb_smem(&accf[b]), 1); pb_mbar_init(pb_smem(&acce[b]), 8); }\n"
              << "        pb_mbar_init(pb_smem(&done_bar), 1);\n"
+             << "#ifdef PB_TEST_STALL\n        pb_mbar_init(pb_smem(&stall_bar), 1);\n#endif\n"
              << "        asm volatile(\"fence.mbarrier_init.release.cluster;\" ::: \"memory\");\n"
              << "    }\n"
              << "    if (warp == 9) {\n"
@@ -452,6 +461,11 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
              // drain of period p - 2.
              << "            int g = 0, per_base = 0;\n"
              << "            bool stop = false;\n"
+             // Failure-detection test hook: CTA 0 waits on a barrier nothing
+             // arrives on, so its bounded wait gives up (site 7).
+             << "#ifdef PB_TEST_STALL\n"
+             << "            if (blockIdx.x == 0u && !pb_wait(pb_smem(&stall_bar), 0u, &abort_flag, err, 7)) stop = true;\n"
+             << "#endif\n"
              << "            for (pb_u32 t = blockIdx.x; t < tiles && !stop; t += gridDim.x, per_base += periods) {\n"
              << "                for (int kb = 0; kb < num_kb; ++kb, ++g) {\n"
              << "                    const int s = g % PB_STAGES;\n"

@@ -9,6 +9,7 @@
 //    cuModuleLoadData on every launch (src/cuda_jit.cpp:819-823).
 #include "detail.hpp"
 
+#include <algorithm>
 #include <cstring>
 #include <map>
 #include <sstream>
@@ -90,12 +91,66 @@ namespace porch::detail {
             std::vector<std::pair<int, pbrt_event>> events; // (device, event) per foreign reader
         };
 
+        // Blocks are carved from slabs of device memory by bumping an
+        // offset, so a cache miss costs no driver call: cuMemAlloc runs once
+        // per 256 MiB slab (a larger request gets a slab of its own), and it
+        // stalls behind the device's queued work, up to milliseconds while
+        // GEMMs run. A block is never handed back to its slab one by one: it
+        // lives in the size-class free lists; a slab returns to the driver
+        // once every block carved from it has been dropped from the cache.
+        struct slab {
+            size_t size = 0;
+            size_t used = 0; // bump offset
+            size_t live = 0; // blocks carved and not yet dropped
+        };
+        constexpr size_t kSlabBytes = size_t{256} << 20;
+
         struct device_cache {
             std::mutex mutex;
             std::unordered_map<size_t, std::vector<cached_block>> free;
             std::vector<pending_block> pending;
             size_t cached_bytes = 0;
+            std::map<uint64_t, slab> slabs; // by base address
+            uint64_t current = 0;           // the slab new blocks are bumped from
         };
+
+        // A block of `cls` bytes (a multiple of 512) from the current slab,
+        // or from a new one. Caller holds dc.mutex.
+        int slab_alloc_locked(int device, device_cache& dc, size_t cls, uint64_t* out) {
+            if (dc.current != 0) {
+                slab& s = dc.slabs.at(dc.current);
+                if (s.used + cls <= s.size) {
+                    *out = dc.current + s.used;
+                    s.used += cls;
+                    ++s.live;
+                    return PBRT_OK;
+                }
+            }
+            const size_t size = std::max(kSlabBytes, cls);
+            uint64_t base = 0;
+            const int st = pbrt_mem_alloc(device, size, &base);
+            if (st != PBRT_OK) return st;
+            host_count("slab_alloc");
+            dc.slabs[base] = slab{size, cls, 1};
+            if (size == kSlabBytes) dc.current = base; // larger slabs hold one block
+            *out = base;
+            return PBRT_OK;
+        }
+
+        // Drops one block carved from a slab; the slab goes back to the
+        // driver when it was the last (cuMemFree waits for the device's
+        // queued work, so nothing still running can touch it). Caller holds
+        // dc.mutex.
+        void slab_drop_locked(int device, device_cache& dc, uint64_t ptr) {
+            auto it = dc.slabs.upper_bound(ptr);
+            if (it == dc.slabs.begin()) return;
+            --it;
+            if (ptr >= it->first + it->second.size) return;
+            if (--it->second.live != 0) return;
+            (void)pbrt_mem_free(device, it->first);
+            if (dc.current == it->first) dc.current = 0;
+            dc.slabs.erase(it);
+        }
 
         // Moves pending blocks whose readers have all finished to the free
         // lists. Caller holds dc.mutex.
@@ -158,19 +213,29 @@ namespace porch::detail {
             bytes = dc.cached_bytes;
             dc.cached_bytes = 0;
         }
-        // Blocks come from cuMemAlloc; cuMemFree waits for the device's
-        // queued work, so no block is freed under a running kernel.
-        for (auto& [size, list] : drop)
-            for (auto& b : list) (void)pbrt_mem_free(device, b.ptr);
         for (auto& p : waiting) {
             for (const auto& [dev, ev] : p.events) {
                 (void)pbrt_event_synchronize(dev, ev);
                 (void)pbrt_event_destroy(dev, ev);
             }
-            (void)pbrt_mem_free(device, p.ptr);
             bytes += p.capacity;
         }
+        // Slabs whose every block is dropped here go back to the driver.
+        std::scoped_lock lock{dc.mutex};
+        for (auto& [size, list] : drop)
+            for (auto& b : list) slab_drop_locked(device, dc, b.ptr);
+        for (auto& p : waiting) slab_drop_locked(device, dc, p.ptr);
         return bytes;
+    }
+
+    void release_block(int device, uint64_t ptr, size_t capacity) {
+        if (capacity == 0) {
+            (void)pbrt_mem_free(device, ptr);
+            return;
+        }
+        device_cache& dc = blocks().of(device);
+        std::scoped_lock lock{dc.mutex};
+        slab_drop_locked(device, dc, ptr);
     }
 
     void defer_recycle(int device, uint64_t ptr, size_t capacity, std::shared_ptr<stream_ref> stream,
@@ -208,9 +273,15 @@ namespace porch::detail {
             }
             host_count(state->ptr ? "alloc_cache_hit" : "alloc_cache_miss");
             if (state->ptr == 0) {
-                int st = pbrt_mem_alloc(device, cls, &state->ptr);
-                if (st != PBRT_OK && release_cached_blocks(device) != 0)
-                    st = pbrt_mem_alloc(device, cls, &state->ptr);
+                int st = PBRT_OK;
+                {
+                    std::scoped_lock lock{dc.mutex};
+                    st = slab_alloc_locked(device, dc, cls, &state->ptr);
+                }
+                if (st != PBRT_OK && release_cached_blocks(device) != 0) {
+                    std::scoped_lock lock{dc.mutex};
+                    st = slab_alloc_locked(device, dc, cls, &state->ptr);
+                }
                 check(st);
             }
             state->producer = stream;
@@ -303,7 +374,7 @@ namespace porch::cuda_jit {
             for (const auto& [dev, ev] : events) (void)pbrt_event_destroy(dev, ev);
             for (const auto& reader : readers)
                 if (reader != free_stream) (void)pbrt_stream_synchronize(reader->device, reader->stream);
-            (void)pbrt_mem_free(device, ptr);
+            detail::release_block(device, ptr, capacity);
         } catch (...) {
         }
     }

@@ -53,6 +53,12 @@ namespace porch::detail {
 
     const char* kernel_prelude();
 
+    // Test hook (off by default; part of the plan key): tcgen05 GEMMs built
+    // while it is on make CTA 0 wait on a barrier nothing arrives on, so the
+    // bounded wait expires and the kernel reports and tears down.
+    void set_test_gemm_stall(bool on);
+    bool test_gemm_stall();
+
     // A matmul operand [rows, cols] read in place: element (i, j) at
     // off + i * s0 + j * s1 of `arg` (an input slot, or a contiguous temp).
     struct gemm_operand {

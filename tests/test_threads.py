@@ -74,3 +74,45 @@ def test_threads_realise_the_same_values(gpu):
            if not np.array_equal(got.view(np.uint32), want[key[2]].view(np.uint32))]
     assert len(results) == 6 * 4 * 7
     assert not bad, bad[:10]
+
+
+@pytest.mark.gpu
+def test_slab_allocator_serves_misses_without_driver_calls_and_releases(gpu):
+    """Cache misses are carved from 256 MiB slabs: many distinct block sizes
+    cost at most a slab or two, and dropping the cache gives a slab whose
+    blocks are all gone back to the driver."""
+    import ctypes
+
+    api = gpu
+    cu = ctypes.CDLL("libcuda.so.1")
+
+    def free_bytes():
+        ctx = ctypes.c_void_p()
+        assert cu.cuDevicePrimaryCtxRetain(ctypes.byref(ctx), 0) == 0
+        assert cu.cuCtxPushCurrent_v2(ctx) == 0
+        f, t = ctypes.c_size_t(), ctypes.c_size_t()
+        assert cu.cuMemGetInfo_v2(ctypes.byref(f), ctypes.byref(t)) == 0
+        assert cu.cuCtxPopCurrent_v2(ctypes.byref(ctypes.c_void_p())) == 0
+        cu.cuDevicePrimaryCtxRelease_v2(0)
+        return f.value
+
+    api.synchronize()
+    api.empty_cache(0)
+    base = free_bytes()
+    api.host_profile_enable(True)
+    api.host_profile_read()
+    held = []
+    for i in range(40):  # 40 distinct sizes from 40 KB to 1.6 MB: all misses
+        n = 1024 * (i + 1) * 10
+        held.append(api.materialize(api.tensor([n], np.ones(n, np.float32)) + float(i)))
+    api.synchronize()
+    counters = api.host_profile_read()
+    api.host_profile_enable(False)
+    assert counters.get("alloc_cache_miss", 0) >= 40
+    assert counters.get("slab_alloc", 0) <= 2, counters
+    for i, t in enumerate(held):
+        assert float(t.cpu()[0]) == 1.0 + i
+    held.clear()
+    api.synchronize()
+    api.empty_cache(0)
+    assert free_bytes() >= base - (64 << 20)
