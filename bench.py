@@ -68,6 +68,12 @@ KEYS = {
     "c3b_relu_logistic": ["x"], "c4_matmul": ["a", "b", "bias"],
     "c5_mlp": ["x", "w1", "b1", "w2", "b2"],
 }
+# Activations of the GEMM configurations: in a serving loop a data loader
+# writes each new batch through the tensor's device pointer, so the bench
+# hands their pointers out (tensor::device_data()) and their 3xTF32 split
+# runs every step; the weights (c4's B, c5's W1 and W2) are realised once and
+# keep their split from the first step on.
+ACTIVATIONS = {"c4_matmul": ["a"], "c5_mlp": ["x"]}
 # Kernel family whose launches the roofline line describes.
 DOMINANT = {"c1_elementwise": "pb_elem", "c2_view": "pb_elem", "c3a_softmax": "pb_softmax",
             "c3b_relu_logistic": "pb_elem", "c4_matmul": "pb_gemm_tc", "c5_mlp": "pb_gemm_tc"}
@@ -270,6 +276,10 @@ def cpu_baseline(workload: str, arrays, seconds: float = 10.0) -> dict:
             "sample": f"{sample}, evaluated {reps} times", "seconds": round(dt, 3)}
 
 
+def shape_of(workload: str, key: str) -> list:
+    return CONFIGS[workload][0][KEYS[workload].index(key)][0]
+
+
 def _config_keys(workload: str, world: int) -> dict:
     specs = CONFIGS[workload][0]
     return {"workload": workload,
@@ -297,6 +307,9 @@ def measure(api, workload: str, args, rank, world, local, dist, cpu_seconds: flo
     sets = []
     for s in range(n_sets):
         sets.append({k: api.tensor(list(a.shape), a, device=device) for k, a in zip(keys, arrays)})
+    for t in sets:
+        for k in ACTIVATIONS.get(workload, []):
+            t[k].device_data()
     graphs = [api.config_graph(workload, t) for t in sets]
 
     # Config 5 gathers its output P whole on every rank (one ncclAllGather
@@ -512,6 +525,10 @@ def measure(api, workload: str, args, rank, world, local, dist, cpu_seconds: flo
         "dtype": "f32", "data": "synthetic (seeded; distributions as the baseline config)",
         "config": config,
         "setup": {"l2": f"inputs rotated over {n_sets} device-resident sets, each larger than L2",
+                  "weights": (f"{', '.join(k for k in KEYS[workload] if k not in ACTIVATIONS[workload] and k[0] in 'wb' and len(shape_of(workload, k)) == 2)} "
+                              "realised once and keep their 3xTF32 split; the activations' device pointers are handed "
+                              "out (as a data loader writing each batch would), so their split runs every step"
+                              if workload in ACTIVATIONS else None),
                   "collective": (f"ncclAllGather of the output rows ({total_rows} rows whole on every "
                                  "rank) inside every step, on its own stream (overlapping the next "
                                  "step's GEMMs), all complete before the timed region ends"

@@ -145,6 +145,15 @@ namespace porch::detail {
         std::atomic<uint32_t> layout_epoch{0};
         bool escaped = false; // a handle to device_values was handed out
         std::vector<std::weak_ptr<realized_storage>> views;
+
+        // 3xTF32 splits of these values kept for later GEMMs (hi, lo and the
+        // non-finite flag, per operand layout key); dropped when a handle to
+        // the values is handed out. Guarded by view_mutex.
+        struct kept_split {
+            std::string key;
+            cuda_jit::device_buffer hi, lo, flag;
+        };
+        std::vector<kept_split> splits;
     };
 
     // A strided layout over a storage's linear values.

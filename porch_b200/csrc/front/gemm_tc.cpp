@@ -225,7 +225,11 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
         // Set by the split kernels when an operand holds Inf or NaN; the
         // tensor-core kernels then leave the output to the CUDA-core GEMM
         // that follows them in the plan.
+        // Each split flags its own operand (fa, fb: a kept split keeps its
+        // flag); a one-thread merge then sets nf = fa | fb.
         const int nf = new_temp(256);
+        const int fa = new_temp(256);
+        const int fb = new_temp(256);
         *nonfinite = nf;
         auto temp_arg = [](int t) {
             kernel_arg a;
@@ -237,11 +241,16 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
             launch_spec l;
             l.name = "pb_nonfinite_clear";
             l.source = std::string(kernel_prelude()) +
-                       "extern \"C\" __global__ void pb_nonfinite_clear(int* nf) { nf[0] = 0; }\n";
-            l.schedule = "clear the non-finite operand flag";
+                       "extern \"C\" __global__ void pb_nonfinite_clear(int* fa, int* fb) { fa[0] = 0; fb[0] = 0; }\n";
+            l.schedule = "clear the operands' non-finite flags";
             l.grid = {1, 1, 1};
             l.block = {1, 1, 1};
-            l.args = {temp_arg(nf)};
+            kernel_arg ca, cb;
+            ca.kind = cb.kind = arg_kind::flag_clear;
+            ca.index = fa;
+            cb.index = fb;
+            ca.value = cb.value = static_cast<uint64_t>(nf); // harmless stand-in for a kept flag
+            l.args = {ca, cb};
             finish_kernel(l);
             p_.launches.push_back(std::move(l));
         }
@@ -255,7 +264,7 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
         // and the K-major stores stay coalesced; otherwise the same tiles
         // with strided loads.
         auto emit_split = [&](const std::string& what, const gemm_operand& X, int64_t R, int64_t sr, int64_t sk,
-                              int hi_t, int lo_t) {
+                              int hi_t, int lo_t, int flag_t) {
             std::ostringstream src;
             src << kernel_prelude() << gemm_device_source();
             launch_spec l;
@@ -317,12 +326,32 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
                 l.grid = {static_cast<uint32_t>((R + 63) / 64), static_cast<uint32_t>((Kp + 63) / 64), 1};
             }
             l.source = src.str();
-            l.args = {X.arg, temp_arg(hi_t), temp_arg(lo_t), temp_arg(nf)};
+            l.args = {X.arg, temp_arg(hi_t), temp_arg(lo_t), temp_arg(flag_t)};
+            if (X.arg.kind == arg_kind::slot) {
+                // A realised input: its storage may keep this split.
+                l.cache_slot = X.arg.index;
+                l.cache_key = "split R" + std::to_string(R) + " K" + std::to_string(K) + " Kp" + std::to_string(Kp) +
+                              " off" + std::to_string(X.off) + " sr" + std::to_string(sr) + " sk" + std::to_string(sk);
+                l.cache_temps = {hi_t, lo_t, flag_t};
+            }
             finish_kernel(l);
             p_.launches.push_back(std::move(l));
         };
-        emit_split("A", A, M, A.s0, A.s1, a_hi, a_lo);
-        emit_split("B", B, N, B.s1, B.s0, b_hi, b_lo);
+        emit_split("A", A, M, A.s0, A.s1, a_hi, a_lo, fa);
+        emit_split("B", B, N, B.s1, B.s0, b_hi, b_lo, fb);
+        {
+            launch_spec l;
+            l.name = "pb_nonfinite_merge";
+            l.source = std::string(kernel_prelude()) +
+                       "extern \"C\" __global__ void pb_nonfinite_merge(int* nf, const int* fa, const int* fb) "
+                       "{ nf[0] = fa[0] | fb[0]; }\n";
+            l.schedule = "merge the operands' non-finite flags";
+            l.grid = {1, 1, 1};
+            l.block = {1, 1, 1};
+            l.args = {temp_arg(nf), temp_arg(fa), temp_arg(fb)};
+            finish_kernel(l);
+            p_.launches.push_back(std::move(l));
+        }
         // ---- 3. tcgen05 GEMM + epilogue -------------------------------------
         std::vector<int> order;
         const std::string efn = emit_expr_function(b, "0", order);

@@ -453,9 +453,35 @@ namespace porch::detail {
         }
         if (timing) tb = now_ns();
 
+        // Operand splits kept by their input's storage: the launch is
+        // skipped and its hi / lo / flag temps are the kept buffers.
+        std::vector<char> skip(p->launches.size(), 0);
+        std::vector<cuda_jit::device_buffer> kept(p->temp_bytes.size());
+        for (size_t li = 0; li < p->launches.size(); ++li) {
+            const launch_spec& l = p->launches[li];
+            if (l.cache_slot < 0) continue;
+            realized_storage& st = *g.slots[static_cast<size_t>(l.cache_slot)];
+            std::scoped_lock lock{st.view_mutex};
+            for (const auto& e : st.splits) {
+                if (e.key != l.cache_key) continue;
+                skip[li] = 1;
+                kept[static_cast<size_t>(l.cache_temps[0])] = e.hi;
+                kept[static_cast<size_t>(l.cache_temps[1])] = e.lo;
+                kept[static_cast<size_t>(l.cache_temps[2])] = e.flag;
+                break;
+            }
+        }
         std::vector<cuda_jit::device_buffer> temps;
         temps.reserve(p->temp_bytes.size());
-        for (size_t bytes : p->temp_bytes) temps.push_back(allocate(device, bytes, stream));
+        for (size_t ti = 0; ti < p->temp_bytes.size(); ++ti) {
+            if (const auto& ks = cuda_jit::buffer_access::state(kept[ti]); ks != nullptr) {
+                order_read(*ks, stream);
+                temps.push_back(kept[ti]);
+                host_count("split_kept");
+            } else {
+                temps.push_back(allocate(device, p->temp_bytes[ti], stream));
+            }
+        }
         if (timing) t2 = now_ns();
 
         uint64_t error_word = 0;
@@ -470,7 +496,9 @@ namespace porch::detail {
         };
         tensor_map_storage maps[8];
         int nmaps = 0;
-        for (launch_spec& l : p->launches) {
+        for (size_t li = 0; li < p->launches.size(); ++li) {
+            if (skip[li]) continue;
+            launch_spec& l = p->launches[li];
             pbrt_function fn = nullptr;
             const bool slot = device < static_cast<int>(l.per_device->function.size());
             if (slot) fn = l.per_device->function[device].load(std::memory_order_acquire);
@@ -519,6 +547,12 @@ namespace porch::detail {
                     case arg_kind::u64:
                         values[i] = a.value;
                         break;
+                    case arg_kind::flag_clear: {
+                        const bool is_kept = cuda_jit::buffer_access::state(kept[static_cast<size_t>(a.index)]) != nullptr;
+                        const size_t t = is_kept ? static_cast<size_t>(a.value) : static_cast<size_t>(a.index);
+                        values[i] = cuda_jit::buffer_access::state(temps[t])->ptr;
+                        break;
+                    }
                     case arg_kind::tmap: {
                         if (nmaps >= 8) throw std::runtime_error("too many tensor maps");
                         const uint64_t base =
@@ -548,6 +582,20 @@ namespace porch::detail {
             check(pbrt_launch_ex(device, fn, grid.data(), l.block.data(), l.smem, stream->stream,
                                  params.data(), l.cluster_x > 1 ? cluster : nullptr,
                                  l.pdl ? PBRT_LAUNCH_PDL : 0u));
+        }
+        // Splits computed now are kept by their input's storage (a few per
+        // storage, the oldest dropped first), unless a handle to its values
+        // has been handed out.
+        for (size_t li = 0; li < p->launches.size(); ++li) {
+            const launch_spec& l = p->launches[li];
+            if (l.cache_slot < 0 || skip[li]) continue;
+            realized_storage& st = *g.slots[static_cast<size_t>(l.cache_slot)];
+            std::scoped_lock lock{st.view_mutex};
+            if (st.escaped || st.placeholder) continue;
+            if (st.splits.size() >= 4) st.splits.erase(st.splits.begin());
+            st.splits.push_back({l.cache_key, temps[static_cast<size_t>(l.cache_temps[0])],
+                                 temps[static_cast<size_t>(l.cache_temps[1])],
+                                 temps[static_cast<size_t>(l.cache_temps[2])]});
         }
         if (timing) t3 = now_ns();
 

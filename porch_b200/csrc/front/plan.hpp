@@ -80,6 +80,8 @@ namespace porch::detail {
         u64,        // immediate
         tmap,       // TMA tensor map (128 bytes) over a temp: `value` rows x
                     // `cols` fp32, box `box_rows` x `box_cols`, 128B swizzle
+        flag_clear, // temp `index` (an operand's non-finite flag) to clear, or
+                    // temp `value` when that operand's split is kept (below)
     };
 
     struct kernel_arg {
@@ -112,6 +114,14 @@ namespace porch::detail {
         // Thread-block cluster size along x (1: no cluster); grid[0] is a
         // multiple of it.
         uint32_t cluster_x = 1;
+        // A 3xTF32 operand split of input slot `cache_slot` (>= 0) that the
+        // slot's storage may keep under `cache_key`: when it holds one, the
+        // launch is skipped and temps cache_temps = {hi, lo, flag} are bound
+        // to the kept buffers; otherwise, after the launch, those temps are
+        // kept. Storage whose device handle was handed out is never kept.
+        int cache_slot = -1;
+        std::string cache_key;
+        std::array<int, 3> cache_temps{-1, -1, -1};
         // The kernel waits for the stream's previous kernel itself
         // (griddepcontrol.wait first thing), so it may launch with
         // programmatic stream serialization.

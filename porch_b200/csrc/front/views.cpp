@@ -171,6 +171,7 @@ namespace porch::detail {
         {
             std::scoped_lock lock{s->view_mutex};
             s->escaped = true;
+            s->splits.clear(); // the values may now be written
             for (auto& w : s->views)
                 if (auto v = w.lock()) live.push_back(std::move(v));
             s->views.clear();
