@@ -2,8 +2,8 @@
 
     python -m porch_b200.profile_case c3a_softmax --rows 16384 --steps 3
 
-Builds the named configuration's graph (porch_b200.api.config_graph) on
-seeded synthetic inputs whose leading dimension is cut to --rows (0 keeps
+Builds the named configuration's graph (porch_b200.api.config_graph), or
+one of the other kernel families' graphs below, on seeded synthetic inputs whose leading dimension is cut to --rows (0 keeps
 the benchmark's full shape), realises it --steps times on --device and
 synchronises. Nothing is timed here: under ncu the per-launch figures come
 from the profiler; without it the run only checks that the case exits 0.
@@ -32,15 +32,47 @@ ROW_INPUTS = {"c3a_softmax": {"x"}, "c3b_relu_logistic": {"x"}, "c4_matmul": {"a
 # and long-row softmax shapes (streaming two-pass; a cluster per row).
 REDUCTIONS = {"sum_axis0": ([262144, 256], 0), "sum_axis1": ([4096, 16384], 1)}
 SOFTMAX = {"softmax_long": [4096, 32768], "softmax_cluster": [64, 65536]}
+# Other kernel families: (input shapes, graph builder).
+#  gather:       a reshape of a transpose whose index map is not affine
+#                (pb_gather_*), 134 MB in and out;
+#  reduce_part:  a sum over the middle axis of [8192, 2048, 3] (rows of 3:
+#                no column tiles; pb_reduce_part_* + pb_reduce_comb_*);
+#  splitk:       [128, 4096] @ [4096, 4096] (16 tiles: split-K x8,
+#                pb_splitk_*);
+#  gemm_simt:    [512, 512] @ [512, 256] (below the tensor-core threshold,
+#                the CUDA-core GEMM);
+#  split:        [2048, 8192] @ [8192, 8192] (the 3xTF32 split passes
+#                pb_split_rows / pb_split_transpose; the GEMM itself too).
+GRAPHS = {
+    "gather": ([[8192, 4095]], lambda t: api.reshape(api.transpose(t[0]), [4095 * 8192])),
+    "reduce_part": ([[8192, 2048, 3]], lambda t: api.sum(t[0], 1)),
+    "splitk": ([[128, 4096], [4096, 4096]], lambda t: api.matmul(t[0], t[1])),
+    "gemm_simt": ([[512, 512], [512, 256]], lambda t: api.matmul(t[0], t[1])),
+    "split": ([[2048, 8192], [8192, 8192]], lambda t: api.matmul(t[0], t[1])),
+}
 
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("workload", choices=sorted(api.CONFIG_SHAPES) + sorted(REDUCTIONS) + sorted(SOFTMAX))
+    ap.add_argument("workload", choices=sorted(api.CONFIG_SHAPES) + sorted(REDUCTIONS) + sorted(SOFTMAX)
+                    + sorted(GRAPHS))
     ap.add_argument("--rows", type=int, default=0)
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--device", type=int, default=0)
     args = ap.parse_args()
+    if args.workload in GRAPHS:
+        shapes, build = GRAPHS[args.workload]
+        ts = []
+        for i, shape in enumerate(shapes):
+            arr = np.empty(int(np.prod(shape)), dtype=np.float32)
+            api.fill_synthetic(arr, 20261201 + i, "uniform", -1, 1)
+            t = api.tensor(shape, arr, device=args.device)
+            t.device_data()  # handed out: every realisation splits its GEMM operands again
+            ts.append(t)
+        outs = [api.materialize(build(ts)) for _ in range(max(1, args.steps))]
+        api.device_synchronize(args.device)
+        print(f"{args.workload}: {len(outs)} realisations of shape {outs[-1].shape()}")
+        return
     if args.workload in SOFTMAX:
         shape = list(SOFTMAX[args.workload])
         if args.rows:
