@@ -422,6 +422,14 @@ def measure(api, workload: str, args, rank, world, local, dist, cpu_seconds: flo
                     "how": "CUDA events around every launch over a second pass of the same K steps "
                            "(the timed region itself runs without them)",
                     "kernel_ms": round(per_launch_ms, 5)}
+        if launches == args.steps and k_launches == args.steps:
+            # One launch per step: the timed region is that kernel back to
+            # back on its stream, so its average launch duration there is
+            # the step time (each launch overlapping the previous one's tail
+            # through programmatic launch); `frac` keeps the isolated figure.
+            in_stream = work_rank / (ms_rank * 1e-3) / scale
+            roofline["kernel_ms_in_stream"] = round(ms_rank, 5)
+            roofline["frac_in_stream"] = round(in_stream / peak, 4)
         if bound == "tensor" and pk.get("bf16_tflops_sustained"):
             # Context: the same ceiling from the power-capped figure (bf16
             # GEMMs back to back for seconds); `frac` keeps the burst one.

@@ -278,8 +278,9 @@ namespace porch::detail {
 
     size_t checked_numel(std::span<const index_t> shape);
     std::vector<index_t> contiguous_strides(std::span<const index_t> shape);
-    // `ordinal` as a device index among `count` visible devices; throws
-    // std::invalid_argument when it is negative or not present.
+    // The GPU that device{ordinal} runs on among `count` visible devices:
+    // the ordinal itself when present, else device 0 (the reference's only
+    // device); a negative ordinal throws std::invalid_argument.
     int checked_ordinal(int ordinal, int count);
 
     // Lower, compile and launch `root`; the result is a realised tensor on the

@@ -80,11 +80,11 @@ namespace porch {
         int checked_ordinal(int ordinal, int count) {
             if (ordinal < 0)
                 throw std::invalid_argument("CUDA device ordinal must be non-negative");
-            if (ordinal >= count)
-                throw std::invalid_argument("CUDA device ordinal " + std::to_string(ordinal) +
-                                            " is not present (" + std::to_string(count) +
-                                            " visible devices)");
-            return ordinal;
+            // An ordinal with no GPU behind it keeps the reference's meaning
+            // (metadata; the work runs on device 0, src/cuda_jit.cpp:446-450):
+            // its own tests build device{1} tensors on one GPU. It never
+            // lands on another present GPU.
+            return ordinal < count ? ordinal : 0;
         }
 
         std::vector<index_t> contiguous_strides(std::span<const index_t> shape) {
@@ -323,7 +323,7 @@ namespace porch {
                 check(pbrt_device_count(&count));
                 // The reference treats the ordinal as metadata and always runs on
                 // device 0 (src/cuda_jit.cpp:446-450). Here ordinals address real
-                // devices, so one that is not present is an argument error.
+                // devices; one that is not present runs on device 0.
                 return checked_ordinal(placement.ordinal(), count);
             }
         } // namespace

@@ -269,16 +269,21 @@ def test_strided_axis_and_inner_softmax_match_oracle(gpu, case):
 
 
 @pytest.mark.gpu
-def test_device_ordinal_not_present_is_an_argument_error(gpu):
-    """device{n} addresses GPU n; an ordinal past the visible devices is an
-    std::invalid_argument (it used to wrap around to n % count)."""
+def test_device_ordinal_not_present_runs_on_device_zero(gpu):
+    """device{n} runs on GPU n when it is present. An ordinal with no GPU
+    behind it keeps the reference's meaning -- metadata, with the work on
+    device 0 (src/cuda_jit.cpp:446-450; its own test builds device{1}
+    tensors, tests/tensor_test.cpp:17-31) -- and never lands on another
+    present GPU (it used to wrap around to n % count)."""
     api = gpu
     count = api.device_count()
     values = np.arange(4, dtype=np.float32)
-    with pytest.raises(ValueError, match="is not present"):
-        api.tensor([4], values, device=count)
+    t = api.tensor([4], values, device=count + 7)
+    assert t.placement() == count + 7
+    assert_bitwise(api.materialize(t + 1.0).cpu(), values + 1.0, "absent ordinal")
+    with pytest.raises(ValueError, match="devices must match"):
+        api.materialize(t + api.tensor([4], values, device=0))
     with pytest.raises(ValueError, match="non-negative"):
         api.tensor([4], values, device=-1)
-    # The last present device still works.
-    t = api.tensor([4], values, device=count - 1)
-    assert_bitwise(api.materialize(t + 1.0).cpu(), values + 1.0, "last device")
+    last = api.tensor([4], values, device=count - 1)
+    assert_bitwise(api.materialize(last + 1.0).cpu(), values + 1.0, "last device")

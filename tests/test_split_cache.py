@@ -33,7 +33,7 @@ def _run(api, fn):
 
 
 def _splits(kernels):
-    return sum(n for k, n in kernels.items() if k.startswith("pb_split"))
+    return sum(n for k, n in kernels.items() if k.startswith(("pb_split_rows", "pb_split_transpose")))
 
 
 def test_weight_split_is_kept_until_its_handle_escapes(gpu):

@@ -110,8 +110,8 @@ def test_slab_allocator_serves_misses_without_driver_calls_and_releases(gpu):
     api.host_profile_enable(False)
     assert counters.get("alloc_cache_miss", 0) >= 40
     assert counters.get("slab_alloc", 0) <= 2, counters
-    for i, t in enumerate(held):
-        assert float(t.cpu()[0]) == 1.0 + i
+    for i in range(len(held)):
+        assert float(held[i].cpu().reshape(-1)[0]) == 1.0 + i
     held.clear()
     api.synchronize()
     api.empty_cache(0)

@@ -121,7 +121,7 @@ def test_noalloc_matmul_rejects_sizes_and_pointers_it_cannot_take(gpu):
     pb, _ = B.device_data()
     pc, _ = Cm.device_data()
     assert L.pb_matmul_3xtf32_noalloc(p2, pb, pc, 128, 256, 64, None) == 0, L.pb_last_error().decode()
-    assert np.array_equal(Cm.cpu(), np.full(128 * 256, 64.0, dtype=np.float32))
+    assert np.array_equal(Cm.cpu().reshape(-1), np.full(128 * 256, 64.0, dtype=np.float32))
 
 
 def test_noalloc_matmul_refuses_nonfinite_operands_and_recovers(gpu):
