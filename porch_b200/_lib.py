@@ -69,6 +69,7 @@ def _declare(L: ctypes.CDLL) -> None:
         "pb_expr_unsqueeze": (c_int, [T, c_size_t, P(T)]),
         "pb_expr_permute": (c_int, [T, P(c_int64), c_size_t, P(T)]),
         "pb_test_gemm_stall": (c_int, [c_int]),
+        "pb_expr_batched_matmul": (c_int, [T, T, P(T)]),
         "pb_expr_concat": (c_int, [T, T, c_size_t, P(T)]),
         "pb_expr_reduce": (c_int, [c_int, T, c_size_t, c_int, P(T)]),
         "pb_expr_softmax": (c_int, [T, c_size_t, P(T)]),

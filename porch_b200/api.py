@@ -439,6 +439,15 @@ def unsqueeze(a, axis: int) -> Expr:
     return Expr(out.value)
 
 
+def batched_matmul(a, b) -> Expr:
+    """[B, M, K] @ [B, K, N] -> [B, M, N]; an extension, the reference's
+    matmul is rank 2 only."""
+    ea, eb = _expr(a), _expr(b)
+    out = c_void_p()
+    _check(lib().pb_expr_batched_matmul(ea._h, eb._h, byref(out)))
+    return Expr(out.value)
+
+
 def permute(a, perm: Sequence[int]) -> Expr:
     """N-D axis permutation (output axis d = input axis perm[d]); an
     extension, the reference's transpose is rank 2 only."""

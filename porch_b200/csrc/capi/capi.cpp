@@ -351,6 +351,21 @@ int pb_test_gemm_stall(int enable) {
     return guarded([&] { porch::detail::set_test_gemm_stall(enable != 0); });
 }
 
+int pb_expr_batched_matmul(const pb_expr* lhs, const pb_expr* rhs, pb_expr** out) {
+    return guarded([&] {
+        require(lhs, "lhs");
+        require(rhs, "rhs");
+        require(out, "out");
+        auto n = std::make_shared<porch::tensor_expr::node>();
+        n->kind = porch::detail::expr_kind::batched_matmul;
+        n->lhs = porch::expr_access::root(lhs->value);
+        n->rhs = porch::expr_access::root(rhs->value);
+        porch::tensor_expr e = porch::expr_access::make(std::move(n));
+        (void)porch::detail::infer(*porch::expr_access::root(e));
+        *out = wrap(std::move(e));
+    });
+}
+
 int pb_expr_permute(const pb_expr* value, const int64_t* perm, size_t rank, pb_expr** out) {
     return guarded([&] {
         require(value, "value");

@@ -198,6 +198,9 @@ namespace porch::detail {
         // is rank 2 only, src/tensor.cpp:430-437); `shape` holds the
         // permutation, output dim d = input dim perm[d].
         permute,
+        // Internal batched matmul [B, M, K] @ [B, K, N] -> [B, M, N] (the
+        // reference's matmul is rank 2 only, src/tensor.cpp:366-381).
+        batched_matmul,
     };
 
     const char* kind_name(expr_kind kind);

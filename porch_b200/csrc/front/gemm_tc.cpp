@@ -200,7 +200,7 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
 
     int lowerer::emit_gemm_tc(int id, const box& b, kernel& k, const gemm_operand& A,
                               const gemm_operand& B, int64_t M, int64_t N, int64_t K, int* nonfinite,
-                              int* row_partials) {
+                              int* row_partials, int out_temp, int64_t out_off, gemm_temps* shared) {
         const bool softmax = row_partials != nullptr;
         (void)id;
         if (tensor_cores_disabled()) return -1;
@@ -217,19 +217,25 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
         // (zeros past K), so every row starts on a 128-byte line and the
         // TMA boxes (64-byte rows) never straddle one.
         const int64_t Kp = (K + 31) / 32 * 32;
-        const int a_hi = new_temp(static_cast<size_t>(M * Kp) * 4);
-        const int a_lo = new_temp(static_cast<size_t>(M * Kp) * 4);
-        const int b_hi = new_temp(static_cast<size_t>(N * Kp) * 4);
-        const int b_lo = new_temp(static_cast<size_t>(N * Kp) * 4);
-        const int out = new_temp(static_cast<size_t>(M * N) * 4);
+        gemm_temps own;
+        gemm_temps& tt = shared != nullptr ? *shared : own;
+        if (tt.a_hi < 0) {
+            tt.a_hi = new_temp(static_cast<size_t>(M * Kp) * 4);
+            tt.a_lo = new_temp(static_cast<size_t>(M * Kp) * 4);
+            tt.b_hi = new_temp(static_cast<size_t>(N * Kp) * 4);
+            tt.b_lo = new_temp(static_cast<size_t>(N * Kp) * 4);
+            tt.nf = new_temp(256);
+            tt.fa = new_temp(256);
+            tt.fb = new_temp(256);
+        }
+        const int a_hi = tt.a_hi, a_lo = tt.a_lo, b_hi = tt.b_hi, b_lo = tt.b_lo;
+        const int out = out_temp >= 0 ? out_temp : new_temp(static_cast<size_t>(M * N) * 4);
         // Set by the split kernels when an operand holds Inf or NaN; the
         // tensor-core kernels then leave the output to the CUDA-core GEMM
         // that follows them in the plan.
         // Each split flags its own operand (fa, fb: a kept split keeps its
         // flag); a one-thread merge then sets nf = fa | fb.
-        const int nf = new_temp(256);
-        const int fa = new_temp(256);
-        const int fb = new_temp(256);
+        const int nf = tt.nf, fa = tt.fa, fb = tt.fb;
         *nonfinite = nf;
         auto temp_arg = [](int t) {
             kernel_arg a;
@@ -331,7 +337,8 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
                 // A realised input: its storage may keep this split.
                 l.cache_slot = X.arg.index;
                 l.cache_key = "split R" + std::to_string(R) + " K" + std::to_string(K) + " Kp" + std::to_string(Kp) +
-                              " off" + std::to_string(X.off) + " sr" + std::to_string(sr) + " sk" + std::to_string(sk);
+                              " off" + std::to_string(X.off + X.arg.elem_offset) + " sr" + std::to_string(sr) +
+                              " sk" + std::to_string(sk);
                 l.cache_temps = {hi_t, lo_t, flag_t};
             }
             finish_kernel(l);
@@ -793,7 +800,9 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
         l.args = {tmap_arg(a_hi, M, kBM), tmap_arg(a_lo, M, kBM), tmap_arg(b_hi, N, kBN),
                   tmap_arg(b_lo, N, kBN)};
         for (const kernel_arg& a : k.leaves) l.args.push_back(a);
-        l.args.push_back(temp_arg(split > 1 ? part : out));
+        kernel_arg out_arg = temp_arg(out);
+        out_arg.elem_offset = out_off;
+        l.args.push_back(split > 1 ? temp_arg(part) : out_arg);
         if (softmax) l.args.push_back(temp_arg(stats));
         kernel_arg e;
         e.kind = arg_kind::error_word;
@@ -841,7 +850,7 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
             r.block = {256, 1, 1};
             r.args = k.leaves;
             r.args.push_back(temp_arg(part));
-            r.args.push_back(temp_arg(out));
+            r.args.push_back(out_arg);
             r.args.push_back(temp_arg(nf));
             finish_kernel(r);
             p_.launches.push_back(std::move(r));

@@ -204,6 +204,9 @@ namespace porch::detail {
                     case expr_kind::matmul:
                         n.shape = {a->shape[0], b->shape[1]};
                         return;
+                    case expr_kind::batched_matmul:
+                        n.shape = {a->shape[0], a->shape[1], b->shape[2]};
+                        return;
                     case expr_kind::slice:
                         n.shape = n.p_shape;
                         return;
@@ -533,12 +536,12 @@ namespace porch::detail {
                     case arg_kind::slot:
                         values[i] = cuda_jit::buffer_access::state(
                                         g.slots[static_cast<size_t>(a.index)]->device_values)
-                                        ->ptr;
+                                        ->ptr + static_cast<uint64_t>(a.elem_offset) * 4u;
                         break;
                     case arg_kind::temp:
                         values[i] = cuda_jit::buffer_access::state(
                                         temps[static_cast<size_t>(a.index)])
-                                        ->ptr;
+                                        ->ptr + static_cast<uint64_t>(a.elem_offset) * 4u;
                         break;
                     case arg_kind::error_word:
                         if (error_word == 0) check(pbrt_error_word(device, &error_word));

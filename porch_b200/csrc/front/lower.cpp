@@ -155,7 +155,7 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
 
     bool lowerer::is_barrier(int id) const {
         const gnode& n = g_.nodes[static_cast<size_t>(id)];
-        if (n.kind == expr_kind::matmul || n.kind == expr_kind::sum ||
+        if (n.kind == expr_kind::matmul || n.kind == expr_kind::batched_matmul || n.kind == expr_kind::sum ||
             n.kind == expr_kind::max)
             return true;
         // Only a softmax over the last axis has a kernel of its own; over
@@ -227,6 +227,8 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
             if (t < 0) t = emit_softmax(id, x);
         } else if (n.kind == expr_kind::sum || n.kind == expr_kind::max) {
             t = emit_reduce(id);
+        } else if (n.kind == expr_kind::batched_matmul) {
+            t = emit_batched_gemm(id);
         } else {
             const int mm = match_gemm(id);
             if (mm >= 0) t = emit_gemm(id, mm);
@@ -428,6 +430,7 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
                 break;
             }
             case expr_kind::matmul:
+            case expr_kind::batched_matmul:
             case expr_kind::sum:
             case expr_kind::max:
                 out = load_from(arg_kind::temp, materialize(id));
@@ -1094,6 +1097,7 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
             case expr_kind::input:
                 return "pb_ld(in" + std::to_string(k.leaf(arg_kind::slot, n.slot)) + " + (" + idx + "))";
             case expr_kind::matmul:
+            case expr_kind::batched_matmul:
             case expr_kind::sum:
             case expr_kind::max:
                 return "pb_ld(in" + std::to_string(k.leaf(arg_kind::temp, materialize(id))) + " + (" +
@@ -2172,6 +2176,51 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
         return emit_gemm_simt(boxes[0], k, A, B, M, N, K);
     }
 
+    int lowerer::emit_batched_gemm(int id) {
+        const gnode& n = g_.nodes[static_cast<size_t>(id)];
+        const int64_t Bt = n.shape[0], M = n.shape[1], N = n.shape[2];
+        const int64_t K = g_.nodes[static_cast<size_t>(n.a)].shape[2];
+        const kernel_arg A = as_buffer(n.a); // contiguous [Bt, M, K]
+        const kernel_arg B = as_buffer(n.b); // contiguous [Bt, K, N]
+        const int out = new_temp(static_cast<size_t>(Bt * M * N) * sizeof(float));
+        if (Bt == 0 || M == 0 || N == 0) return out;
+        rank_ = 2;
+        // The plain product as the epilogue: one box over [M, N] holding
+        // the accumulator.
+        box b;
+        b.lo = {0, 0};
+        b.hi = {M, N};
+        vnode acc;
+        acc.kind = vnode::op::acc;
+        b.nodes.push_back(acc);
+        b.root = 0;
+        kernel k;
+        auto at = [](const kernel_arg& base, int64_t off, int64_t s0) {
+            gemm_operand o;
+            o.arg = base;
+            o.arg.elem_offset = off;
+            o.s0 = s0;
+            o.s1 = 1;
+            return o;
+        };
+        // Tensor cores: one GEMM per batch, each reading its operands and
+        // writing its output block through pointer offsets, so every batch
+        // runs the same compiled kernels and reuses one set of split temps.
+        gemm_temps shared;
+        for (int64_t t = 0; t < Bt; ++t) {
+            const gemm_operand ga = at(A, t * M * K, K), gb = at(B, t * K * N, N);
+            int nonfinite = -1;
+            if (emit_gemm_tc(id, b, k, ga, gb, M, N, K, &nonfinite, nullptr, out, t * M * N, &shared) < 0) {
+                if (t != 0) throw std::logic_error("batched GEMM eligibility changed between batches");
+                // CUDA cores: every batch in one launch (blockIdx.y).
+                emit_gemm_simt(b, k, at(A, 0, K), at(B, 0, N), M, N, K, out, -1, 0, Bt);
+                return out;
+            }
+            emit_gemm_simt(b, k, ga, gb, M, N, K, out, nonfinite, t * M * N);
+        }
+        return out;
+    }
+
     int lowerer::emit_gemm_softmax(int id, int x, int mm) {
         (void)id;
         const gnode& m = g_.nodes[static_cast<size_t>(mm)];
@@ -2298,8 +2347,10 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
     }
 
     int lowerer::emit_gemm_simt(const box& b, kernel& k, const gemm_operand& A, const gemm_operand& B,
-                                int64_t M, int64_t N, int64_t K, int out_temp, int guard_temp) {
-        const int out = out_temp >= 0 ? out_temp : new_temp(static_cast<size_t>(M * N) * sizeof(float));
+                                int64_t M, int64_t N, int64_t K, int out_temp, int guard_temp, int64_t out_off,
+                                int64_t batches) {
+        const int out = out_temp >= 0 ? out_temp
+                                      : new_temp(static_cast<size_t>(batches * M * N) * sizeof(float));
         rank_ = 2;
         const bool wide = M * N >= (int64_t{1} << 31) - 4096 || M * K >= (int64_t{1} << 31) - 4096 ||
                           K * N >= (int64_t{1} << 31) - 4096 ||
@@ -2329,6 +2380,11 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
         // operand is finite it costs one short launch, not tiles' worth.
         const int64_t tiles_n = (N + 63) / 64, tiles = tiles_n * ((M + 63) / 64);
         if (guard_temp >= 0) body << "    if (*(const volatile int*)guard == 0) return;\n";
+        if (batches > 1)
+            // One matrix product per blockIdx.y over contiguous [M, K] and
+            // [K, N] operands and [M, N] outputs.
+            body << "    A += (pb_u64)blockIdx.y * " << M * K << "ull;\n    B += (pb_u64)blockIdx.y * " << K * N
+                 << "ull;\n    out += (pb_u64)blockIdx.y * " << M * N << "ull;\n";
         body << "    __shared__ float As[16][68];\n    __shared__ float Bs[16][68];\n";
         body << "    const pb_u32 tx = threadIdx.x & 15u, ty = threadIdx.x >> 4;\n";
         body << "    for (" << I << " tile = blockIdx.x; tile < " << lit(tiles, wide) << "; tile += gridDim.x) {\n";
@@ -2374,7 +2430,9 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
             << body.str() << "}\n";
         l.source = src.str();
         if (tiles > 0x7fffffff) throw std::invalid_argument("matmul output is too large for one launch");
-        l.grid = {static_cast<uint32_t>(guard_temp >= 0 ? std::min<int64_t>(tiles, 148 * 8) : tiles), 1, 1};
+        l.grid = {static_cast<uint32_t>(guard_temp >= 0 ? std::min<int64_t>(tiles, 148 * 8) : tiles),
+                  static_cast<uint32_t>(batches), 1};
+        if (batches > 65535) throw std::invalid_argument("batched matmul has too many batches for one launch");
         l.block = {256, 1, 1};
         l.schedule = "gemm CUDA-core 64x64x16 tiles, k-ordered FMA chain, fused epilogue";
         if (guard_temp >= 0) l.schedule += " (runs only for non-finite operands)";
@@ -2384,6 +2442,7 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
         kernel_arg o;
         o.kind = arg_kind::temp;
         o.index = out;
+        o.elem_offset = out_off;
         l.args.push_back(o);
         if (guard_temp >= 0) {
             kernel_arg gk;

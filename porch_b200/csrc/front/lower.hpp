@@ -61,6 +61,12 @@ namespace porch::detail {
 
     // A matmul operand [rows, cols] read in place: element (i, j) at
     // off + i * s0 + j * s1 of `arg` (an input slot, or a contiguous temp).
+    // Temps of one tensor-core GEMM's operand splits and flags, shared by
+    // the GEMMs of a batched matmul (they run one after another).
+    struct gemm_temps {
+        int a_hi = -1, a_lo = -1, b_hi = -1, b_lo = -1, nf = -1, fa = -1, fb = -1;
+    };
+
     struct gemm_operand {
         kernel_arg arg;
         int64_t off = 0;
@@ -128,8 +134,14 @@ namespace porch::detail {
         int emit_gemm(int id, int mm);
         // CUDA-core GEMM (fp32 FMA chain in k order). out_temp >= 0 writes
         // into that temp; guard_temp >= 0 runs only when its first int is set.
+        // out_off: the output starts out_off floats into out_temp; batches > 1:
+        // that many products over contiguous operands (blockIdx.y).
         int emit_gemm_simt(const box& b, kernel& k, const gemm_operand& A, const gemm_operand& B,
-                           int64_t M, int64_t N, int64_t K, int out_temp = -1, int guard_temp = -1);
+                           int64_t M, int64_t N, int64_t K, int out_temp = -1, int guard_temp = -1,
+                           int64_t out_off = 0, int64_t batches = 1);
+        // Internal batched matmul: a tensor-core GEMM per batch, or one
+        // CUDA-core launch over every batch.
+        int emit_batched_gemm(int id);
         // tcgen05 3xTF32 path; returns -1 when the shape is not eligible. On
         // success *nonfinite receives a temp whose first int is set when an
         // operand holds Inf or NaN (the tensor-core result is then skipped).
@@ -139,7 +151,8 @@ namespace porch::detail {
         // the tile's row maximum and its sum of exp(y - m).
         int emit_gemm_tc(int id, const box& b, kernel& k, const gemm_operand& A,
                          const gemm_operand& B, int64_t M, int64_t N, int64_t K, int* nonfinite,
-                         int* row_partials = nullptr);
+                         int* row_partials = nullptr, int out_temp = -1, int64_t out_off = 0,
+                         gemm_temps* shared = nullptr);
         // softmax(x, last axis) where x is an elementwise tree over one
         // rank-2 matmul `mm`: the GEMM's softmax epilogue plus a normalising
         // pass; -1 when the tensor-core GEMM does not apply.

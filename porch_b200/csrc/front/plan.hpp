@@ -88,6 +88,9 @@ namespace porch::detail {
         arg_kind kind = arg_kind::u64;
         int index = 0;
         uint64_t value = 0;
+        // slot / temp: the pointer passed is the buffer's + elem_offset floats
+        // (one batch of a batched matmul; the kernel source stays the same).
+        int64_t elem_offset = 0;
         int64_t cols = 0;
         int box_rows = 0;
         int box_cols = 0;

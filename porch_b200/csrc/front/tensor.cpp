@@ -63,6 +63,7 @@ namespace porch {
                 case expr_kind::exp: return "exp";
                 case expr_kind::reciprocal: return "reciprocal";
                 case expr_kind::permute: return "permute";
+                case expr_kind::batched_matmul: return "batched_matmul";
             }
             return "?";
         }
@@ -214,6 +215,19 @@ namespace porch {
                         if (l.shape[1] != r.shape[0])
                             throw std::invalid_argument("matmul inner dimensions must match");
                         return {{l.shape[0], r.shape[1]}, false};
+                    }
+                    case expr_kind::batched_matmul: {
+                        info l = infer_rec(*n.lhs, c);
+                        info r = infer_rec(*n.rhs, c);
+                        if (l.scalar || r.scalar)
+                            throw std::invalid_argument("batched matmul operands must be tensors");
+                        if (l.shape.size() != 3 || r.shape.size() != 3)
+                            throw std::invalid_argument("batched matmul requires rank-3 tensors");
+                        if (l.shape[0] != r.shape[0])
+                            throw std::invalid_argument("batched matmul batch dimensions must match");
+                        if (l.shape[2] != r.shape[1])
+                            throw std::invalid_argument("batched matmul inner dimensions must match");
+                        return {{l.shape[0], l.shape[1], r.shape[2]}, false};
                     }
                     case expr_kind::slice:
                         (void)infer_rec(*n.lhs, c);
