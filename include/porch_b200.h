@@ -81,6 +81,16 @@ int pb_synchronize(void);
  * so a later read copies from the device. */
 int pb_tensor_create(const int64_t* shape, size_t rank, const float* values,
                      size_t count, int device, pb_tensor** out);
+/* The same tensor with the host-to-device copy enqueued on this thread's
+ * upload stream and not waited for: the call returns at once, and every
+ * kernel or copy that later reads the tensor waits (on the device) for the
+ * copy, so an upload overlaps work that does not read it. `values` must stay
+ * unchanged and allocated until the copy is done (any read of the tensor, or
+ * pb_synchronize); page-locked memory (pb_host_alloc) makes it a DMA. No
+ * counterpart in the reference, whose copies are synchronous
+ * (src/cuda_jit.cpp:711-734). */
+int pb_tensor_create_async(const int64_t* shape, size_t rank, const float* values,
+                           size_t count, int device, pb_tensor** out);
 /* full(shape, value, device) (tensor.hpp:184-186) */
 int pb_tensor_full(const int64_t* shape, size_t rank, float value, int device,
                    pb_tensor** out);

@@ -44,6 +44,7 @@ def _declare(L: ctypes.CDLL) -> None:
         "pb_backend_name": (c_char_p, []),
         "pb_synchronize": (c_int, []),
         "pb_tensor_create": (c_int, [P(c_int64), c_size_t, P(c_float), c_size_t, c_int, P(T)]),
+        "pb_tensor_create_async": (c_int, [P(c_int64), c_size_t, P(c_float), c_size_t, c_int, P(T)]),
         "pb_tensor_full": (c_int, [P(c_int64), c_size_t, c_float, c_int, P(T)]),
         "pb_tensor_placeholder": (c_int, [P(c_int64), c_size_t, c_int, P(T)]),
         "pb_tensor_release": (None, [T]),

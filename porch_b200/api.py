@@ -329,12 +329,16 @@ def tensor(shape: Sequence[int], values, device: int = 0) -> Tensor:
     return Tensor(out.value)
 
 
-def tensor_from_pointer(shape: Sequence[int], pointer: int, count: int, device: int = 0) -> Tensor:
-    """tensor from `count` floats at host address `pointer` (e.g. pinned)."""
+def tensor_from_pointer(shape: Sequence[int], pointer: int, count: int, device: int = 0,
+                        asynchronous: bool = False) -> Tensor:
+    """tensor from `count` floats at host address `pointer` (e.g. pinned).
+    asynchronous=True enqueues the copy on this thread's upload stream and
+    returns at once (pb_tensor_create_async): readers wait for it on the
+    device, and the host memory must stay unchanged until it is done."""
     s, r = _shape_arg(shape)
     out = c_void_p()
-    _check(lib().pb_tensor_create(s, r, ctypes.cast(pointer, ctypes.POINTER(c_float)), count,
-                                  int(device), byref(out)))
+    fn = lib().pb_tensor_create_async if asynchronous else lib().pb_tensor_create
+    _check(fn(s, r, ctypes.cast(pointer, ctypes.POINTER(c_float)), count, int(device), byref(out)))
     return Tensor(out.value)
 
 

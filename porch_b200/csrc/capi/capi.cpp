@@ -115,6 +115,39 @@ int pb_tensor_create(const int64_t* shape, size_t rank, const float* values, siz
     });
 }
 
+int pb_tensor_create_async(const int64_t* shape, size_t rank, const float* values, size_t count,
+                           int device, pb_tensor** out) {
+    return guarded([&] {
+        require(out, "out");
+        auto s = shape_of(shape, rank);
+        const size_t expected = porch::detail::checked_numel(s);
+        if (count != expected)
+            throw std::invalid_argument("tensor data size does not match shape");
+        if (count != 0) require(values, "values");
+        int ndev = 0;
+        porch::detail::check(pbrt_device_count(&ndev));
+        auto storage = std::make_shared<porch::detail::realized_storage>();
+        storage->count = count;
+        storage->device = porch::detail::checked_ordinal(device, ndev);
+        // The block and its copy belong to the upload stream: the first
+        // kernel (or copy) that reads the tensor waits for it with an event.
+        auto stream = porch::detail::upload_stream(storage->device);
+        storage->device_values =
+            porch::detail::allocate(storage->device, count * sizeof(float), stream);
+        if (count != 0) {
+            const auto& st = porch::cuda_jit::buffer_access::state(storage->device_values);
+            porch::detail::check(pbrt_memcpy_h2d_async(storage->device, st->ptr, values,
+                                                       count * sizeof(float), stream->stream));
+            pbrt_event e = nullptr;
+            porch::detail::check(pbrt_event_create(storage->device, 0, &e));
+            st->ready = e;
+            porch::detail::check(pbrt_event_record(storage->device, e, stream->stream));
+        }
+        *out = wrap(porch::tensor_access::from_storage(std::move(s), std::move(storage),
+                                                       porch::device{device}));
+    });
+}
+
 int pb_tensor_full(const int64_t* shape, size_t rank, float value, int device,
                    pb_tensor** out) {
     return guarded([&] {

@@ -41,6 +41,9 @@ namespace porch::detail {
     std::shared_ptr<stream_ref> current_stream(int device);
     // Streams the calling thread has created so far.
     std::vector<std::shared_ptr<stream_ref>> thread_streams();
+    // The calling thread's host-to-device upload stream on `device`
+    // (pb_tensor_create_async); readers order behind it with events.
+    std::shared_ptr<stream_ref> upload_stream(int device);
 
     // ------------------------------------------------------- dry run --
     // True while a plan is being inspected without a device (placeholder
@@ -59,6 +62,10 @@ namespace porch::cuda_jit {
         std::mutex mutex;
         std::shared_ptr<detail::stream_ref> producer;
         std::vector<std::shared_ptr<detail::stream_ref>> readers;
+        // Set for an asynchronous upload: recorded on the producer stream
+        // right after the copy; readers wait on it rather than on
+        // everything the producer stream holds.
+        pbrt_event ready = nullptr;
 
         device_buffer_state() = default;
         device_buffer_state(const device_buffer_state&) = delete;

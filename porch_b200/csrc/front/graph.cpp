@@ -452,7 +452,9 @@ namespace porch::detail {
                 throw std::invalid_argument(empty_input_message(g, static_cast<int>(si)));
             if (st->device != device)
                 throw std::invalid_argument("tensor expression devices must match");
-            order_read(*st, stream);
+            // Ordered behind its producer at its first launch (below), so a
+            // launch waits only for the inputs it reads: an input still
+            // uploading on another stream holds back only its readers.
         }
         if (timing) tb = now_ns();
 
@@ -499,6 +501,7 @@ namespace porch::detail {
         };
         tensor_map_storage maps[8];
         int nmaps = 0;
+        std::vector<char> slot_ordered(g.slots.size(), 0);
         for (size_t li = 0; li < p->launches.size(); ++li) {
             if (skip[li]) continue;
             launch_spec& l = p->launches[li];
@@ -534,6 +537,12 @@ namespace porch::detail {
                 const kernel_arg& a = l.args[i];
                 switch (a.kind) {
                     case arg_kind::slot:
+                        if (!slot_ordered[static_cast<size_t>(a.index)]) {
+                            slot_ordered[static_cast<size_t>(a.index)] = 1;
+                            order_read(*cuda_jit::buffer_access::state(
+                                           g.slots[static_cast<size_t>(a.index)]->device_values),
+                                       stream);
+                        }
                         values[i] = cuda_jit::buffer_access::state(
                                         g.slots[static_cast<size_t>(a.index)]->device_values)
                                         ->ptr + static_cast<uint64_t>(a.elem_offset) * 4u;
@@ -586,6 +595,11 @@ namespace porch::detail {
                                  params.data(), l.cluster_x > 1 ? cluster : nullptr,
                                  l.pdl ? PBRT_LAUNCH_PDL : 0u));
         }
+        // A slot whose every read was served by kept splits still joins the
+        // stream's readers, so its eventual free is ordered after this work.
+        for (size_t si = 0; si < g.slots.size(); ++si)
+            if (!slot_ordered[si] && !p->launches.empty())
+                order_read(*cuda_jit::buffer_access::state(g.slots[si]->device_values), stream);
         // Splits computed now are kept by their input's storage (a few per
         // storage, the oldest dropped first), unless a handle to its values
         // has been handed out.

@@ -43,7 +43,25 @@ namespace porch::detail {
             std::vector<std::shared_ptr<stream_ref>> streams;
         };
         thread_local thread_stream_table tl_streams;
+        thread_local thread_stream_table tl_upload_streams;
+
+        std::shared_ptr<stream_ref> stream_in(thread_stream_table& t, int device) {
+            auto& table = t.streams;
+            if (device < 0)
+                throw std::invalid_argument("CUDA device ordinal must be non-negative");
+            if (table.size() <= static_cast<size_t>(device))
+                table.resize(static_cast<size_t>(device) + 1);
+            std::shared_ptr<stream_ref>& slot = table[static_cast<size_t>(device)];
+            if (slot == nullptr) {
+                pbrt_stream s = nullptr;
+                check(pbrt_stream_create(device, &s));
+                slot = std::make_shared<stream_ref>(device, s);
+            }
+            return slot;
+        }
     } // namespace
+
+    std::shared_ptr<stream_ref> upload_stream(int device) { return stream_in(tl_upload_streams, device); }
 
     std::shared_ptr<stream_ref> current_stream(int device) {
         auto& table = tl_streams.streams;
@@ -63,6 +81,8 @@ namespace porch::detail {
     std::vector<std::shared_ptr<stream_ref>> thread_streams() {
         std::vector<std::shared_ptr<stream_ref>> out;
         for (const auto& s : tl_streams.streams)
+            if (s != nullptr) out.push_back(s);
+        for (const auto& s : tl_upload_streams.streams)
             if (s != nullptr) out.push_back(s);
         return out;
     }
@@ -310,7 +330,11 @@ namespace porch::detail {
             for (const auto& r : buffer.readers) known = known || r == stream;
             if (!known) buffer.readers.push_back(stream);
         }
-        if (producer->device == stream->device) {
+        if (producer->device == stream->device && buffer.ready != nullptr) {
+            // Recorded right after the buffer's own upload: later work on the
+            // producer stream (other uploads) is not waited for.
+            check(pbrt_stream_wait_event(stream->device, stream->stream, buffer.ready));
+        } else if (producer->device == stream->device) {
             pbrt_event e = nullptr;
             check(pbrt_event_create(producer->device, 0, &e));
             check(pbrt_event_record(producer->device, e, producer->stream));
@@ -335,6 +359,7 @@ namespace porch::detail {
 namespace porch::cuda_jit {
 
     device_buffer_state::~device_buffer_state() {
+        if (ready != nullptr) (void)pbrt_event_destroy(device, ready);
         if (ptr == 0) return;
         try {
             std::shared_ptr<detail::stream_ref> free_stream =

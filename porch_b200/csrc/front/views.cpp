@@ -167,6 +167,10 @@ namespace porch::detail {
 
     void escape(const std::shared_ptr<realized_storage>& s) {
         make_contiguous(s);
+        // A raw handle carries no stream order: an upload still in flight
+        // (pb_tensor_create_async) completes first.
+        if (const auto& st = cuda_jit::buffer_access::state(s->device_values); st && st->ready != nullptr)
+            check(pbrt_event_synchronize(st->device, st->ready));
         std::vector<std::shared_ptr<realized_storage>> live;
         {
             std::scoped_lock lock{s->view_mutex};

@@ -116,3 +116,26 @@ def test_slab_allocator_serves_misses_without_driver_calls_and_releases(gpu):
     api.synchronize()
     api.empty_cache(0)
     assert free_bytes() >= base - (64 << 20)
+
+
+@pytest.mark.gpu
+def test_async_uploads_order_each_reader_behind_its_own_copy(gpu):
+    """pb_tensor_create_async returns before its copy is done; every reader
+    (a kernel, a host read, a handed-out pointer) waits for that tensor's own
+    copy. Five uploads, then graphs reading them in another order."""
+    api = gpu
+    rng = np.random.default_rng(3)
+    arrays = [rng.integers(-8, 9, 1 << 22).astype(np.float32) for _ in range(5)]
+    pinned = [api.PinnedBuffer(a.size) for a in arrays]
+    for pb, a in zip(pinned, arrays):
+        pb.array[:] = a
+    for _ in range(3):
+        ts = [api.tensor_from_pointer([a.size], pb.address, a.size, asynchronous=True)
+              for a, pb in zip(arrays, pinned)]
+        got = api.materialize((ts[4] - ts[0]) * 2.0 + ts[2]).cpu()
+        assert np.array_equal(got, (arrays[4] - arrays[0]) * np.float32(2) + arrays[2])
+        assert np.array_equal(ts[1].cpu(), arrays[1])
+        ptr, nbytes = ts[3].device_data()
+        assert ptr != 0 and nbytes == arrays[3].size * 4
+        assert np.array_equal(ts[3].cpu(), arrays[3])
+    api.synchronize()
