@@ -529,6 +529,9 @@ namespace porch::detail {
                 }
             }
             if (l.args.size() > kMaxArgs) throw std::runtime_error("kernel has too many arguments");
+            // Parameters are copied at launch: the tensor-map scratch serves
+            // each launch afresh.
+            nmaps = 0;
             if (values.size() < l.args.size()) {
                 values.resize(l.args.size());
                 params.resize(l.args.size());
@@ -566,7 +569,7 @@ namespace porch::detail {
                         break;
                     }
                     case arg_kind::tmap: {
-                        if (nmaps >= 8) throw std::runtime_error("too many tensor maps");
+                        if (nmaps >= 8) throw std::runtime_error("a kernel has more than 8 tensor maps");
                         const uint64_t base =
                             cuda_jit::buffer_access::state(temps[static_cast<size_t>(a.index)])->ptr;
                         const uint64_t dims[2] = {static_cast<uint64_t>(a.cols), a.value};
