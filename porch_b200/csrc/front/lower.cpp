@@ -229,6 +229,12 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
             t = emit_reduce(id);
         } else if (n.kind == expr_kind::batched_matmul) {
             t = emit_batched_gemm(id);
+        } else if ((n.kind == expr_kind::reshape || n.kind == expr_kind::unsqueeze) &&
+                   g_.nodes[static_cast<size_t>(n.a)].kind != expr_kind::input) {
+            // A contiguous result holds the same bytes under any shape:
+            // realise the operand under its own shape (its schedules see
+            // no carries), and read that buffer as this node.
+            t = materialize(n.a);
         } else {
             const int mm = match_gemm(id);
             if (mm >= 0) t = emit_gemm(id, mm);

@@ -33,8 +33,8 @@ ROW_INPUTS = {"c3a_softmax": {"x"}, "c3b_relu_logistic": {"x"}, "c4_matmul": {"a
 REDUCTIONS = {"sum_axis0": ([262144, 256], 0), "sum_axis1": ([4096, 16384], 1)}
 SOFTMAX = {"softmax_long": [4096, 32768], "softmax_cluster": [64, 65536]}
 # Other kernel families: (input shapes, graph builder).
-#  gather:       a reshape of a transpose whose index map is not affine
-#                (pb_gather_*), 134 MB in and out;
+#  gather:       a reshape of a transpose, inside a sum, whose index map is
+#                not affine (pb_gather_*), 268 MB in, 134 MB out;
 #  reduce_part:  a sum over the middle axis of [8192, 2048, 3] (rows of 3:
 #                no column tiles; pb_reduce_part_* + pb_reduce_comb_*);
 #  splitk:       [128, 4096] @ [4096, 4096] (16 tiles: split-K x8,
@@ -44,7 +44,8 @@ SOFTMAX = {"softmax_long": [4096, 32768], "softmax_cluster": [64, 65536]}
 #  split:        [2048, 8192] @ [8192, 8192] (the 3xTF32 split passes
 #                pb_split_rows / pb_split_transpose; the GEMM itself too).
 GRAPHS = {
-    "gather": ([[8192, 4095]], lambda t: api.reshape(api.transpose(t[0]), [4095 * 8192])),
+    "gather": ([[8192, 4095], [4095 * 8192]],
+               lambda t: api.reshape(api.transpose(t[0]), [4095 * 8192]) + t[1]),
     "reduce_part": ([[8192, 2048, 3]], lambda t: api.sum(t[0], 1)),
     "splitk": ([[128, 4096], [4096, 4096]], lambda t: api.matmul(t[0], t[1])),
     "gemm_simt": ([[512, 512], [512, 256]], lambda t: api.matmul(t[0], t[1])),
