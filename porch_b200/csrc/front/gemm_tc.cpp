@@ -195,15 +195,22 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
 
     } // namespace
 
+    bool tensor_core_gemm(int64_t M, int64_t N, int64_t K) {
+        return !tensor_cores_disabled() && M >= 1 && N >= 1 && K >= 1 && M * N * K >= (int64_t{1} << 27) &&
+               M <= (int64_t{1} << 30) && N <= (int64_t{1} << 30) && K <= (int64_t{1} << 30);
+    }
+
     void set_test_gemm_stall(bool on) { g_test_stall.store(on); }
     bool test_gemm_stall() { return g_test_stall.load(); }
 
     int lowerer::emit_gemm_tc(int id, const box& b, kernel& k, const gemm_operand& A,
                               const gemm_operand& B, int64_t M, int64_t N, int64_t K, int* nonfinite,
-                              int* row_partials, int out_temp, int64_t out_off, gemm_temps* shared) {
+                              int* row_partials, int out_temp, int64_t out_off, gemm_temps* shared,
+                              const split_output* so) {
         const bool softmax = row_partials != nullptr;
+        if (so != nullptr && (softmax || N % 32 != 0 || so->kp != N)) return -1;
         (void)id;
-        if (tensor_cores_disabled()) return -1;
+        if (!tensor_core_gemm(M, N, K)) return -1;
         // Any M, N, K. The K-major hi/lo arrays have padded rows (16-byte
         // TMA strides whatever K is); edge tiles read zeros past M, N and K
         // (TMA out-of-bounds fill) and mask their stores; when N is not a
@@ -219,17 +226,18 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
         const int64_t Kp = (K + 31) / 32 * 32;
         gemm_temps own;
         gemm_temps& tt = shared != nullptr ? *shared : own;
-        if (tt.a_hi < 0) {
-            tt.a_hi = new_temp(static_cast<size_t>(M * Kp) * 4);
-            tt.a_lo = new_temp(static_cast<size_t>(M * Kp) * 4);
-            tt.b_hi = new_temp(static_cast<size_t>(N * Kp) * 4);
-            tt.b_lo = new_temp(static_cast<size_t>(N * Kp) * 4);
-            tt.nf = new_temp(256);
-            tt.fa = new_temp(256);
-            tt.fb = new_temp(256);
-        }
+        auto need = [&](int& t, size_t bytes) {
+            if (t < 0) t = new_temp(bytes);
+        };
+        need(tt.a_hi, static_cast<size_t>(M * Kp) * 4);
+        need(tt.a_lo, static_cast<size_t>(M * Kp) * 4);
+        need(tt.b_hi, static_cast<size_t>(N * Kp) * 4);
+        need(tt.b_lo, static_cast<size_t>(N * Kp) * 4);
+        need(tt.nf, 256);
+        need(tt.fa, 256);
+        need(tt.fb, 256);
         const int a_hi = tt.a_hi, a_lo = tt.a_lo, b_hi = tt.b_hi, b_lo = tt.b_lo;
-        const int out = out_temp >= 0 ? out_temp : new_temp(static_cast<size_t>(M * N) * 4);
+        const int out = so != nullptr ? so->hi : out_temp >= 0 ? out_temp : new_temp(static_cast<size_t>(M * N) * 4);
         // Set by the split kernels when an operand holds Inf or NaN; the
         // tensor-core kernels then leave the output to the CUDA-core GEMM
         // that follows them in the plan.
@@ -253,7 +261,7 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
             l.block = {1, 1, 1};
             kernel_arg ca, cb;
             ca.kind = cb.kind = arg_kind::flag_clear;
-            ca.index = fa;
+            ca.index = tt.a_ready ? nf : fa; // a flag set by A's producer is not cleared
             cb.index = fb;
             ca.value = cb.value = static_cast<uint64_t>(nf); // harmless stand-in for a kept flag
             l.args = {ca, cb};
@@ -344,7 +352,7 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
             finish_kernel(l);
             p_.launches.push_back(std::move(l));
         };
-        emit_split("A", A, M, A.s0, A.s1, a_hi, a_lo, fa);
+        if (!tt.a_ready) emit_split("A", A, M, A.s0, A.s1, a_hi, a_lo, fa);
         emit_split("B", B, N, B.s1, B.s0, b_hi, b_lo, fb);
         {
             launch_spec l;
@@ -389,7 +397,7 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
         // a part-filled last wave runs at a higher clock.
         const int64_t tiles = tiles_m * tiles_n;
         int64_t split = 1;
-        if (tiles < 74 && !softmax) {
+        if (tiles < 74 && !softmax && so == nullptr) {
             double best = static_cast<double>(tiles) / 148.0;
             for (int64_t s = 2; s <= 16; s *= 2) {
                 if (raw_kb / s < 16) break;
@@ -710,6 +718,37 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
                     "acc[c * 32 + j + 2], acc[c * 32 + j + 3]));\n"
                  << "            }\n"
                  << "            }\n";
+        } else if (so != nullptr) {
+            // Split output: the result as the next GEMM's A operand halves,
+            // hi = rn_tf32(y) and lo = rn_tf32(y - hi) in rows of N = Kp
+            // floats; an Inf or NaN result sets the flag and gets lo = 0.
+            body << "            if (rr < " << M << "ull) {\n";
+            emit_hoisted(body, "            ");
+            body << "            bool bad = false;\n"
+                 << "            #pragma unroll\n"
+                 << "            for (int c = 0; c < PB_BN / 64; ++c) {\n"
+                 << "                const int cbase = n0 + (int)half * (PB_BN / 2) + c * 32;\n"
+                 << "                float* hrow = out + rr * " << N << "ull + cbase;\n"
+                 << "                float* lrow = lo_out + rr * " << N << "ull + cbase;\n"
+                 << "                #pragma unroll\n"
+                 << "                for (int j = 0; j < 32; j += 4) {\n"
+                 << "                    const pb_u64 cc = (pb_u64)(cbase + j);\n"
+                 << "                    if (cc >= " << N << "ull) continue;\n";
+            emit_epilogue4(body, "                    ", "acc[c * 32 + j + e]");
+            body << "                    float h[4], l[4];\n"
+                 << "                    #pragma unroll\n"
+                 << "                    for (int e = 0; e < 4; ++e) {\n"
+                 << "                        const bool fin = isfinite(y[e]);\n"
+                 << "                        bad = bad || !fin;\n"
+                 << "                        h[e] = pb_tf32_hi(y[e]);\n"
+                 << "                        l[e] = fin ? pb_tf32_rn(y[e] - h[e]) : 0.0f;\n"
+                 << "                    }\n"
+                 << "                    pb_st4(hrow + j, make_float4(h[0], h[1], h[2], h[3]));\n"
+                 << "                    pb_st4(lrow + j, make_float4(l[0], l[1], l[2], l[3]));\n"
+                 << "                }\n"
+                 << "            }\n"
+                 << "            if (bad) atomicOr(split_flag, 1);\n"
+                 << "            }\n";
         } else {
             // Rows past M and columns past N (edge tiles) are neither read
             // (leaves) nor written.
@@ -764,6 +803,7 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
                "const __grid_constant__ pb_tmap tm_bhi, const __grid_constant__ pb_tmap tm_blo, ";
         for (size_t i = 0; i < k.leaves.size(); ++i) src << "const float* __restrict__ in" << i << ", ";
         src << "float* __restrict__ out, " << (softmax ? "float2* __restrict__ stats, " : "")
+            << (so != nullptr ? "float* __restrict__ lo_out, int* __restrict__ split_flag, " : "")
             << "int* __restrict__ err, const int* __restrict__ nf) {\n" << body.str() << "}\n";
         l.source = src.str();
         l.schedule = "gemm tcgen05 3xTF32 128x256x16, 4-stage TMA ring (64B swizzle, no multicast), "
@@ -804,6 +844,11 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
         out_arg.elem_offset = out_off;
         l.args.push_back(split > 1 ? temp_arg(part) : out_arg);
         if (softmax) l.args.push_back(temp_arg(stats));
+        if (so != nullptr) {
+            l.args.push_back(temp_arg(so->lo));
+            l.args.push_back(temp_arg(so->flag));
+            l.schedule += ", split-output epilogue (the next GEMM's A operand halves)";
+        }
         kernel_arg e;
         e.kind = arg_kind::error_word;
         l.args.push_back(e);

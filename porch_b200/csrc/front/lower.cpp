@@ -2167,10 +2167,15 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
             return -1;
         }
         if (boxes.size() != 1) return -1;
-        const gemm_operand A = as_gemm_operand(m.a);
+        // A produced by a GEMM that nothing else reads arrives as 3xTF32
+        // halves from that GEMM's epilogue: no split pass, no fp32 copy.
+        gemm_temps shared;
+        gemm_operand A;
+        if (!presplit_operand(m.a, M, N, K, shared, A)) A = as_gemm_operand(m.a);
         const gemm_operand B = as_gemm_operand(m.b);
         int nonfinite = -1;
-        if (const int t = emit_gemm_tc(id, boxes[0], k, A, B, M, N, K, &nonfinite); t >= 0) {
+        if (const int t = emit_gemm_tc(id, boxes[0], k, A, B, M, N, K, &nonfinite, nullptr, -1, 0, &shared);
+            t >= 0) {
             // Inf or NaN in an operand: the 3xTF32 expansion turns inf * 0
             // (an inf hi times a zero lo) into NaN where the reference's fp32
             // chain gives +-inf, so that case reruns on the CUDA cores with
@@ -2180,6 +2185,68 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
             return t;
         }
         return emit_gemm_simt(boxes[0], k, A, B, M, N, K);
+    }
+
+    bool lowerer::presplit_operand(int a, int64_t M, int64_t N, int64_t K, gemm_temps& t, gemm_operand& op) {
+        const gnode& h = g_.nodes[static_cast<size_t>(a)];
+        if (a == g_.root || h.kind == expr_kind::input || g_.uses[static_cast<size_t>(a)] != 1 ||
+            done_.count(a) != 0)
+            return false;
+        if (K % 32 != 0 || !tensor_core_gemm(M, N, K)) return false;
+        const int mh = match_gemm(a);
+        if (mh < 0) return false;
+        const gnode& hm = g_.nodes[static_cast<size_t>(mh)];
+        const int64_t Kh = g_.nodes[static_cast<size_t>(hm.a)].shape[1];
+        if (hm.shape[0] != M || hm.shape[1] != K || !tensor_core_gemm(M, K, Kh)) return false;
+        kernel kh;
+        std::vector<box> boxes;
+        try {
+            boxes = build_boxes(kh, a, h.shape, mh);
+        } catch (const not_fusable&) {
+            return false;
+        } catch (const not_affine&) {
+            return false;
+        }
+        if (boxes.size() != 1) return false;
+        auto temp = [](int i) {
+            kernel_arg x;
+            x.kind = arg_kind::temp;
+            x.index = i;
+            return x;
+        };
+        // The consumer's A halves and flag; the flag is cleared before the
+        // producer runs (the consumer's own clear then leaves it alone).
+        t.a_hi = new_temp(static_cast<size_t>(M * K) * 4);
+        t.a_lo = new_temp(static_cast<size_t>(M * K) * 4);
+        t.fa = new_temp(256);
+        {
+            launch_spec l;
+            l.name = "pb_flag_clear";
+            l.source = std::string(kernel_prelude()) +
+                       "extern \"C\" __global__ void pb_flag_clear(int* f) { f[0] = 0; }\n";
+            l.schedule = "clear the next GEMM's operand flag (its A comes from a split-output epilogue)";
+            l.grid = {1, 1, 1};
+            l.block = {1, 1, 1};
+            l.args = {temp(t.fa)};
+            finish_kernel(l);
+            p_.launches.push_back(std::move(l));
+        }
+        const split_output so{t.a_hi, t.a_lo, t.fa, K};
+        const gemm_operand Ah = as_gemm_operand(hm.a);
+        const gemm_operand Bh = as_gemm_operand(hm.b);
+        int nfh = -1;
+        if (emit_gemm_tc(a, boxes[0], kh, Ah, Bh, M, K, Kh, &nfh, nullptr, -1, 0, nullptr, &so) < 0)
+            throw std::logic_error("split-output GEMM was not eligible");
+        emit_gemm_simt(boxes[0], kh, Ah, Bh, M, K, Kh, -1, nfh, 0, 1, &so);
+        t.a_ready = true;
+        op = gemm_operand{};
+        op.arg = temp(t.a_hi);
+        op.s0 = K;
+        op.s1 = 1;
+        op.has_lo = true;
+        op.lo = temp(t.a_lo);
+        done_[a] = -1; // its only reader takes the halves
+        return true;
     }
 
     int lowerer::emit_batched_gemm(int id) {
@@ -2246,11 +2313,14 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
             return -1;
         }
         if (boxes.size() != 1) return -1;
-        const gemm_operand A = as_gemm_operand(m.a);
+        if (!tensor_core_gemm(M, N, K)) return -1;
+        gemm_temps shared;
+        gemm_operand A;
+        if (!presplit_operand(m.a, M, N, K, shared, A)) A = as_gemm_operand(m.a);
         const gemm_operand B = as_gemm_operand(m.b);
         int nonfinite = -1, stats = -1;
-        const int out = emit_gemm_tc(x, boxes[0], k, A, B, M, N, K, &nonfinite, &stats);
-        if (out < 0) return -1;
+        const int out = emit_gemm_tc(x, boxes[0], k, A, B, M, N, K, &nonfinite, &stats, -1, 0, &shared);
+        if (out < 0) throw std::logic_error("softmax GEMM was not eligible");
         auto temp = [](int t) {
             kernel_arg a;
             a.kind = arg_kind::temp;
@@ -2354,9 +2424,10 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
 
     int lowerer::emit_gemm_simt(const box& b, kernel& k, const gemm_operand& A, const gemm_operand& B,
                                 int64_t M, int64_t N, int64_t K, int out_temp, int guard_temp, int64_t out_off,
-                                int64_t batches) {
-        const int out = out_temp >= 0 ? out_temp
-                                      : new_temp(static_cast<size_t>(batches * M * N) * sizeof(float));
+                                int64_t batches, const split_output* so) {
+        const int out = so != nullptr ? so->hi
+                        : out_temp >= 0 ? out_temp
+                                        : new_temp(static_cast<size_t>(batches * M * N) * sizeof(float));
         rank_ = 2;
         const bool wide = M * N >= (int64_t{1} << 31) - 4096 || M * K >= (int64_t{1} << 31) - 4096 ||
                           K * N >= (int64_t{1} << 31) - 4096 ||
@@ -2368,6 +2439,12 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
             if (A.contiguous(K)) return "A + (" + r + ") * " + lit(K, wide) + " + " + c;
             return "A + " + lit(A.off, wide) + " + (" + r + ") * " + lit(A.s0, wide) + " + (" + c + ") * " +
                    lit(A.s1, wide);
+        };
+        // A held as 3xTF32 halves: its value is hi + lo at the same place.
+        auto a_val = [&](const std::string& r, const std::string& c) {
+            const std::string at = a_at(r, c);
+            if (!A.has_lo) return "pb_ld(" + at + ")";
+            return "(pb_ld(" + at + ") + pb_ld(Alo" + at.substr(1) + "))";
         };
         auto b_at = [&](const std::string& r, const std::string& c) {
             if (B.contiguous(N)) return "B + (" + r + ") * " + lit(N, wide) + " + " + c;
@@ -2403,7 +2480,7 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
         body << "            const pb_u32 f = threadIdx.x + 256u * u;\n";
         body << "            const pb_u32 ar = f >> 4, ak = f & 15u;\n";
         body << "            As[ak][ar] = (row0 + ar < " << lit(M, wide) << " && k0 + ak < " << lit(K, wide)
-             << ") ? pb_ld(" << a_at("row0 + ar", "k0 + ak") << ") : 0.0f;\n";
+             << ") ? " << a_val("row0 + ar", "k0 + ak") << " : 0.0f;\n";
         body << "            const pb_u32 bk = f >> 6, bc = f & 63u;\n";
         body << "            Bs[bk][bc] = (k0 + bk < " << lit(K, wide) << " && col0 + bc < " << lit(N, wide)
              << ") ? pb_ld(" << b_at("k0 + bk", "col0 + bc") << ") : 0.0f;\n";
@@ -2423,17 +2500,36 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
             body << "                const float x" << li << " = pb_ld(in" << v.buffer << " + " << address(v.map, cvar, wide, -1)
                  << ");\n";
         }
-        body << "                out[r * " << lit(N, wide) << " + c] = pb_e0(acc[i][j]";
+        body << "                const float y = pb_e0(acc[i][j]";
         for (size_t li = 0; li < order.size(); ++li) body << ", x" << li;
-        body << ");\n            }\n        }\n";
+        body << ");\n";
+        if (so != nullptr)
+            // Split output (see split_output): hi, lo and the Inf/NaN flag.
+            body << "                const float h = pb_tf32_hi_s(y);\n"
+                 << "                out[r * " << lit(N, wide) << " + c] = h;\n"
+                 << "                lo_out[r * " << lit(N, wide) << " + c] = isfinite(y) ? pb_tf32_rn_s(y - h) : 0.0f;\n"
+                 << "                if (!isfinite(y)) atomicOr(split_flag, 1);\n";
+        else
+            body << "                out[r * " << lit(N, wide) << " + c] = y;\n";
+        body << "            }\n        }\n";
         body << "    __syncthreads();  // shared tiles are reused by the next output tile\n    }\n";
         launch_spec l;
         l.name = "pb_gemm_simt_" + hex64(hash_string(src.str() + body.str())).substr(0, 8);
+        if (so != nullptr)
+            // Round to nearest TF32 (hi truncated where rounding would
+            // overflow), as the split passes do.
+            src << "static __device__ __forceinline__ float pb_tf32_rn_s(float x) {\n"
+                   "    unsigned r;\n    asm(\"cvt.rna.tf32.f32 %0, %1;\" : \"=r\"(r) : \"f\"(x));\n"
+                   "    return __uint_as_float(r);\n}\n"
+                   "static __device__ __forceinline__ float pb_tf32_hi_s(float x) {\n"
+                   "    const float r = pb_tf32_rn_s(x);\n"
+                   "    return isinf(r) && !isinf(x) ? __uint_as_float(__float_as_uint(x) & 0xFFFFE000u) : r;\n}\n";
         src << "extern \"C\" __global__ void __launch_bounds__(256) " << l.name
-            << "(const float* __restrict__ A, const float* __restrict__ B, ";
+            << "(const float* __restrict__ A, " << (A.has_lo ? "const float* __restrict__ Alo, " : "")
+            << "const float* __restrict__ B, ";
         for (size_t i = 0; i < k.leaves.size(); ++i) src << "const float* __restrict__ in" << i << ", ";
-        src << "float* __restrict__ out" << (guard_temp >= 0 ? ", const int* guard" : "") << ") {\n"
-            << body.str() << "}\n";
+        src << "float* __restrict__ out" << (so != nullptr ? ", float* __restrict__ lo_out, int* split_flag" : "")
+            << (guard_temp >= 0 ? ", const int* guard" : "") << ") {\n" << body.str() << "}\n";
         l.source = src.str();
         if (tiles > 0x7fffffff) throw std::invalid_argument("matmul output is too large for one launch");
         l.grid = {static_cast<uint32_t>(guard_temp >= 0 ? std::min<int64_t>(tiles, 148 * 8) : tiles),
@@ -2443,6 +2539,7 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
         l.schedule = "gemm CUDA-core 64x64x16 tiles, k-ordered FMA chain, fused epilogue";
         if (guard_temp >= 0) l.schedule += " (runs only for non-finite operands)";
         l.args.push_back(A.arg);
+        if (A.has_lo) l.args.push_back(A.lo);
         l.args.push_back(B.arg);
         for (const kernel_arg& a : k.leaves) l.args.push_back(a);
         kernel_arg o;
@@ -2450,6 +2547,14 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
         o.index = out;
         o.elem_offset = out_off;
         l.args.push_back(o);
+        if (so != nullptr) {
+            kernel_arg lo, fl;
+            lo.kind = fl.kind = arg_kind::temp;
+            lo.index = so->lo;
+            fl.index = so->flag;
+            l.args.push_back(lo);
+            l.args.push_back(fl);
+        }
         if (guard_temp >= 0) {
             kernel_arg gk;
             gk.kind = arg_kind::temp;

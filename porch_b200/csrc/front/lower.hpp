@@ -57,6 +57,8 @@ namespace porch::detail {
     // while it is on make CTA 0 wait on a barrier nothing arrives on, so the
     // bounded wait expires and the kernel reports and tears down.
     void set_test_gemm_stall(bool on);
+    // Whether an [M, K] @ [K, N] product runs on the tensor cores.
+    bool tensor_core_gemm(int64_t M, int64_t N, int64_t K);
     bool test_gemm_stall();
 
     // A matmul operand [rows, cols] read in place: element (i, j) at
@@ -65,6 +67,18 @@ namespace porch::detail {
     // the GEMMs of a batched matmul (they run one after another).
     struct gemm_temps {
         int a_hi = -1, a_lo = -1, b_hi = -1, b_lo = -1, nf = -1, fa = -1, fb = -1;
+        // A's hi / lo / flag were written by the GEMM that produced A (its
+        // split-output epilogue): no split pass for A, and fa not cleared.
+        bool a_ready = false;
+    };
+
+    // A GEMM epilogue that writes its result as the 3xTF32 halves a
+    // following GEMM reads for its A operand: hi / lo temps of rows of `kp`
+    // floats (kp = the result's columns, a multiple of 32) and a flag set
+    // when a result is Inf or NaN (lo is then 0, so hi + lo is the result).
+    struct split_output {
+        int hi = -1, lo = -1, flag = -1;
+        int64_t kp = 0;
     };
 
     struct gemm_operand {
@@ -72,6 +86,11 @@ namespace porch::detail {
         int64_t off = 0;
         int64_t s0 = 0;
         int64_t s1 = 1;
+        // Set when the operand exists only as 3xTF32 halves: element
+        // (i, j) = arg[..] + lo[..] at the same offsets (a GEMM's
+        // split-output result, read by the CUDA-core fallback).
+        bool has_lo = false;
+        kernel_arg lo;
         bool contiguous(int64_t cols) const { return off == 0 && s1 == 1 && s0 == cols; }
     };
 
@@ -138,7 +157,11 @@ namespace porch::detail {
         // that many products over contiguous operands (blockIdx.y).
         int emit_gemm_simt(const box& b, kernel& k, const gemm_operand& A, const gemm_operand& B,
                            int64_t M, int64_t N, int64_t K, int out_temp = -1, int guard_temp = -1,
-                           int64_t out_off = 0, int64_t batches = 1);
+                           int64_t out_off = 0, int64_t batches = 1, const split_output* so = nullptr);
+        // When matmul operand `a` ([M, K]) is a GEMM-with-epilogue read by
+        // nothing else, lowers it with a split-output epilogue into `t`'s A
+        // temps and returns true; `op` then reads those halves.
+        bool presplit_operand(int a, int64_t M, int64_t N, int64_t K, gemm_temps& t, gemm_operand& op);
         // Internal batched matmul: a tensor-core GEMM per batch, or one
         // CUDA-core launch over every batch.
         int emit_batched_gemm(int id);
@@ -152,7 +175,7 @@ namespace porch::detail {
         int emit_gemm_tc(int id, const box& b, kernel& k, const gemm_operand& A,
                          const gemm_operand& B, int64_t M, int64_t N, int64_t K, int* nonfinite,
                          int* row_partials = nullptr, int out_temp = -1, int64_t out_off = 0,
-                         gemm_temps* shared = nullptr);
+                         gemm_temps* shared = nullptr, const split_output* so = nullptr);
         // softmax(x, last axis) where x is an elementwise tree over one
         // rank-2 matmul `mm`: the GEMM's softmax epilogue plus a normalising
         // pass; -1 when the tensor-core GEMM does not apply.
