@@ -341,7 +341,7 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
             }
             l.source = src.str();
             l.args = {X.arg, temp_arg(hi_t), temp_arg(lo_t), temp_arg(flag_t)};
-            if (X.arg.kind == arg_kind::slot) {
+            if (X.arg.kind == arg_kind::slot && !tt.reused) {
                 // A realised input: its storage may keep this split.
                 l.cache_slot = X.arg.index;
                 l.cache_key = "split R" + std::to_string(R) + " K" + std::to_string(K) + " Kp" + std::to_string(Kp) +

@@ -2280,6 +2280,7 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
         // writing its output block through pointer offsets, so every batch
         // runs the same compiled kernels and reuses one set of split temps.
         gemm_temps shared;
+        shared.reused = true;
         for (int64_t t = 0; t < Bt; ++t) {
             const gemm_operand ga = at(A, t * M * K, K), gb = at(B, t * K * N, N);
             int nonfinite = -1;

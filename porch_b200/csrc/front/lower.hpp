@@ -70,6 +70,9 @@ namespace porch::detail {
         // A's hi / lo / flag were written by the GEMM that produced A (its
         // split-output epilogue): no split pass for A, and fa not cleared.
         bool a_ready = false;
+        // The temps serve several GEMMs in turn (a batched matmul): their
+        // splits are not kept, since kept splits are bound by temp.
+        bool reused = false;
     };
 
     // A GEMM epilogue that writes its result as the 3xTF32 halves a
