@@ -397,22 +397,48 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
         // a part-filled last wave runs at a higher clock.
         const int64_t tiles = tiles_m * tiles_n;
         int64_t split = 1;
+        auto wave_fill = [](int64_t u) {
+            return static_cast<double>(u) / (148.0 * static_cast<double>((u + 147) / 148));
+        };
+        // The softmax epilogue can hand a split-K combine the whole row
+        // softmax when a row fits one CTA's registers (16 float4 a thread).
+        const bool softmax_split_ok = softmax && N % 1024 == 0 && N <= 16384;
         if (tiles < 74 && !softmax && so == nullptr) {
             double best = static_cast<double>(tiles) / 148.0;
             for (int64_t s = 2; s <= 16; s *= 2) {
                 if (raw_kb / s < 16) break;
                 const int64_t u = tiles * s;
-                const double eff = static_cast<double>(u) / (148.0 * static_cast<double>((u + 147) / 148));
+                const double eff = wave_fill(u);
                 if (eff > best + 1e-9) {
                     best = eff;
                     split = s;
                 }
             }
+        } else if (so == nullptr && (!softmax || softmax_split_ok) && tiles < 4 * 148 && K > 4096) {
+            // A few waves of long tiles whose last wave leaves SMs idle
+            // (config 5's second GEMM per rank at 4 and 8 GPUs: 512 and 256
+            // tiles, 86.5 % filled): split K in 2 or 4 when that fills the
+            // waves clearly better and each part keeps >= 2048 of K (the
+            // partials' extra traffic, 2 x S x M x N x 4 bytes, is then a
+            // few percent of the tile's tensor time).
+            double best = wave_fill(tiles);
+            int64_t pick = 1;
+            for (int64_t s = 2; s <= 4; s *= 2) {
+                if (raw_kb / s < 128) break;
+                const double eff = wave_fill(tiles * s);
+                if (eff > best + 0.05) {
+                    best = eff;
+                    pick = s;
+                }
+            }
+            split = pick;
         }
+        const bool softmax_split = softmax && split > 1;
         const int64_t kb_unit = (raw_kb + split - 1) / split;
         const int64_t units = tiles * split;
         const int part = split > 1 ? new_temp(static_cast<size_t>(split * M * ((N + 3) / 4 * 4)) * 4) : -1;
-        const int stats = softmax ? new_temp(static_cast<size_t>(M * tiles_n) * 8) : -1;
+        // With split-K the combine does the whole softmax: no row partials.
+        const int stats = softmax && !softmax_split ? new_temp(static_cast<size_t>(M * tiles_n) * 8) : -1;
         if (softmax) *row_partials = stats;
         std::ostringstream src;
         src << kernel_prelude() << (test_gemm_stall() ? "#define PB_TEST_STALL 1\n" : "") << "#define PB_PERIOD "
@@ -447,7 +473,7 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
              << "    __shared__ int abort_flag;\n"
              << "    __shared__ int issued, consumed;\n"
              << "#ifdef PB_TEST_STALL\n    __shared__ __align__(8) unsigned long long stall_bar;\n#endif\n"
-             << (softmax ? "    __shared__ float sm_max[2][PB_BM], sm_sum[2][PB_BM];\n" : "")
+             << (softmax && !softmax_split ? "    __shared__ float sm_max[2][PB_BM], sm_sum[2][PB_BM];\n" : "")
              << "    const pb_u32 warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;\n"
              << "    const pb_u32 base = (pb_smem(pb_dyn_smem) + 1023u) & ~1023u;\n"
              << "    const pb_u32 tiles = " << units << "u;  // work units: tiles x K splits\n"
@@ -573,7 +599,7 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
              << "                __syncwarp();\n"
              << "                if (lane == 0) pb_mbar_arrive(pb_smem(&acce[buf]));\n"
              << "            }\n"
-             << (softmax ? "            // The softmax epilogue exchanges row statistics between the\n"
+             << (softmax && !softmax_split ? "            // The softmax epilogue exchanges row statistics between the\n"
                            "            // column halves: all 256 drain threads agree on going on.\n"
                            "            ok = pb_bar_all(ok);\n" : "")
              << "            if (!ok) break;\n"
@@ -636,7 +662,7 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
                    << ");\n";
             }
         };
-        if (softmax) {
+        if (softmax && !softmax_split) {
             // Softmax over the output row, per tile: y = tree(acc) (columns
             // past N count as -inf), m = the tile row's maximum (the two
             // column halves meet in shared memory), E = exp(y - m) stored in
@@ -802,7 +828,7 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
             << "(const __grid_constant__ pb_tmap tm_ahi, const __grid_constant__ pb_tmap tm_alo, "
                "const __grid_constant__ pb_tmap tm_bhi, const __grid_constant__ pb_tmap tm_blo, ";
         for (size_t i = 0; i < k.leaves.size(); ++i) src << "const float* __restrict__ in" << i << ", ";
-        src << "float* __restrict__ out, " << (softmax ? "float2* __restrict__ stats, " : "")
+        src << "float* __restrict__ out, " << (softmax && !softmax_split ? "float2* __restrict__ stats, " : "")
             << (so != nullptr ? "float* __restrict__ lo_out, int* __restrict__ split_flag, " : "")
             << "int* __restrict__ err, const int* __restrict__ nf) {\n" << body.str() << "}\n";
         l.source = src.str();
@@ -823,7 +849,8 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
             l.schedule += ", persistent CTAs (epilogue overlaps the next tile)";
         }
         if (split > 1) l.schedule += ", split-K x" + std::to_string(split) + " (raw partial tiles)";
-        if (softmax) l.schedule += ", softmax epilogue (exp(y - tile row max) and per-tile row (max, sum))";
+        if (softmax && !softmax_split)
+            l.schedule += ", softmax epilogue (exp(y - tile row max) and per-tile row (max, sum))";
         l.block = {320, 1, 1};
         l.smem = kStages * (2 * kBM * kBK * 4 + 2 * kBN * kBK * 4) + 1024;
         auto tmap_arg = [&](int temp, int64_t rows, int box_rows) {
@@ -843,7 +870,7 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
         kernel_arg out_arg = temp_arg(out);
         out_arg.elem_offset = out_off;
         l.args.push_back(split > 1 ? temp_arg(part) : out_arg);
-        if (softmax) l.args.push_back(temp_arg(stats));
+        if (softmax && !softmax_split) l.args.push_back(temp_arg(stats));
         if (so != nullptr) {
             l.args.push_back(temp_arg(so->lo));
             l.args.push_back(temp_arg(so->flag));
@@ -856,6 +883,88 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
         finish_kernel(l);
         p_.launches.push_back(std::move(l));
         if (split == 1) return out;
+
+        // ---- 4b. split-K + softmax: one CTA per row sums the partials in
+        // split order, applies the epilogue, and runs the row softmax (max,
+        // exp(y - max), sum, one division, multiplies) on values held in
+        // registers: the result is written once.
+        if (softmax_split) {
+            const int64_t NV = N / 1024; // float4 columns per thread
+            std::ostringstream ks;
+            ks << kernel_prelude() << efn;
+            std::ostringstream kb;
+            kb << "    if (*(const volatile int*)nf != 0) return;  // the CUDA-core GEMM writes out\n"
+               << "    __shared__ float red_m[8], red_s[8];\n"
+               << "    const pb_u32 warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;\n"
+               << "    for (pb_u64 rr = blockIdx.x; rr < " << M << "ull; rr += gridDim.x) {\n"
+               << "        float v[" << NV << "][4];\n";
+            emit_hoisted(kb, "        ");
+            kb << "        #pragma unroll\n"
+               << "        for (int q = 0; q < " << NV << "; ++q) {\n"
+               << "            const pb_u64 cc = 4u * ((pb_u64)threadIdx.x + 256u * (pb_u64)q);\n"
+               << "            const pb_u64 o = rr * " << N << "ull + cc;\n"
+               << "            float4 s = pb_ld4(part + o);\n"
+               << "            #pragma unroll\n"
+               << "            for (int p = 1; p < " << split << "; ++p) {\n"
+               << "                const float4 w = pb_ld4(part + (pb_u64)p * " << M * N << "ull + o);\n"
+               << "                s.x = s.x + w.x; s.y = s.y + w.y; s.z = s.z + w.z; s.w = s.w + w.w;\n"
+               << "            }\n"
+               << "            const float sv[4] = {s.x, s.y, s.z, s.w};\n";
+            emit_epilogue4(kb, "            ", "sv[e]");
+            kb << "            #pragma unroll\n"
+               << "            for (int e = 0; e < 4; ++e) v[q][e] = y[e];\n"
+               << "        }\n"
+               << "        float m = __int_as_float(0xff800000);\n"
+               << "        #pragma unroll\n"
+               << "        for (int q = 0; q < " << NV << "; ++q)\n"
+               << "            #pragma unroll\n"
+               << "            for (int e = 0; e < 4; ++e) m = v[q][e] > m ? v[q][e] : m;\n"
+               << "        #pragma unroll\n"
+               << "        for (int x = 16; x > 0; x >>= 1) { const float t = __shfl_xor_sync(0xffffffffu, m, x); m = t > m ? t : m; }\n"
+               << "        if (lane == 0u) red_m[warp] = m;\n"
+               << "        __syncthreads();\n"
+               << "        m = red_m[0];\n"
+               << "        #pragma unroll\n"
+               << "        for (int w = 1; w < 8; ++w) m = red_m[w] > m ? red_m[w] : m;\n"
+               << "        float sum = 0.0f;\n"
+               << "        #pragma unroll\n"
+               << "        for (int q = 0; q < " << NV << "; ++q)\n"
+               << "            #pragma unroll\n"
+               << "            for (int e = 0; e < 4; ++e) { v[q][e] = __expf(v[q][e] - m); sum = sum + v[q][e]; }\n"
+               << "        #pragma unroll\n"
+               << "        for (int x = 16; x > 0; x >>= 1) sum = sum + __shfl_xor_sync(0xffffffffu, sum, x);\n"
+               << "        if (lane == 0u) red_s[warp] = sum;\n"
+               << "        __syncthreads();\n"
+               << "        sum = red_s[0];\n"
+               << "        #pragma unroll\n"
+               << "        for (int w = 1; w < 8; ++w) sum = sum + red_s[w];\n"
+               << "        const float inv = 1.0f / sum;\n"
+               << "        #pragma unroll\n"
+               << "        for (int q = 0; q < " << NV << "; ++q) {\n"
+               << "            const pb_u64 cc = 4u * ((pb_u64)threadIdx.x + 256u * (pb_u64)q);\n"
+               << "            pb_st4(out + rr * " << N << "ull + cc, make_float4(v[q][0] * inv, v[q][1] * inv, v[q][2] * inv, v[q][3] * inv));\n"
+               << "        }\n"
+               << "        __syncthreads();  // red_m / red_s serve the next row\n"
+               << "    }\n";
+            launch_spec r;
+            r.name = "pb_splitk_softmax_" + hex8(ks.str() + kb.str());
+            ks << "extern \"C\" __global__ void __launch_bounds__(256) " << r.name << "(";
+            for (size_t i = 0; i < k.leaves.size(); ++i) ks << "const float* __restrict__ in" << i << ", ";
+            ks << "const float* __restrict__ part, float* __restrict__ out, const int* __restrict__ nf) {\n"
+               << kb.str() << "}\n";
+            r.source = ks.str();
+            r.schedule = "split-K softmax combine: " + std::to_string(split) +
+                         " partials summed in split order, fused epilogue, row softmax in registers (a CTA per row)";
+            r.grid = {static_cast<uint32_t>(std::min<int64_t>(M, 148 * 8)), 1, 1};
+            r.block = {256, 1, 1};
+            r.args = k.leaves;
+            r.args.push_back(temp_arg(part));
+            r.args.push_back(out_arg);
+            r.args.push_back(temp_arg(nf));
+            finish_kernel(r);
+            p_.launches.push_back(std::move(r));
+            return out;
+        }
 
         // ---- 4. split-K: sum the partials in split order + epilogue ---------
         {

@@ -2373,8 +2373,9 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
         // The normalising pass, in place: per row, M = max of the tiles'
         // maxima, S = sum_t s_t exp(m_t - M), and each tile's values times
         // f_t = exp(m_t - M) * (1 / S). A warp per row; the row's T factors
-        // in shared memory.
-        {
+        // in shared memory. (With split-K its combine did the whole
+        // softmax: no row statistics, no pass.)
+        if (stats >= 0) {
             const bool vec = N % 4 == 0;
             std::ostringstream src;
             src << kernel_prelude();

@@ -37,8 +37,11 @@ def _kernels(api, fn):
         api.profile_enable(False)
 
 
-@pytest.mark.parametrize("m,k,n", [(1024, 512, 4396), (640, 768, 1000), (256, 2048, 256)])
+@pytest.mark.parametrize("m,k,n", [(1024, 512, 4396), (640, 768, 1000), (256, 2048, 256),
+                                   (512, 8192, 4096), (1024, 6144, 2048)])
 def test_gemm_softmax_epilogue_matches_fp64(gpu, m, k, n):
+    """The last two shapes have few tiles of long K: the GEMM splits K to
+    fill its waves and the split-K combine runs the whole row softmax."""
     api = gpu
     rng = np.random.default_rng(m + k + n)
     s = 3.0 / np.sqrt(k)
@@ -48,9 +51,14 @@ def test_gemm_softmax_epilogue_matches_fp64(gpu, m, k, n):
     A, B, Bi = api.tensor([m, k], a), api.tensor([k, n], b), api.tensor([n], bias)
     z_expr = api.matmul(A, B) + api.broadcast_to(Bi, [m, n])
     plan = api.describe(api.softmax(z_expr, 1))
-    assert "softmax epilogue" in plan and "pb_softmax_norm" in plan, plan
+    split = k > 4096
+    if split:
+        assert "split-K softmax combine" in plan, plan
+    else:
+        assert "softmax epilogue" in plan and "pb_softmax_norm" in plan, plan
     P, kernels = _kernels(api, lambda: api.materialize(api.softmax(z_expr, 1)))
-    assert any(name.startswith("pb_softmax_norm") for name in kernels), kernels
+    fused = "pb_splitk_softmax" if split else "pb_softmax_norm"
+    assert any(name.startswith(fused) for name in kernels), kernels
     got = P.cpu().reshape(m, n)
     z = api.materialize(z_expr).cpu().reshape(m, n)
     z64 = a.astype(np.float64) @ b.astype(np.float64) + bias.astype(np.float64)
