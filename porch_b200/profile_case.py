@@ -50,6 +50,13 @@ GRAPHS = {
     "splitk": ([[128, 4096], [4096, 4096]], lambda t: api.matmul(t[0], t[1])),
     "gemm_simt": ([[512, 512], [512, 256]], lambda t: api.matmul(t[0], t[1])),
     "split": ([[2048, 8192], [8192, 8192]], lambda t: api.matmul(t[0], t[1])),
+    # Config 5's first GEMM at 4096 rows writing H in fp32, and the same GEMM
+    # writing H as the second GEMM's 3xTF32 halves (split output).
+    "gemm1_plain": ([[4096, 4096], [4096, 16384], [16384]],
+                    lambda t: api.logistic(api.matmul(t[0], t[1]) + api.broadcast_to(t[2], [4096, 16384]))),
+    "gemm1_split": ([[4096, 4096], [4096, 16384], [16384], [16384, 4096]],
+                    lambda t: api.matmul(api.logistic(api.matmul(t[0], t[1]) + api.broadcast_to(t[2], [4096, 16384])),
+                                         t[3])),
 }
 
 
