@@ -285,7 +285,10 @@ def _config_keys(workload: str, world: int) -> dict:
     return {"workload": workload,
             "shapes": {k: s for k, (s, *_) in zip(KEYS[workload], specs)},
             "parallelism": (f"row-shard x{world}" if workload in ROW_SHARDED and world > 1
-                            else (f"replicas x{world}" if world > 1 else "single GPU"))}
+                            else (f"replicas x{world}" if world > 1 else "single GPU")),
+            # Both arms: each step's inputs together exceed the 126 MB L2
+            # (this arm also rotates two input sets, `setup`).
+            "l2": "inputs larger than L2"}
 
 
 def measure(api, workload: str, args, rank, world, local, dist, cpu_seconds: float | None,
