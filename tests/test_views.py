@@ -152,3 +152,34 @@ def test_permute_checks_its_axes(gpu):
     Y = api.tensor([5, 7, 9], x)
     got = api.materialize(api.permute(Y, [1, 2, 0]) * 3.0).cpu().reshape(7, 9, 5)
     assert_bitwise(got, np.transpose(x, (1, 2, 0)) * np.float32(3), "permute in a graph")
+
+
+def test_threads_reading_one_view_concurrently(gpu):
+    """Several threads realise graphs over, and read the values of, the same
+    view at once: each first read copies the view out; one copy wins, and
+    every reader sees the same values."""
+    import threading
+
+    api = gpu
+    x = _ints([256, 512], 8)
+    X = api.tensor([256, 512], x)
+    V = api.materialize(api.transpose(X[16:240:2, 100:400]))
+    want = np.ascontiguousarray(x[16:240:2, 100:400].T)
+    errors = []
+
+    def reader(j):
+        try:
+            for _ in range(5):
+                got = api.materialize(V * float(j + 1)).cpu().reshape(want.shape)
+                assert np.array_equal(got, want * np.float32(j + 1))
+                assert np.array_equal(V.cpu().reshape(want.shape), want)
+        except Exception as exc:  # reported below
+            errors.append(repr(exc))
+
+    threads = [threading.Thread(target=reader, args=(j,)) for j in range(4)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join()
+    api.synchronize()
+    assert not errors, errors
