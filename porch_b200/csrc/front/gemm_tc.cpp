@@ -403,7 +403,9 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
         // The softmax epilogue can hand a split-K combine the whole row
         // softmax when a row fits one CTA's registers (16 float4 a thread).
         const bool softmax_split_ok = softmax && N % 1024 == 0 && N <= 16384;
-        if (tiles < 74 && !softmax && so == nullptr) {
+        // One policy for both epilogues, so a softmax over a product and the
+        // product realised alone sum K in the same parts.
+        if (tiles < 74 && (!softmax || softmax_split_ok) && so == nullptr) {
             double best = static_cast<double>(tiles) / 148.0;
             for (int64_t s = 2; s <= 16; s *= 2) {
                 if (raw_kb / s < 16) break;

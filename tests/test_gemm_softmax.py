@@ -63,8 +63,28 @@ def test_gemm_softmax_epilogue_matches_fp64(gpu, m, k, n):
     z = api.materialize(z_expr).cpu().reshape(m, n)
     z64 = a.astype(np.float64) @ b.astype(np.float64) + bias.astype(np.float64)
     assert matmul_error(z, z64, k) <= MATMUL_TOL
-    assert_relative(got, _softmax64(z), REL_TOL, f"gemm softmax {m}x{k}x{n}")
+    if _split_parts(api.describe(z_expr)) == _split_parts(plan):
+        # The realised product summed K in the same parts as the fused GEMM:
+        # the same z, so the softmax steps alone are measured.
+        assert_relative(got, _softmax64(z), REL_TOL, f"gemm softmax {m}x{k}x{n}")
+    else:
+        # Different parts (a softmax epilogue splits only rows of a multiple
+        # of 1024 columns): against fp64, the softmax bar plus the GEMM bar
+        # carried through the softmax (|d log P| <= 2 max |dz|).
+        zscale = np.maximum(np.abs(z64), np.sqrt(np.mean(z64 ** 2))).max(axis=1, keepdims=True)
+        rel = np.abs(got - _softmax64(z64)) / _softmax64(z64)
+        assert np.all(rel <= REL_TOL + 2 * MATMUL_TOL * np.sqrt(k) * zscale)
     assert np.allclose(got.sum(axis=1, dtype=np.float64), 1.0, atol=1e-5)
+
+
+def _split_parts(plan: str) -> int:
+    import re
+
+    for line in plan.splitlines():
+        if "pb_gemm_tc" in line:
+            found = re.search(r"split-K x(\d+)", line)
+            return int(found.group(1)) if found else 1
+    return 1
 
 
 def test_gemm_softmax_with_nonfinite_operand_takes_the_reference_steps(gpu, oracle_lib):
