@@ -133,6 +133,10 @@ int pbrt_function_set_max_dynamic_smem(pbrt_function function, int bytes);
  * dynamic shared memory (registers, shared memory and thread limits). */
 int pbrt_occupancy(int device, pbrt_function function, int block_threads, size_t dynamic_smem,
                    int* blocks_per_sm);
+/* Clusters of `cluster_x` CTAs of `function` that can be resident on
+ * `device` at once (cuOccupancyMaxActiveClusters). */
+int pbrt_max_active_clusters(int device, pbrt_function function, int block_threads, size_t dynamic_smem,
+                             unsigned cluster_x, int* clusters);
 int pbrt_function_attribute(pbrt_function function, int attribute,
                             int* value);
 /* grid/block are 3-vectors; cluster may be NULL (no cluster attribute). */

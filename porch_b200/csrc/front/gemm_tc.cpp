@@ -54,15 +54,26 @@ namespace porch::detail {
         constexpr int kBN = 256;
         constexpr int kBK = 16;
         constexpr int kStages = 4;
+        constexpr int kPairStages = 6;
 
         const char* gemm_device_source() {
             return R"PB(
 #define PB_BM 128
 #define PB_BN 256
 #define PB_BK 16
+// PB_PAIR: a cluster of two CTAs (on one SM pair) computes a 256 x 256
+// tile with cta_group::2 MMAs: each CTA holds its own 128 rows of A and
+// half (128 rows of N) of B, and its own 128 x 256 accumulator in TMEM.
+#ifdef PB_PAIR
+#define PB_CTAS 2
+#define PB_STAGES 6
+#else
+#define PB_CTAS 1
 #define PB_STAGES 4
+#endif
+#define PB_BNH (PB_BN / PB_CTAS)
 #define PB_TILE_A_BYTES (PB_BM * PB_BK * 4)
-#define PB_TILE_B_BYTES (PB_BN * PB_BK * 4)
+#define PB_TILE_B_BYTES (PB_BNH * PB_BK * 4)
 #define PB_STAGE_BYTES (2 * PB_TILE_A_BYTES + 2 * PB_TILE_B_BYTES)
 #define PB_WAIT_CYCLES 4000000000ll
 
@@ -84,6 +95,40 @@ static __device__ __forceinline__ void pb_mbar_expect_tx(pb_u32 bar, pb_u32 byte
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(bar), "r"(bytes) : "memory");
 }
 
+// Rank of this CTA in its cluster (0 without PB_PAIR) and the
+// shared::cluster address of the same shared variable in CTA `rank`.
+static __device__ __forceinline__ pb_u32 pb_cta_rank() {
+#ifdef PB_PAIR
+    pb_u32 r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+#else
+    return 0u;
+#endif
+}
+
+static __device__ __forceinline__ pb_u32 pb_mapa(pb_u32 addr, pb_u32 rank) {
+    pb_u32 r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+
+// All threads of both CTAs of the pair (release / acquire; the forms that
+// do not need the warp converged).
+static __device__ __forceinline__ void pb_cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release;\nbarrier.cluster.wait.acquire;" ::: "memory");
+}
+
+// Arrivals on an mbarrier of either CTA of the pair (shared::cluster address).
+static __device__ __forceinline__ void pb_mbar_arrive_cl(pb_u32 bar) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" :: "r"(bar) : "memory");
+}
+
+// Counts `bytes` as landed on a local barrier (for bytes that will never come).
+static __device__ __forceinline__ void pb_mbar_complete_tx(pb_u32 bar, pb_u32 bytes) {
+    asm volatile("mbarrier.complete_tx.shared::cta.b64 [%0], %1;" :: "r"(bar), "r"(bytes) : "memory");
+}
+
 static __device__ __forceinline__ pb_u32 pb_mbar_try(pb_u32 bar, pb_u32 parity) {
     pb_u32 ok;
     asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
@@ -91,15 +136,23 @@ static __device__ __forceinline__ pb_u32 pb_mbar_try(pb_u32 bar, pb_u32 parity) 
     return ok;
 }
 
-// Bounded wait: false when the budget ran out or another role aborted.
-static __device__ __forceinline__ bool pb_wait(pb_u32 bar, pb_u32 parity, volatile int* abort_flag,
-                                               int* err, int site) {
+// Bounded wait: false when the budget ran out or another role (of this
+// CTA or, in a pair, of the other CTA) aborted.
+static __device__ __forceinline__ bool pb_wait_for(pb_u32 bar, pb_u32 parity, volatile int* abort_flag,
+                                                   int* err, int site, long long budget) {
     const long long start = clock64();
     for (;;) {
         if (pb_mbar_try(bar, parity)) return true;
         if (*abort_flag) return false;
-        if (clock64() - start > PB_WAIT_CYCLES) {
+        if (clock64() - start > budget) {
             *abort_flag = 1;
+#ifdef PB_PAIR
+            {   // the other CTA of the pair stops too (its flag, through distributed shared memory)
+                pb_u64 peer;
+                asm volatile("mapa.u64 %0, %1, %2;" : "=l"(peer) : "l"((pb_u64)abort_flag), "r"(pb_cta_rank() ^ 1u));
+                *(volatile int*)peer = 1;
+            }
+#endif
             if (atomicCAS(err, 0, 0x7c00 + site) == 0) {
                 err[1] = site;
                 err[2] = (int)blockIdx.x;
@@ -109,9 +162,35 @@ static __device__ __forceinline__ bool pb_wait(pb_u32 bar, pb_u32 parity, volati
     }
 }
 
+static __device__ __forceinline__ bool pb_wait(pb_u32 bar, pb_u32 parity, volatile int* abort_flag, int* err,
+                                               int site) {
+    return pb_wait_for(bar, parity, abort_flag, err, site, PB_WAIT_CYCLES);
+}
+
+// Teardown wait: bounded, records nothing.
+static __device__ __forceinline__ void pb_wait_quiet(pb_u32 bar, pb_u32 parity) {
+    const long long start = clock64();
+    while (!pb_mbar_try(bar, parity) && clock64() - start <= PB_WAIT_CYCLES) {
+    }
+}
+
+// An int in the other CTA of the pair (distributed shared memory).
+static __device__ __forceinline__ int pb_peer_int(const int* p) {
+    pb_u64 q;
+    asm volatile("mapa.u64 %0, %1, %2;" : "=l"(q) : "l"((pb_u64)p), "r"(pb_cta_rank() ^ 1u));
+    return *(const volatile int*)q;
+}
+
+// Tile load into this CTA's shared memory; completion is counted on `bar`,
+// which in a pair is the first CTA's barrier (a shared::cluster address).
 static __device__ __forceinline__ void pb_tma_load(pb_u32 dst, const pb_tmap* map, pb_u32 bar, int x, int y) {
+#ifdef PB_PAIR
+    asm volatile("cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+                 :: "r"(dst), "l"((unsigned long long)map), "r"(bar), "r"(x), "r"(y) : "memory");
+#else
     asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
                  :: "r"(dst), "l"((unsigned long long)map), "r"(bar), "r"(x), "r"(y) : "memory");
+#endif
 }
 
 // tcgen05 shared-memory matrix descriptor: K-major, 64B swizzle (one
@@ -128,16 +207,41 @@ static __device__ __forceinline__ pb_u64 pb_desc(pb_u32 addr) {
     return d;
 }
 
-// Instruction descriptor: D f32, A/B tf32, both K-major, N>>3, M>>4.
-#define PB_IDESC ((1u << 4) | (2u << 7) | (2u << 10) | ((pb_u32)(PB_BN >> 3) << 17) | ((pb_u32)(PB_BM >> 4) << 24))
+// Instruction descriptor: D f32, A/B tf32, both K-major, N>>3, M>>4 (M of
+// the whole MMA: 256 for a pair).
+#define PB_IDESC ((1u << 4) | (2u << 7) | (2u << 10) | ((pb_u32)(PB_BN >> 3) << 17) | ((pb_u32)((PB_BM * PB_CTAS) >> 4) << 24))
 
+// Issued by one thread (of the first CTA in a pair); the descriptors name
+// this CTA's shared memory, and a pair's MMA reads the other CTA's A and B
+// halves at the same offsets.
 static __device__ __forceinline__ void pb_mma(pb_u32 tmem, pb_u64 a, pb_u64 b, pb_u32 accumulate) {
+#ifdef PB_PAIR
+    asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n}\n"
+                 :: "r"(tmem), "l"(a), "l"(b), "r"(PB_IDESC), "r"(accumulate) : "memory");
+#else
     asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}\n"
                  :: "r"(tmem), "l"(a), "l"(b), "r"(PB_IDESC), "r"(accumulate) : "memory");
+#endif
 }
 
+// Arrives on `bar` (a local shared address) once the MMAs issued so far have
+// completed: in a pair, on that barrier in both CTAs.
 static __device__ __forceinline__ void pb_commit(pb_u32 bar) {
+#ifdef PB_PAIR
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" :: "r"(pb_mapa(bar, 0u)) : "memory");
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" :: "r"(pb_mapa(bar, 1u)) : "memory");
+#else
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" :: "r"(bar) : "memory");
+#endif
+}
+
+// The same, on this CTA's barrier only.
+static __device__ __forceinline__ void pb_commit_local(pb_u32 bar) {
+#ifdef PB_PAIR
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" :: "r"(pb_mapa(bar, pb_cta_rank())) : "memory");
+#else
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" :: "r"(bar) : "memory");
+#endif
 }
 
 static __device__ __forceinline__ float pb_tf32_rn(float x) {
@@ -193,11 +297,21 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
             return v != nullptr && std::string{v} == "simt";
         }
 
+        bool gemm_pairs_enabled() {
+            const char* v = std::getenv("PORCH_B200_GEMM");
+            return v != nullptr && std::string{v} == "pair";
+        }
+
     } // namespace
 
     bool tensor_core_gemm(int64_t M, int64_t N, int64_t K) {
         return !tensor_cores_disabled() && M >= 1 && N >= 1 && K >= 1 && M * N * K >= (int64_t{1} << 27) &&
                M <= (int64_t{1} << 30) && N <= (int64_t{1} << 30) && K <= (int64_t{1} << 30);
+    }
+
+    std::string gemm_form_key() {
+        const char* v = std::getenv("PORCH_B200_GEMM");
+        return v == nullptr ? std::string{} : "|gemm=" + std::string{v};
     }
 
     void set_test_gemm_stall(bool on) { g_test_stall.store(on); }
@@ -370,9 +484,23 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
         // ---- 3. tcgen05 GEMM + epilogue -------------------------------------
         std::vector<int> order;
         const std::string efn = emit_expr_function(b, "0", order);
-        const int64_t tiles_m = (M + kBM - 1) / kBM, tiles_n = (N + kBN - 1) / kBN;
+        // CTA pairs (cta_group::2, 256 x 256 tiles), on request
+        // (PORCH_B200_GEMM=pair), wherever there are at least two 128-row
+        // tiles and pairing leaves no more than a sliver of a pair idle.
+        // Each CTA then loads half of B for the same MMAs, and the pair
+        // draws less power (config 5: about 40 MHz higher clock under the
+        // 1 kW cap), but its tensor pipe is busy a smaller share of the
+        // cycles (ncu at 4096 rows: 78 / 77 % against 82 / 87 % for the
+        // two GEMMs): measured 216-220 TFLOP/s against 221-222 for one CTA
+        // per tile, so one CTA per 128 x 256 tile stays the default. The
+        // results are bit-identical either way.
+        const int64_t tiles_m1 = (M + kBM - 1) / kBM;
+        const bool pair = gemm_pairs_enabled() && tiles_m1 >= 2 && (tiles_m1 % 2 == 0 || tiles_m1 >= 8);
+        const int ctas = pair ? 2 : 1;
+        const int64_t slots = 148 / ctas; // work units resident at once
+        const int64_t tiles_m = (M + kBM * ctas - 1) / (kBM * ctas), tiles_n = (N + kBN - 1) / kBN;
         const int64_t raw_kb = (K + kBK - 1) / kBK;
-        const int group_m = 16;
+        const int group_m = 16 / ctas; // 16 rows of 128
         // Accumulation period in k-blocks. The drift of a tensor-core
         // accumulator grows with the number of MMAs added into one period
         // (6 per k-block: 3 products x 2 k-steps), independent of K, while
@@ -397,16 +525,16 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
         // a part-filled last wave runs at a higher clock.
         const int64_t tiles = tiles_m * tiles_n;
         int64_t split = 1;
-        auto wave_fill = [](int64_t u) {
-            return static_cast<double>(u) / (148.0 * static_cast<double>((u + 147) / 148));
+        auto wave_fill = [slots](int64_t u) {
+            return static_cast<double>(u) / static_cast<double>(slots * ((u + slots - 1) / slots));
         };
         // The softmax epilogue can hand a split-K combine the whole row
         // softmax when a row fits one CTA's registers (16 float4 a thread).
         const bool softmax_split_ok = softmax && N % 1024 == 0 && N <= 16384;
         // One policy for both epilogues, so a softmax over a product and the
         // product realised alone sum K in the same parts.
-        if (tiles < 74 && (!softmax || softmax_split_ok) && so == nullptr) {
-            double best = static_cast<double>(tiles) / 148.0;
+        if (tiles < slots / 2 && (!softmax || softmax_split_ok) && so == nullptr) {
+            double best = static_cast<double>(tiles) / static_cast<double>(slots);
             for (int64_t s = 2; s <= 16; s *= 2) {
                 if (raw_kb / s < 16) break;
                 const int64_t u = tiles * s;
@@ -416,7 +544,7 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
                     split = s;
                 }
             }
-        } else if (so == nullptr && (!softmax || softmax_split_ok) && tiles < 4 * 148 && K > 4096) {
+        } else if (so == nullptr && (!softmax || softmax_split_ok) && tiles < 4 * slots && K > 4096) {
             // A few waves of long tiles whose last wave leaves SMs idle
             // (config 5's second GEMM per rank at 4 and 8 GPUs: 512 and 256
             // tiles, 86.5 % filled): split K in 2 or 4 when that fills the
@@ -443,7 +571,8 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
         const int stats = softmax && !softmax_split ? new_temp(static_cast<size_t>(M * tiles_n) * 8) : -1;
         if (softmax) *row_partials = stats;
         std::ostringstream src;
-        src << kernel_prelude() << (test_gemm_stall() ? "#define PB_TEST_STALL 1\n" : "") << "#define PB_PERIOD "
+        src << kernel_prelude() << (test_gemm_stall() ? "#define PB_TEST_STALL 1\n" : "")
+            << (pair ? "#define PB_PAIR 1\n" : "") << "#define PB_PERIOD "
             << period << "\n#define PB_SPLIT " << split << "\n"
             << gemm_device_source() << efn;
         // Tile t -> output origin, tiles ordered in groups of group_m M-tiles
@@ -454,7 +583,7 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
             << "    const pb_u32 per_group = " << group_m << "u * tiles_n;\n"
             << "    const pb_u32 g = t / per_group, first_m = g * " << group_m << "u;\n"
             << "    const pb_u32 gm = (tiles_m - first_m) < " << group_m << "u ? (tiles_m - first_m) : " << group_m << "u;\n"
-            << "    m0 = (int)((first_m + (t % per_group) % gm) * PB_BM);\n"
+            << "    m0 = (int)((first_m + (t % per_group) % gm) * (PB_BM * PB_CTAS));\n"
             << "    n0 = (int)(((t % per_group) / gm) * PB_BN);\n"
             << "}\n";
         std::ostringstream body;
@@ -477,24 +606,31 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
              << "#ifdef PB_TEST_STALL\n    __shared__ __align__(8) unsigned long long stall_bar;\n#endif\n"
              << (softmax && !softmax_split ? "    __shared__ float sm_max[2][PB_BM], sm_sum[2][PB_BM];\n" : "")
              << "    const pb_u32 warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;\n"
+             << "    const pb_u32 rank = pb_cta_rank();  // 1: the second CTA of a pair\n"
              << "    const pb_u32 base = (pb_smem(pb_dyn_smem) + 1023u) & ~1023u;\n"
              << "    const pb_u32 tiles = " << units << "u;  // work units: tiles x K splits\n"
              << "    if (threadIdx.x == 0) {\n"
              << "        abort_flag = 0;\n"
              << "        issued = 0;\n"
              << "        consumed = 0;\n"
+             // In a pair the first CTA's full barriers count both CTAs'
+             // bytes (the first CTA arms them for both), its acce barriers
+             // both CTAs' drains.
              << "        for (int s = 0; s < PB_STAGES; ++s) { pb_mbar_init(pb_smem(&full_bar[s]), 1); pb_mbar_init(pb_smem(&empty_bar[s]), 1); }\n"
-             << "        for (int b = 0; b < 2; ++b) { pb_mbar_init(pb_smem(&accf[b]), 1); pb_mbar_init(pb_smem(&acce[b]), 8); }\n"
+             << "        for (int b = 0; b < 2; ++b) { pb_mbar_init(pb_smem(&accf[b]), 1); pb_mbar_init(pb_smem(&acce[b]), 8 * PB_CTAS); }\n"
              << "        pb_mbar_init(pb_smem(&done_bar), 1);\n"
              << "#ifdef PB_TEST_STALL\n        pb_mbar_init(pb_smem(&stall_bar), 1);\n#endif\n"
              << "        asm volatile(\"fence.mbarrier_init.release.cluster;\" ::: \"memory\");\n"
              << "    }\n"
+             // Warp 9 of each CTA allocates (a pair allocates together,
+             // the same columns in both CTAs).
              << "    if (warp == 9) {\n"
-             << "        asm volatile(\"tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;\" :: \"r\"(pb_smem(&tmem_slot)) : \"memory\");\n"
-             << "        asm volatile(\"tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\" ::: \"memory\");\n"
+             << "        asm volatile(\"tcgen05.alloc.cta_group::" << ctas << ".sync.aligned.shared::cta.b32 [%0], 512;\" :: \"r\"(pb_smem(&tmem_slot)) : \"memory\");\n"
+             << "        asm volatile(\"tcgen05.relinquish_alloc_permit.cta_group::" << ctas << ".sync.aligned;\" ::: \"memory\");\n"
              << "    }\n"
              << "    asm volatile(\"tcgen05.fence::before_thread_sync;\" ::: \"memory\");\n"
-             << "    __syncthreads();\n"
+             << (pair ? "    pb_cluster_sync();  // barriers initialised and TMEM allocated in both CTAs\n"
+                      : "    __syncthreads();\n")
              << "    asm volatile(\"tcgen05.fence::after_thread_sync;\" ::: \"memory\");\n"
              << "    const pb_u32 tmem = tmem_slot;\n"
              << "    const int num_kb = " << kb_unit << ";  // k-blocks per work unit\n"
@@ -504,17 +640,21 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
              // producer
              << "            int g = 0;\n"
              << "            bool stop = false;\n"
-             << "            for (pb_u32 t = blockIdx.x; t < tiles && !stop; t += gridDim.x) {\n"
+             << "            for (pb_u32 t = blockIdx.x / PB_CTAS; t < tiles && !stop; t += gridDim.x / PB_CTAS) {\n"
              << "                int m0, n0;\n"
              << "                pb_tile_origin(t / PB_SPLIT, m0, n0);\n"
+             << "                m0 += (int)(rank * PB_BM);   // this CTA's rows of A\n"
+             << "                n0 += (int)(rank * PB_BNH);  // and of B (N)\n"
              << "                const int kbase = (int)(t % PB_SPLIT) * num_kb;\n"
              << "                for (int kb = 0; kb < num_kb; ++kb, ++g) {\n"
              << "                    const int s = g % PB_STAGES;\n"
              << "                    const pb_u32 phase = (pb_u32)(g / PB_STAGES) & 1u;\n"
              << "                    if (!pb_wait(pb_smem(&empty_bar[s]), phase ^ 1u, &abort_flag, err, 1)) { stop = true; break; }\n"
              << "                    const pb_u32 st = base + (pb_u32)s * PB_STAGE_BYTES;\n"
-             << "                    const pb_u32 fb = pb_smem(&full_bar[s]);\n"
-             << "                    pb_mbar_expect_tx(fb, PB_STAGE_BYTES);\n"
+             << (pair ? "                    const pb_u32 fb = pb_mapa(pb_smem(&full_bar[s]), 0u);\n"
+                        "                    if (rank == 0) pb_mbar_expect_tx(pb_smem(&full_bar[s]), 2 * PB_STAGE_BYTES);\n"
+                      : "                    const pb_u32 fb = pb_smem(&full_bar[s]);\n"
+                        "                    pb_mbar_expect_tx(fb, PB_STAGE_BYTES);\n")
              << "                    const int kx = (kbase + kb) * PB_BK;\n"
              << "                    pb_tma_load(st, &tm_ahi, fb, kx, m0);\n"
              << "                    pb_tma_load(st + PB_TILE_A_BYTES, &tm_alo, fb, kx, m0);\n"
@@ -526,7 +666,7 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
              << "        }\n"
              << "        __syncwarp();\n"
              << "    } else if (warp == 9) {\n"
-             << "        if (lane == 0) {\n"
+             << "        if (lane == 0 && rank == 0) {\n"
              // MMA issuer: period p (PB_PERIOD k-blocks, never straddling a
              // tile) accumulates from zero into TMEM buffer p % 2 (columns
              // 256 (p % 2)..+255); before reusing a buffer it waits for the
@@ -536,9 +676,10 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
              // Failure-detection test hook: CTA 0 waits on a barrier nothing
              // arrives on, so its bounded wait gives up (site 7).
              << "#ifdef PB_TEST_STALL\n"
-             << "            if (blockIdx.x == 0u && !pb_wait(pb_smem(&stall_bar), 0u, &abort_flag, err, 7)) stop = true;\n"
+             // Half the usual budget, so that this wait is the first to give up.
+             << "            if (blockIdx.x == 0u && !pb_wait_for(pb_smem(&stall_bar), 0u, &abort_flag, err, 7, PB_WAIT_CYCLES / 2)) stop = true;\n"
              << "#endif\n"
-             << "            for (pb_u32 t = blockIdx.x; t < tiles && !stop; t += gridDim.x, per_base += periods) {\n"
+             << "            for (pb_u32 t = blockIdx.x / PB_CTAS; t < tiles && !stop; t += gridDim.x / PB_CTAS, per_base += periods) {\n"
              << "                for (int kb = 0; kb < num_kb; ++kb, ++g) {\n"
              << "                    const int s = g % PB_STAGES;\n"
              << "                    const pb_u32 phase = (pb_u32)(g / PB_STAGES) & 1u;\n"
@@ -569,7 +710,7 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
              << "            }\n"
              // Whether or not the loops finished: completes once every MMA
              // issued so far has (the teardown waits for it).
-             << "            pb_commit(pb_smem(&done_bar));\n"
+             << "            pb_commit_local(pb_smem(&done_bar));\n"
              << "        }\n"
              << "        __syncwarp();\n"
              << "    } else {\n"
@@ -577,9 +718,10 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
              << "        const pb_u32 quad = warp & 3u, half = warp >> 2;\n"
              << "        int per = 0;\n"
              << "        bool ok = true;\n"
-             << "        for (pb_u32 t = blockIdx.x; t < tiles && ok; t += gridDim.x) {\n"
+             << "        for (pb_u32 t = blockIdx.x / PB_CTAS; t < tiles && ok; t += gridDim.x / PB_CTAS) {\n"
              << "            int m0, n0;\n"
              << "            pb_tile_origin(t / PB_SPLIT, m0, n0);\n"
+             << "            m0 += (int)(rank * PB_BM);  // this CTA's 128 rows of the tile\n"
              << "            float acc[PB_BN / 2];\n"
              << "            #pragma unroll\n"
              << "            for (int j = 0; j < PB_BN / 2; ++j) acc[j] = 0.0f;\n"
@@ -599,7 +741,8 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
              << "                }\n"
              << "                asm volatile(\"tcgen05.fence::before_thread_sync;\" ::: \"memory\");\n"
              << "                __syncwarp();\n"
-             << "                if (lane == 0) pb_mbar_arrive(pb_smem(&acce[buf]));\n"
+             << (pair ? "                if (lane == 0) pb_mbar_arrive_cl(pb_mapa(pb_smem(&acce[buf]), 0u));\n"
+                      : "                if (lane == 0) pb_mbar_arrive(pb_smem(&acce[buf]));\n")
              << "            }\n"
              << (softmax && !softmax_split ? "            // The softmax epilogue exchanges row statistics between the\n"
                            "            // column halves: all 256 drain threads agree on going on.\n"
@@ -809,20 +952,48 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
              // arrival lands after the CTA leaves -- and, after an abort, for
              // every TMA copy issued but not consumed, so nothing writes
              // freed TMEM or shared memory.
-             << "    __syncthreads();\n"
-             << "    if (threadIdx.x == 0) {\n"
-             << "        int dummy = 0;\n"
-             << "        volatile int never = 0;\n"
-             << "        (void)pb_wait(pb_smem(&done_bar), 0u, &never, &dummy, 4);\n"
-             << "        if (abort_flag)\n"
-             << "            for (int g = consumed; g < issued; ++g)\n"
-             << "                (void)pb_wait(pb_smem(&full_bar[g % PB_STAGES]), (pb_u32)(g / PB_STAGES) & 1u, &never, &dummy, 5);\n"
-             << "    }\n"
-             << "    asm volatile(\"tcgen05.fence::before_thread_sync;\" ::: \"memory\");\n"
-             << "    __syncthreads();\n"
-             << "    if (warp == 9) {\n"
+             ;
+        if (!pair)
+            body << "    __syncthreads();\n"
+                 << "    if (threadIdx.x == 0) {\n"
+                 << "        pb_wait_quiet(pb_smem(&done_bar), 0u);\n"
+                 << "        if (abort_flag)\n"
+                 << "            for (int g = consumed; g < issued; ++g)\n"
+                 << "                pb_wait_quiet(pb_smem(&full_bar[g % PB_STAGES]), (pb_u32)(g / PB_STAGES) & 1u);\n"
+                 << "    }\n"
+                 << "    asm volatile(\"tcgen05.fence::before_thread_sync;\" ::: \"memory\");\n"
+                 << "    __syncthreads();\n";
+        else
+            // A pair: once both CTAs have left their roles (no more loads,
+            // arrivals or MMAs issued), the first CTA waits for the MMAs
+            // (which write both CTAs' TMEM and read both CTAs' shared
+            // memory) and, after an abort, for every stage either CTA
+            // loaded but no MMA consumed. The first CTA arms a stage for
+            // both CTAs' bytes when it loads its own half: where only the
+            // second CTA loaded, it arms the barrier for those bytes now;
+            // where only it loaded, it counts the missing half as landed.
+            // Either way the phase completes when the bytes that were
+            // loaded have landed. Then both CTAs free the TMEM.
+            body << "    asm volatile(\"tcgen05.fence::before_thread_sync;\" ::: \"memory\");\n"
+                 << "    pb_cluster_sync();\n"
+                 << "    if (threadIdx.x == 0 && rank == 0) {\n"
+                 << "        pb_wait_quiet(pb_smem(&done_bar), 0u);\n"
+                 << "        if (abort_flag) {\n"
+                 << "            const int peer_issued = pb_peer_int(&issued);\n"
+                 << "            const int hi = issued > peer_issued ? issued : peer_issued;\n"
+                 << "            for (int g = consumed; g < hi; ++g) {\n"
+                 << "                const pb_u32 fb = pb_smem(&full_bar[g % PB_STAGES]);\n"
+                 << "                if (g >= issued) pb_mbar_expect_tx(fb, PB_STAGE_BYTES);\n"
+                 << "                else if (g >= peer_issued) pb_mbar_complete_tx(fb, PB_STAGE_BYTES);\n"
+                 << "                pb_wait_quiet(fb, (pb_u32)(g / PB_STAGES) & 1u);\n"
+                 << "            }\n"
+                 << "        }\n"
+                 << "    }\n"
+                 << "    asm volatile(\"tcgen05.fence::before_thread_sync;\" ::: \"memory\");\n"
+                 << "    pb_cluster_sync();\n";
+        body << "    if (warp == 9) {\n"
              << "        asm volatile(\"tcgen05.fence::after_thread_sync;\" ::: \"memory\");\n"
-             << "        asm volatile(\"tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;\" :: \"r\"(tmem) : \"memory\");\n"
+             << "        asm volatile(\"tcgen05.dealloc.cta_group::" << ctas << ".sync.aligned.b32 %0, 512;\" :: \"r\"(tmem) : \"memory\");\n"
              << "    }\n";
         launch_spec l;
         l.name = "pb_gemm_tc_" + hex8(src.str() + body.str());
@@ -834,9 +1005,12 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
             << (so != nullptr ? "float* __restrict__ lo_out, int* __restrict__ split_flag, " : "")
             << "int* __restrict__ err, const int* __restrict__ nf) {\n" << body.str() << "}\n";
         l.source = src.str();
-        l.schedule = "gemm tcgen05 3xTF32 128x256x16, 4-stage TMA ring (64B swizzle, no multicast), "
-                     "two TMEM accumulators drained per period into fp32 registers, fused epilogue, "
-                     "grouped tile order";
+        l.schedule = pair ? "gemm tcgen05 3xTF32 CTA pairs (cta_group::2) 256x256x16, 6-stage TMA ring (64B swizzle, "
+                            "no multicast), two TMEM accumulators drained per period into fp32 registers, fused "
+                            "epilogue, grouped tile order"
+                          : "gemm tcgen05 3xTF32 128x256x16, 4-stage TMA ring (64B swizzle, no multicast), "
+                            "two TMEM accumulators drained per period into fp32 registers, fused epilogue, "
+                            "grouped tile order";
         // Persistent CTAs (grid = SMs x resident CTAs = 148) when tiles are
         // short (K <= 4096): hiding each tile's epilogue behind the next
         // tile's first period then wins (A/B on one box: config 5's GEMM1,
@@ -845,7 +1019,8 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
         // closer together in L2 (K = 8192 and 16384: 1-3 % fewer cycles than
         // persistent). The kernel is the same; its tile loop runs once.
         const bool persistent = kb_unit * kBK <= 4096;
-        l.grid = {static_cast<uint32_t>(persistent ? std::min<int64_t>(units, 148) : units), 1, 1};
+        l.grid = {static_cast<uint32_t>((persistent ? std::min<int64_t>(units, slots) : units) * ctas), 1, 1};
+        l.cluster_x = static_cast<uint32_t>(ctas);
         if (persistent) {
             l.persistent_units = units;
             l.schedule += ", persistent CTAs (epilogue overlaps the next tile)";
@@ -854,7 +1029,7 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
         if (softmax && !softmax_split)
             l.schedule += ", softmax epilogue (exp(y - tile row max) and per-tile row (max, sum))";
         l.block = {320, 1, 1};
-        l.smem = kStages * (2 * kBM * kBK * 4 + 2 * kBN * kBK * 4) + 1024;
+        l.smem = (pair ? kPairStages : kStages) * (2 * kBM * kBK * 4 + 2 * (kBN / ctas) * kBK * 4) + 1024;
         auto tmap_arg = [&](int temp, int64_t rows, int box_rows) {
             kernel_arg a;
             a.kind = arg_kind::tmap;
@@ -866,8 +1041,8 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
             a.swizzle = 2; // 64B: the box's 16-fp32 inner extent is one swizzle row
             return a;
         };
-        l.args = {tmap_arg(a_hi, M, kBM), tmap_arg(a_lo, M, kBM), tmap_arg(b_hi, N, kBN),
-                  tmap_arg(b_lo, N, kBN)};
+        l.args = {tmap_arg(a_hi, M, kBM), tmap_arg(a_lo, M, kBM), tmap_arg(b_hi, N, kBN / ctas),
+                  tmap_arg(b_lo, N, kBN / ctas)};
         for (const kernel_arg& a : k.leaves) l.args.push_back(a);
         kernel_arg out_arg = temp_arg(out);
         out_arg.elem_offset = out_off;

@@ -258,8 +258,9 @@ namespace porch::detail {
         }
 
         std::shared_ptr<plan> lookup_plan(const graph& g) {
-            // Plans built under the GEMM test hook never serve normal calls.
-            const std::string key = test_gemm_stall() ? g.key + "|test-stall" : g.key;
+            // Plans built under the GEMM test hook never serve normal calls,
+            // nor plans of another GEMM form.
+            const std::string key = g.key + gemm_form_key() + (test_gemm_stall() ? "|test-stall" : "");
             plan_cache& c = plans();
             {
                 std::scoped_lock lock{c.mutex};
@@ -520,8 +521,18 @@ namespace porch::detail {
                                          l.smem, &per_sm));
                     check(pbrt_device_attribute(device, 16 /* multiprocessor count */, &sms));
                     if (l.persistent_per_sm > 0) per_sm = std::min(per_sm, l.persistent_per_sm);
-                    const int64_t fit = std::max<int64_t>(1, int64_t{per_sm} * sms);
-                    pgrid = static_cast<uint32_t>(std::min<int64_t>(l.persistent_units, fit));
+                    int64_t fit = std::max<int64_t>(1, int64_t{per_sm} * sms);
+                    // Work units of a clustered kernel are clusters of
+                    // cluster_x CTAs, as many as can be resident at once.
+                    const int64_t cx = std::max<uint32_t>(1, l.cluster_x);
+                    if (cx > 1) {
+                        int clusters = 0;
+                        check(pbrt_max_active_clusters(device, fn,
+                                                       static_cast<int>(l.block[0] * l.block[1] * l.block[2]),
+                                                       l.smem, l.cluster_x, &clusters));
+                        fit = std::max<int64_t>(1, std::min<int64_t>(clusters, fit / cx));
+                    }
+                    pgrid = static_cast<uint32_t>(cx * std::min<int64_t>(l.persistent_units, fit));
                 }
                 if (slot) {
                     l.per_device->persistent_grid[device].store(pgrid, std::memory_order_relaxed);

@@ -108,8 +108,9 @@ namespace porch::detail {
         std::vector<kernel_arg> args;
         // Persistent kernels loop over `persistent_units` work units with a
         // grid-stride loop; their grid is fixed on first launch per device to
-        // exactly the CTAs that fit at once (SMs x occupancy), so no CTA waits
-        // for a second wave. 0 = launch `grid` as given.
+        // exactly the CTAs that fit at once (SMs x occupancy; for a clustered
+        // kernel, whose units are clusters, the clusters that fit), so no CTA
+        // waits for a second wave. 0 = launch `grid` as given.
         int64_t persistent_units = 0;
         // With persistent_units: at most this many CTAs per SM (0: as many
         // as fit), e.g. to keep the rows in flight inside L2.

@@ -116,6 +116,8 @@ dl_handle open_first(std::initializer_list<const char*> names) {
       CUresult (*)(int*, CUfunction_attribute, CUfunction))                  \
     X(cuOccupancyMaxActiveBlocksPerMultiprocessor,                           \
       CUresult (*)(int*, CUfunction, int, size_t))                           \
+    X(cuOccupancyMaxActiveClusters,                                          \
+      CUresult (*)(int*, CUfunction, const CUlaunchConfig*))                 \
     X(cuLaunchKernelEx, CUresult (*)(const CUlaunchConfig*, CUfunction,      \
                                      void**, void**))                        \
     X(cuTensorMapEncodeTiled,                                                \
@@ -1146,6 +1148,33 @@ int pbrt_occupancy(int device, pbrt_function function, int block_threads, size_t
                      blocks_per_sm, reinterpret_cast<CUfunction>(function), block_threads,
                      dynamic_smem),
                  "cuOccupancyMaxActiveBlocksPerMultiprocessor");
+}
+
+int pbrt_max_active_clusters(int device, pbrt_function function, int block_threads, size_t dynamic_smem,
+                             unsigned cluster_x, int* clusters) {
+    if (function == nullptr || clusters == nullptr || block_threads <= 0 || cluster_x == 0)
+        return fail(PBRT_ERR_INVALID, "invalid cluster occupancy query");
+    environment* env = nullptr;
+    int s = use_device(device, env);
+    if (s != PBRT_OK) return s;
+    CUlaunchConfig config{};
+    config.gridDimX = cluster_x;
+    config.gridDimY = 1;
+    config.gridDimZ = 1;
+    config.blockDimX = static_cast<unsigned>(block_threads);
+    config.blockDimY = 1;
+    config.blockDimZ = 1;
+    config.sharedMemBytes = static_cast<unsigned>(dynamic_smem);
+    CUlaunchAttribute attribute{};
+    attribute.id = CU_LAUNCH_ATTRIBUTE_CLUSTER_DIMENSION;
+    attribute.value.clusterDim.x = cluster_x;
+    attribute.value.clusterDim.y = 1;
+    attribute.value.clusterDim.z = 1;
+    config.attrs = &attribute;
+    config.numAttrs = 1;
+    return check(*env,
+                 env->cu.cuOccupancyMaxActiveClusters(clusters, reinterpret_cast<CUfunction>(function), &config),
+                 "cuOccupancyMaxActiveClusters");
 }
 
 int pbrt_launch(int device, pbrt_function function, const uint32_t* grid,
