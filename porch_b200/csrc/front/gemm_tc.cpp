@@ -16,14 +16,16 @@
 //     one contiguous along M or N (B as stored, a transposed A) the tile
 //     transpose.
 //  3. pb_gemm_tc:         one 128x256 output tile per CTA, 320 threads.
-//     warp 0 lane 0 issues TMA loads (64B swizzle, BK = 16 fp32 = one 64-byte
+//     warp 8 lane 0 issues TMA loads (64B swizzle, BK = 16 fp32 = one 64-byte
 //     swizzle row) into a 4-stage ring of {Ahi, Alo, Bhi, Blo} tiles (48 KB
 //     per stage, 192 KB in all: three stages are in flight while the MMAs
 //     read the fourth, about 1.8 us of tensor work, enough to cover TMA
 //     latency from L2 or HBM); warp 9
 //     allocates 512 TMEM columns and its lane 0 issues tcgen05.mma
 //     (kind::tf32, M=128, N=256, K=8; 3 products x 2 k-steps per stage),
-//     committing each stage back to the producer.
+//     committing each stage back to the producer. With PB_PAIR (opt-in) a
+//     cluster of two CTAs computes a 256x256 tile with cta_group::2 MMAs
+//     (see the PB_PAIR notes in the device source).
 //     Accumulation: the tensor core's fp32 accumulator loses low-order bits
 //     on every MMA it adds into, so one accumulator over all of K (1024
 //     k-steps at K = 8192) drifts ~6e-5 relative -- five times an fp32 FMA

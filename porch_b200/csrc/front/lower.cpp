@@ -167,18 +167,21 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
         return match_softmax(id, x, axis) && axis + 1 == n.shape.size();
     }
 
-    // Finds the single matmul whose output feeds `id` through elementwise
-    // ops only (the fusable epilogue). Returns -1 when there is none.
+    // Finds the single matmul (rank 2) or batched matmul (rank 3) whose
+    // output feeds `id` through elementwise ops only (the fusable
+    // epilogue). Returns -1 when there is none.
     int lowerer::match_gemm(int id) const {
         const gnode& root = g_.nodes[static_cast<size_t>(id)];
-        if (root.is_scalar || root.shape.size() != 2) return -1;
+        if (root.is_scalar || (root.shape.size() != 2 && root.shape.size() != 3)) return -1;
+        const expr_kind product = root.shape.size() == 2 ? expr_kind::matmul : expr_kind::batched_matmul;
         int found = -1;
         bool ambiguous = false;
         std::function<void(int)> walk = [&](int v) {
             const gnode& n = g_.nodes[static_cast<size_t>(v)];
             switch (n.kind) {
                 case expr_kind::matmul:
-                    if (n.shape == root.shape) {
+                case expr_kind::batched_matmul:
+                    if (n.kind == product && n.shape == root.shape) {
                         if (found >= 0 && found != v) ambiguous = true;
                         found = v;
                     }
@@ -228,7 +231,7 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
         } else if (n.kind == expr_kind::sum || n.kind == expr_kind::max) {
             t = emit_reduce(id);
         } else if (n.kind == expr_kind::batched_matmul) {
-            t = emit_batched_gemm(id);
+            t = emit_batched_gemm(id, id);
         } else if ((n.kind == expr_kind::reshape || n.kind == expr_kind::unsqueeze) &&
                    g_.nodes[static_cast<size_t>(n.a)].kind != expr_kind::input) {
             // A contiguous result holds the same bytes under any shape:
@@ -237,7 +240,7 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
             t = materialize(n.a);
         } else {
             const int mm = match_gemm(id);
-            if (mm >= 0) t = emit_gemm(id, mm);
+            if (mm >= 0) t = n.shape.size() == 3 ? emit_batched_gemm(id, mm) : emit_gemm(id, mm);
             if (t < 0) t = emit_elementwise(id);
         }
         done_[id] = t;
@@ -2249,25 +2252,64 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
         return true;
     }
 
-    int lowerer::emit_batched_gemm(int id) {
-        const gnode& n = g_.nodes[static_cast<size_t>(id)];
+    int lowerer::emit_batched_gemm(int id, int mm) {
+        const gnode& n = g_.nodes[static_cast<size_t>(mm)];
         const int64_t Bt = n.shape[0], M = n.shape[1], N = n.shape[2];
         const int64_t K = g_.nodes[static_cast<size_t>(n.a)].shape[2];
+        kernel k;
+        box b;
+        // Per epilogue leaf: elements between consecutive batches.
+        std::vector<int64_t> batch_stride;
+        if (id == mm) {
+            // The plain product as the epilogue: one box over [M, N]
+            // holding the accumulator.
+            b.lo = {0, 0};
+            b.hi = {M, N};
+            vnode acc;
+            acc.kind = vnode::op::acc;
+            b.nodes.push_back(acc);
+            b.root = 0;
+        } else {
+            // The elementwise graph over [B, M, N] as one box, its leaves'
+            // batch coordinate moved into per-batch pointer offsets: each
+            // batch's GEMM then runs the same [M, N] epilogue. Leaves whose
+            // batch stride would misalign their float4 loads, or a buffer
+            // read at two batch strides, are not fused.
+            if (!tensor_core_gemm(M, N, K)) return -1;
+            std::vector<box> boxes;
+            try {
+                boxes = build_boxes(k, id, g_.nodes[static_cast<size_t>(id)].shape, mm);
+            } catch (const not_fusable&) {
+                return -1;
+            } catch (const not_affine&) {
+                return -1;
+            }
+            if (boxes.size() != 1) return -1;
+            b = std::move(boxes[0]);
+            batch_stride.assign(k.leaves.size(), -1);
+            for (vnode& v : b.nodes) {
+                if (v.kind != vnode::op::load) continue;
+                const int64_t s0 = v.map.st[0];
+                int64_t& bs = batch_stride[static_cast<size_t>(v.buffer)];
+                if (s0 < 0 || s0 % 4 != 0 || (bs >= 0 && bs != s0)) return -1;
+                bs = s0;
+                v.map.st = {v.map.st[1], v.map.st[2]};
+            }
+            b.lo = {0, 0};
+            b.hi = {M, N};
+        }
         const kernel_arg A = as_buffer(n.a); // contiguous [Bt, M, K]
         const kernel_arg B = as_buffer(n.b); // contiguous [Bt, K, N]
         const int out = new_temp(static_cast<size_t>(Bt * M * N) * sizeof(float));
         if (Bt == 0 || M == 0 || N == 0) return out;
         rank_ = 2;
-        // The plain product as the epilogue: one box over [M, N] holding
-        // the accumulator.
-        box b;
-        b.lo = {0, 0};
-        b.hi = {M, N};
-        vnode acc;
-        acc.kind = vnode::op::acc;
-        b.nodes.push_back(acc);
-        b.root = 0;
-        kernel k;
+        // The epilogue's leaves as batch t reads them.
+        auto leaves_at = [&](int64_t t) {
+            kernel kt = k;
+            for (size_t i = 0; i < batch_stride.size(); ++i)
+                if (batch_stride[i] > 0) kt.leaves[i].elem_offset += batch_stride[i] * t;
+            return kt;
+        };
         auto at = [](const kernel_arg& base, int64_t off, int64_t s0) {
             gemm_operand o;
             o.arg = base;
@@ -2283,14 +2325,15 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
         shared.reused = true;
         for (int64_t t = 0; t < Bt; ++t) {
             const gemm_operand ga = at(A, t * M * K, K), gb = at(B, t * K * N, N);
+            kernel kt = leaves_at(t);
             int nonfinite = -1;
-            if (emit_gemm_tc(id, b, k, ga, gb, M, N, K, &nonfinite, nullptr, out, t * M * N, &shared) < 0) {
-                if (t != 0) throw std::logic_error("batched GEMM eligibility changed between batches");
+            if (emit_gemm_tc(id, b, kt, ga, gb, M, N, K, &nonfinite, nullptr, out, t * M * N, &shared) < 0) {
+                if (t != 0 || id != mm) throw std::logic_error("batched GEMM eligibility changed between batches");
                 // CUDA cores: every batch in one launch (blockIdx.y).
                 emit_gemm_simt(b, k, at(A, 0, K), at(B, 0, N), M, N, K, out, -1, 0, Bt);
                 return out;
             }
-            emit_gemm_simt(b, k, ga, gb, M, N, K, out, nonfinite, t * M * N);
+            emit_gemm_simt(b, kt, ga, gb, M, N, K, out, nonfinite, t * M * N);
         }
         return out;
     }

@@ -168,9 +168,14 @@ namespace porch::detail {
         // nothing else, lowers it with a split-output epilogue into `t`'s A
         // temps and returns true; `op` then reads those halves.
         bool presplit_operand(int a, int64_t M, int64_t N, int64_t K, gemm_temps& t, gemm_operand& op);
-        // Internal batched matmul: a tensor-core GEMM per batch, or one
-        // CUDA-core launch over every batch.
-        int emit_batched_gemm(int id);
+        // Internal batched matmul [B, M, K] @ [B, K, N] at `mm`, with the
+        // elementwise graph `id` (rank 3, the product as one leaf; id == mm
+        // for the bare product) as the epilogue: a tensor-core GEMM per batch
+        // (pointer offsets for operands, output and epilogue leaves), or one
+        // CUDA-core launch over every batch for a bare product. Returns -1
+        // when the epilogue cannot be fused (the caller then realises the
+        // product on its own).
+        int emit_batched_gemm(int id, int mm);
         // tcgen05 3xTF32 path; returns -1 when the shape is not eligible. On
         // success *nonfinite receives a temp whose first int is set when an
         // operand holds Inf or NaN (the tensor-core result is then skipped).
