@@ -23,9 +23,10 @@
 //     latency from L2 or HBM); warp 9
 //     allocates 512 TMEM columns and its lane 0 issues tcgen05.mma
 //     (kind::tf32, M=128, N=256, K=8; 3 products x 2 k-steps per stage),
-//     committing each stage back to the producer. With PB_PAIR (opt-in) a
-//     cluster of two CTAs computes a 256x256 tile with cta_group::2 MMAs
-//     (see the PB_PAIR notes in the device source).
+//     committing each stage back to the producer. With PB_PAIR (the
+//     default wherever M has two or more 128-row tiles) a cluster of two
+//     CTAs computes a 256x256 tile with cta_group::2 MMAs over 32-wide
+//     k-blocks (see the PB_PAIR notes in the device source).
 //     Accumulation: the tensor core's fp32 accumulator loses low-order bits
 //     on every MMA it adds into, so one accumulator over all of K (1024
 //     k-steps at K = 8192) drifts ~6e-5 relative -- five times an fp32 FMA
@@ -56,22 +57,30 @@ namespace porch::detail {
         constexpr int kBN = 256;
         constexpr int kBK = 16;
         constexpr int kStages = 4;
-        constexpr int kPairStages = 6;
+        constexpr int kPairStages = 3;
 
         const char* gemm_device_source() {
             return R"PB(
 #define PB_BM 128
 #define PB_BN 256
-#define PB_BK 16
 // PB_PAIR: a cluster of two CTAs (on one SM pair) computes a 256 x 256
 // tile with cta_group::2 MMAs: each CTA holds its own 128 rows of A and
 // half (128 rows of N) of B, and its own 128 x 256 accumulator in TMEM.
+// Its k-blocks are 32 fp32 wide (one 128-byte swizzle row; 8-row groups
+// 1024 B apart) in 3 stages of 64 KB; one CTA per tile uses 16-wide
+// k-blocks (64-byte swizzle, 512 B groups) in 4 stages of 48 KB.
 #ifdef PB_PAIR
 #define PB_CTAS 2
-#define PB_STAGES 6
+#define PB_BK 32
+#define PB_STAGES 3
+#define PB_SWIZZLE 2
+#define PB_SBO 1024
 #else
 #define PB_CTAS 1
+#define PB_BK 16
 #define PB_STAGES 4
+#define PB_SWIZZLE 4
+#define PB_SBO 512
 #endif
 #define PB_BNH (PB_BN / PB_CTAS)
 #define PB_TILE_A_BYTES (PB_BM * PB_BK * 4)
@@ -195,17 +204,18 @@ static __device__ __forceinline__ void pb_tma_load(pb_u32 dst, const pb_tmap* ma
 #endif
 }
 
-// tcgen05 shared-memory matrix descriptor: K-major, 64B swizzle (one
-// 64-byte row = 16 fp32 of K per tile row), 8-row groups 8 x 64 = 512 B
-// apart (SBO), start address in 16-byte units. Tiles start on 1024-byte
-// boundaries, so the swizzle phase (base offset field) is 0.
+// tcgen05 shared-memory matrix descriptor: K-major, one swizzle row per
+// tile row (64 bytes = 16 fp32 of K, or 128 bytes = 32 with PB_PAIR), 8-row
+// groups PB_SBO bytes apart, start address in 16-byte units (a k-step of 8
+// fp32 advances it by 32 bytes within the swizzle row). Tiles start on
+// 1024-byte boundaries, so the swizzle phase (base offset field) is 0.
 static __device__ __forceinline__ pb_u64 pb_desc(pb_u32 addr) {
     pb_u64 d = 0;
     d |= (pb_u64)((addr & 0x3FFFFu) >> 4);
     d |= (pb_u64)1 << 16;             // leading byte offset (unused for swizzled K-major)
-    d |= (pb_u64)(512 >> 4) << 32;    // stride byte offset
+    d |= (pb_u64)(PB_SBO >> 4) << 32; // stride byte offset
     d |= (pb_u64)1 << 46;             // fixed 0b001
-    d |= (pb_u64)4 << 61;             // 64-byte swizzle
+    d |= (pb_u64)PB_SWIZZLE << 61;    // 64- or 128-byte swizzle
     return d;
 }
 
@@ -301,7 +311,7 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
 
         bool gemm_pairs_enabled() {
             const char* v = std::getenv("PORCH_B200_GEMM");
-            return v != nullptr && std::string{v} == "pair";
+            return v == nullptr || std::string{v} != "single";
         }
 
     } // namespace
@@ -486,16 +496,21 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
         // ---- 3. tcgen05 GEMM + epilogue -------------------------------------
         std::vector<int> order;
         const std::string efn = emit_expr_function(b, "0", order);
-        // CTA pairs (cta_group::2, 256 x 256 tiles), on request
-        // (PORCH_B200_GEMM=pair), wherever there are at least two 128-row
-        // tiles and pairing leaves no more than a sliver of a pair idle.
-        // Each CTA then loads half of B for the same MMAs, and the pair
-        // draws less power (config 5: about 40 MHz higher clock under the
-        // 1 kW cap), but its tensor pipe is busy a smaller share of the
-        // cycles (ncu at 4096 rows: 78 / 77 % against 82 / 87 % for the
-        // two GEMMs): measured 216-220 TFLOP/s against 221-222 for one CTA
-        // per tile, so one CTA per 128 x 256 tile stays the default. The
-        // results are bit-identical either way.
+        // CTA pairs (cta_group::2, 256 x 256 tiles) wherever there are at
+        // least two 128-row tiles and pairing leaves no more than a sliver
+        // of a pair idle; one CTA per 128 x 256 tile otherwise (or with
+        // PORCH_B200_GEMM=single). Each CTA of a pair loads half of B for
+        // the same MMAs (a third fewer bytes from L2 and through the tensor
+        // core's shared-memory reads), with 32-wide k-blocks in a 128-byte
+        // swizzle (3 stages of 64 KB): half the barrier round trips between
+        // the two SMs per MMA. Measured on config 5 at the same clock:
+        // 244-245 TFLOP/s against 222-223 for one CTA per tile. (With the
+        // one-CTA form's 16-wide k-blocks in 6 stages the pair ran at
+        // 216-220: the per-stage handshakes between the SMs left the tensor
+        // pipe idle.) The results are bit-identical either way, except
+        // under split-K when a part holds an odd number of 16-wide k-blocks
+        // (a pair's parts are whole 32-wide k-blocks, so its split points
+        // move by 16 of K).
         const int64_t tiles_m1 = (M + kBM - 1) / kBM;
         const bool pair = gemm_pairs_enabled() && tiles_m1 >= 2 && (tiles_m1 % 2 == 0 || tiles_m1 >= 8);
         const int ctas = pair ? 2 : 1;
@@ -566,7 +581,10 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
             split = pick;
         }
         const bool softmax_split = softmax && split > 1;
-        const int64_t kb_unit = (raw_kb + split - 1) / split;
+        int64_t kb_unit = (raw_kb + split - 1) / split;
+        // A pair's k-blocks are 32 wide: whole ones per unit (past K the
+        // loads read zeros). The periods keep the same length in K.
+        if (pair) kb_unit = (kb_unit + 1) / 2 * 2;
         const int64_t units = tiles * split;
         const int part = split > 1 ? new_temp(static_cast<size_t>(split * M * ((N + 3) / 4 * 4)) * 4) : -1;
         // With split-K the combine does the whole softmax: no row partials.
@@ -575,7 +593,7 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
         std::ostringstream src;
         src << kernel_prelude() << (test_gemm_stall() ? "#define PB_TEST_STALL 1\n" : "")
             << (pair ? "#define PB_PAIR 1\n" : "") << "#define PB_PERIOD "
-            << period << "\n#define PB_SPLIT " << split << "\n"
+            << (pair ? period / 2 : period) << "\n#define PB_SPLIT " << split << "\n"
             << gemm_device_source() << efn;
         // Tile t -> output origin, tiles ordered in groups of group_m M-tiles
         // that sweep N (consecutive tiles, run at the same time by the
@@ -635,7 +653,7 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
                       : "    __syncthreads();\n")
              << "    asm volatile(\"tcgen05.fence::after_thread_sync;\" ::: \"memory\");\n"
              << "    const pb_u32 tmem = tmem_slot;\n"
-             << "    const int num_kb = " << kb_unit << ";  // k-blocks per work unit\n"
+             << "    const int num_kb = " << (pair ? kb_unit / 2 : kb_unit) << ";  // k-blocks per work unit\n"
              << "    const int periods = (num_kb + PB_PERIOD - 1) / PB_PERIOD;  // the last may be partial\n"
              << "    if (warp == 8) {\n"
              << "        if (lane == 0) {\n"
@@ -1007,7 +1025,7 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
             << (so != nullptr ? "float* __restrict__ lo_out, int* __restrict__ split_flag, " : "")
             << "int* __restrict__ err, const int* __restrict__ nf) {\n" << body.str() << "}\n";
         l.source = src.str();
-        l.schedule = pair ? "gemm tcgen05 3xTF32 CTA pairs (cta_group::2) 256x256x16, 6-stage TMA ring (64B swizzle, "
+        l.schedule = pair ? "gemm tcgen05 3xTF32 CTA pairs (cta_group::2) 256x256x32, 3-stage TMA ring (128B swizzle, "
                             "no multicast), two TMEM accumulators drained per period into fp32 registers, fused "
                             "epilogue, grouped tile order"
                           : "gemm tcgen05 3xTF32 128x256x16, 4-stage TMA ring (64B swizzle, no multicast), "
@@ -1031,7 +1049,8 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
         if (softmax && !softmax_split)
             l.schedule += ", softmax epilogue (exp(y - tile row max) and per-tile row (max, sum))";
         l.block = {320, 1, 1};
-        l.smem = (pair ? kPairStages : kStages) * (2 * kBM * kBK * 4 + 2 * (kBN / ctas) * kBK * 4) + 1024;
+        const int bk = pair ? 2 * kBK : kBK;
+        l.smem = (pair ? kPairStages : kStages) * (2 * kBM * bk * 4 + 2 * (kBN / ctas) * bk * 4) + 1024;
         auto tmap_arg = [&](int temp, int64_t rows, int box_rows) {
             kernel_arg a;
             a.kind = arg_kind::tmap;
@@ -1039,8 +1058,8 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
             a.value = static_cast<uint64_t>(rows);
             a.cols = Kp;
             a.box_rows = box_rows;
-            a.box_cols = kBK;
-            a.swizzle = 2; // 64B: the box's 16-fp32 inner extent is one swizzle row
+            a.box_cols = pair ? 2 * kBK : kBK;
+            a.swizzle = pair ? 3 : 2; // 128B / 64B: the box's inner extent is one swizzle row
             return a;
         };
         l.args = {tmap_arg(a_hi, M, kBM), tmap_arg(a_lo, M, kBM), tmap_arg(b_hi, N, kBN / ctas),

@@ -60,8 +60,8 @@ namespace porch::detail {
     // Whether an [M, K] @ [K, N] product runs on the tensor cores.
     bool tensor_core_gemm(int64_t M, int64_t N, int64_t K);
     bool test_gemm_stall();
-    // PORCH_B200_GEMM ("simt": no tensor-core GEMMs; "pair": CTA pairs,
-    // cta_group::2, instead of one CTA per tile), as a suffix of the plan key.
+    // PORCH_B200_GEMM ("simt": no tensor-core GEMMs; "single": one CTA per
+    // tile instead of CTA pairs, cta_group::2), as a suffix of the plan key.
     std::string gemm_form_key();
 
     // A matmul operand [rows, cols] read in place: element (i, j) at

@@ -1,8 +1,9 @@
-"""CTA pairs (PORCH_B200_GEMM=pair): the tensor-core GEMM runs a 256 x 256
-tile on a cluster of two CTAs (tcgen05.mma.cta_group::2, each CTA holding
-its own 128 rows of A and half of B) wherever there are at least two
+"""CTA pairs (the default): the tensor-core GEMM runs a 256 x 256 tile on a
+cluster of two CTAs (tcgen05.mma.cta_group::2, each CTA holding its own 128
+rows of A and half of B, 32-wide k-blocks) wherever there are at least two
 128-row tiles. The products and their accumulation order are those of the
-default one-CTA form, so every epilogue gives the same bits either way: plain and fused
+one-CTA form (PORCH_B200_GEMM=single, 16-wide k-blocks, the same periods in
+K), so every epilogue gives the same bits either way: plain and fused
 epilogues, ragged edges (a pair whose second half lies past M), the
 softmax epilogue, the split-output epilogue of an MLP, split-K and the
 persistent schedule. Also checked against fp64 within the sqrt(K)-
@@ -20,10 +21,10 @@ pytestmark = pytest.mark.gpu
 
 
 def _both(api, build):
-    """Realise build() with CTA pairs, then with one CTA per tile (the
-    default); returns both results and both plan descriptions."""
+    """Realise build() with CTA pairs (the default), then with one CTA per
+    tile; returns both results and both plan descriptions."""
     out = []
-    for form in ("pair", None):
+    for form in (None, "single"):
         if form is None:
             os.environ.pop("PORCH_B200_GEMM", None)
         else:
