@@ -95,3 +95,23 @@ def test_pairs_match_single_through_the_softmax_epilogue(gpu):
     assert "CTA pairs" in dp and "softmax epilogue" in dp, dp
     assert "CTA pairs" not in ds, ds
     assert_bitwise(pp, ps, "softmax epilogue: pairs vs single")
+
+
+def test_pairs_with_split_parts_of_odd_length(gpu):
+    """256 x 1040 x 512: split-K x4 over 65 k-blocks of 16, parts of 17 for
+    one CTA per tile; a pair's parts are whole 32-wide k-blocks (18 of 16,
+    the last part reading zeros past K). The split points differ, so the
+    two forms are compared with fp64, each within the sqrt(K)-normalised
+    bar, not bit for bit."""
+    api = gpu
+    m, k, n = 256, 1040, 512
+    rng = np.random.default_rng(81)
+    a = rng.uniform(-1, 1, (m, k)).astype(np.float32)
+    b = rng.uniform(-1, 1, (k, n)).astype(np.float32)
+    A, B = api.tensor([m, k], a), api.tensor([k, n], b)
+    (zp, dp), (zs, ds) = _both(api, lambda: api.matmul(A, B))
+    assert "CTA pairs" in dp and "split-K x4" in dp, dp
+    assert "CTA pairs" not in ds and "split-K x4" in ds, ds
+    ref = a.astype(np.float64) @ b.astype(np.float64)
+    assert matmul_error(zp.reshape(m, n), ref, k) <= MATMUL_TOL
+    assert matmul_error(zs.reshape(m, n), ref, k) <= MATMUL_TOL
