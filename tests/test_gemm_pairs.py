@@ -44,6 +44,8 @@ def _both(api, build):
     (384, 2048, 512, False),     # three tiles: one CTA per tile
     (2048, 4096, 2048, True),    # persistent pairs (K <= 4096)
     (256, 8192, 1024, True),     # few pair tiles: split-K
+    (2048, 1024, 100, True),     # N = 100: the second CTA's half of B lies past N (zeros)
+    (512, 1024, 4099, True),     # N not a multiple of 4: scalar epilogue loads and stores
 ])
 def test_pairs_match_single_cta_tiles(gpu, m, k, n, paired):
     api = gpu
