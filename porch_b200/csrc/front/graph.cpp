@@ -663,8 +663,9 @@ namespace porch::detail {
         os << "temps=" << p->temp_bytes.size() << " result=t" << p->result_temp << "\n";
         for (const launch_spec& l : p->launches) {
             os << "kernel " << l.name << " grid=" << l.grid[0] << "x" << l.grid[1] << "x"
-               << l.grid[2] << " block=" << l.block[0] << " smem=" << l.smem << " : "
-               << l.schedule << "\n";
+               << l.grid[2] << " block=" << l.block[0] << " smem=" << l.smem;
+            if (l.cluster_x > 1) os << " cluster=" << l.cluster_x;
+            os << " : " << l.schedule << "\n";
             if (with_source) os << l.source << "\n";
         }
         return os.str();
