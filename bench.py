@@ -314,6 +314,12 @@ def measure(api, workload: str, args, rank, world, local, dist, cpu_seconds: flo
         for k in ACTIVATIONS.get(workload, []):
             t[k].device_data()
     graphs = [api.config_graph(workload, t) for t in sets]
+    # The tensor-core GEMM form the plan chose (the plan's own description).
+    plan_text = api.describe(graphs[0])
+    gemm_form = None
+    if "pb_gemm_tc_" in plan_text:
+        gemm_form = ("CTA pairs: tcgen05.mma.cta_group::2, 256x256 tiles on 2-CTA clusters, 32-wide k-blocks"
+                     if "CTA pairs" in plan_text else "one CTA per 128x256 tile, 16-wide k-blocks")
 
     # Config 5 gathers its output P whole on every rank (one ncclAllGather
     # over NVLink per step); configs 3a/3b keep their row blocks where they
@@ -539,6 +545,7 @@ def measure(api, workload: str, args, rank, world, local, dist, cpu_seconds: flo
         "dtype": "f32", "data": "synthetic (seeded; distributions as the baseline config)",
         "config": config,
         "setup": {"l2": f"inputs rotated over {n_sets} device-resident sets, each larger than L2",
+                  "gemm": gemm_form,
                   "weights": (f"{', '.join(k for k in KEYS[workload] if k not in ACTIVATIONS[workload] and k[0] in 'wb' and len(shape_of(workload, k)) == 2)} "
                               "realised once and keep their 3xTF32 split; the activations' device pointers are handed "
                               "out (as a data loader writing each batch would), so their split runs every step"
@@ -584,8 +591,8 @@ def run_ours(args, rank, world, local, dist):
             r = measure(api, name, args, rank, world, local, dist,
                         None if args.no_cpu_baseline else 5.0, two_threads=False)
             extra[name] = {k: r[k] for k in ("metric", "value", "unit", "ms_per_step", "scaling", "config",
-                                              "e2e", "gpu_launches", "roofline", "cpu_baseline", "clocks",
-                                              "kernels")}
+                                              "setup", "e2e", "gpu_launches", "roofline", "cpu_baseline",
+                                              "clocks", "kernels")}
         api.empty_cache(local)
     if rank == 0:
         if extra:
