@@ -332,17 +332,24 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
     int lowerer::emit_gemm_tc(int id, const box& b, kernel& k, const gemm_operand& A,
                               const gemm_operand& B, int64_t M, int64_t N, int64_t K, int* nonfinite,
                               int* row_partials, int out_temp, int64_t out_off, gemm_temps* shared,
-                              const split_output* so) {
+                              const split_output* so, const gemm_batches* batches) {
         const bool softmax = row_partials != nullptr;
         if (so != nullptr && (softmax || N % 32 != 0 || so->kp != N)) return -1;
         (void)id;
-        if (!tensor_core_gemm(M, N, K)) return -1;
+        // Grouped batches (plain or fused elementwise epilogues only): the
+        // tensor cores pay off on the total work, and the stacked operand
+        // rows (nb * M, nb * N) must stay within a tensor map's range.
+        const int64_t nb = batches != nullptr ? batches->count : 1;
+        if (nb > 1 && (softmax || so != nullptr || out_off != 0 || N == 1 || nb * M > (int64_t{1} << 30) ||
+                       nb * N > (int64_t{1} << 30) || !tensor_core_gemm(nb * M, N, K)))
+            return -1;
+        if (nb == 1 && !tensor_core_gemm(M, N, K)) return -1;
         // Any M, N, K. The K-major hi/lo arrays have padded rows (16-byte
         // TMA strides whatever K is); edge tiles read zeros past M, N and K
         // (TMA out-of-bounds fill) and mask their stores; when N is not a
         // multiple of 4 the epilogue loads and stores one float at a time.
         if (M < 1 || N < 1 || K < 1) return -1;
-        if (M * N * K < (int64_t{1} << 27)) return -1;
+        if (nb * M * N * K < (int64_t{1} << 27)) return -1;
         if (M > (int64_t{1} << 30) || N > (int64_t{1} << 30) || K > (int64_t{1} << 30)) return -1;
         rank_ = 2;
 
@@ -355,10 +362,10 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
         auto need = [&](int& t, size_t bytes) {
             if (t < 0) t = new_temp(bytes);
         };
-        need(tt.a_hi, static_cast<size_t>(M * Kp) * 4);
-        need(tt.a_lo, static_cast<size_t>(M * Kp) * 4);
-        need(tt.b_hi, static_cast<size_t>(N * Kp) * 4);
-        need(tt.b_lo, static_cast<size_t>(N * Kp) * 4);
+        need(tt.a_hi, static_cast<size_t>(nb * M * Kp) * 4);
+        need(tt.a_lo, static_cast<size_t>(nb * M * Kp) * 4);
+        need(tt.b_hi, static_cast<size_t>(nb * N * Kp) * 4);
+        need(tt.b_lo, static_cast<size_t>(nb * N * Kp) * 4);
         need(tt.nf, 256);
         need(tt.fa, 256);
         need(tt.fb, 256);
@@ -403,8 +410,10 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
         // stored): 64 x 64 tiles through shared memory so both the loads
         // and the K-major stores stay coalesced; otherwise the same tiles
         // with strided loads.
+        // zb > 1: zb operands zx elements apart (blockIdx.z), their halves
+        // stacked R rows apart (the transposing split of batched B).
         auto emit_split = [&](const std::string& what, const gemm_operand& X, int64_t R, int64_t sr, int64_t sk,
-                              int hi_t, int lo_t, int flag_t) {
+                              int hi_t, int lo_t, int flag_t, int64_t zb = 1, int64_t zx = 0) {
             std::ostringstream src;
             src << kernel_prelude() << gemm_device_source();
             launch_spec l;
@@ -445,6 +454,10 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
                 // stores walk k of the K-major output.
                 src << "extern \"C\" __global__ void __launch_bounds__(256) pb_split_transpose(const float* __restrict__ x, "
                        "float* __restrict__ hi, float* __restrict__ lo, int* __restrict__ nf) {\n"
+                    << (zb > 1 ? "    x += (pb_u64)blockIdx.z * " + std::to_string(zx) + "ull;\n    hi += (pb_u64)blockIdx.z * " +
+                                     std::to_string(R * Kp) + "ull;\n    lo += (pb_u64)blockIdx.z * " +
+                                     std::to_string(R * Kp) + "ull;\n"
+                               : std::string{})
                     << "    __shared__ float t[64][65];\n"
                     << "    const pb_u64 k0 = (pb_u64)blockIdx.y * 64u, n0 = (pb_u64)blockIdx.x * 64u;\n"
                     << "    #pragma unroll\n    for (int u = 0; u < 16; ++u) {\n"
@@ -463,23 +476,27 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
                     << "        hi[o] = h;\n        lo[o] = pb_tf32_rn(v - h);\n    }\n}\n";
                 l.name = "pb_split_transpose";
                 l.schedule = "3xTF32 split of " + what + " with transpose to K-major";
-                l.grid = {static_cast<uint32_t>((R + 63) / 64), static_cast<uint32_t>((Kp + 63) / 64), 1};
+                l.grid = {static_cast<uint32_t>((R + 63) / 64), static_cast<uint32_t>((Kp + 63) / 64),
+                          static_cast<uint32_t>(zb)};
             }
             l.source = src.str();
             l.args = {X.arg, temp_arg(hi_t), temp_arg(lo_t), temp_arg(flag_t)};
-            if (X.arg.kind == arg_kind::slot && !tt.reused) {
+            if (X.arg.kind == arg_kind::slot) {
                 // A realised input: its storage may keep this split.
                 l.cache_slot = X.arg.index;
                 l.cache_key = "split R" + std::to_string(R) + " K" + std::to_string(K) + " Kp" + std::to_string(Kp) +
                               " off" + std::to_string(X.off + X.arg.elem_offset) + " sr" + std::to_string(sr) +
-                              " sk" + std::to_string(sk);
+                              " sk" + std::to_string(sk) +
+                              (zb > 1 ? " z" + std::to_string(zb) + "x" + std::to_string(zx) : std::string{});
                 l.cache_temps = {hi_t, lo_t, flag_t};
             }
             finish_kernel(l);
             p_.launches.push_back(std::move(l));
         };
-        if (!tt.a_ready) emit_split("A", A, M, A.s0, A.s1, a_hi, a_lo, fa);
-        emit_split("B", B, N, B.s1, B.s0, b_hi, b_lo, fb);
+        // Batched operands are contiguous: A's rows of every batch form one
+        // [nb * M, K] matrix; B's batches are transposed one per blockIdx.z.
+        if (!tt.a_ready) emit_split("A", A, nb * M, A.s0, A.s1, a_hi, a_lo, fa);
+        emit_split("B", B, N, B.s1, B.s0, b_hi, b_lo, fb, nb, K * N);
         {
             launch_spec l;
             l.name = "pb_nonfinite_merge";
@@ -550,7 +567,7 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
         const bool softmax_split_ok = softmax && N % 1024 == 0 && N <= 16384;
         // One policy for both epilogues, so a softmax over a product and the
         // product realised alone sum K in the same parts.
-        if (tiles < slots / 2 && (!softmax || softmax_split_ok) && so == nullptr) {
+        if (nb == 1 && tiles < slots / 2 && (!softmax || softmax_split_ok) && so == nullptr) {
             double best = static_cast<double>(tiles) / static_cast<double>(slots);
             for (int64_t s = 2; s <= 16; s *= 2) {
                 if (raw_kb / s < 16) break;
@@ -561,7 +578,7 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
                     split = s;
                 }
             }
-        } else if (so == nullptr && (!softmax || softmax_split_ok) && tiles < 4 * slots && K > 4096) {
+        } else if (nb == 1 && so == nullptr && (!softmax || softmax_split_ok) && tiles < 4 * slots && K > 4096) {
             // A few waves of long tiles whose last wave leaves SMs idle
             // (config 5's second GEMM per rank at 4 and 8 GPUs: 512 and 256
             // tiles, 86.5 % filled): split K in 2 or 4 when that fills the
@@ -585,7 +602,7 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
         // A pair's k-blocks are 32 wide: whole ones per unit (past K the
         // loads read zeros). The periods keep the same length in K.
         if (pair) kb_unit = (kb_unit + 1) / 2 * 2;
-        const int64_t units = tiles * split;
+        const int64_t units = tiles * split * nb;  // grouped batches: every batch's tiles
         const int part = split > 1 ? new_temp(static_cast<size_t>(split * M * ((N + 3) / 4 * 4)) * 4) : -1;
         // With split-K the combine does the whole softmax: no row partials.
         const int stats = softmax && !softmax_split ? new_temp(static_cast<size_t>(M * tiles_n) * 8) : -1;
@@ -598,7 +615,10 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
         // Tile t -> output origin, tiles ordered in groups of group_m M-tiles
         // that sweep N (consecutive tiles, run at the same time by the
         // persistent CTAs, share A and B panels in L2).
-        src << "static __device__ __forceinline__ void pb_tile_origin(pb_u32 t, int& m0, int& n0) {\n"
+        // With grouped batches, tile t of batch bt is unit bt * tiles + t.
+        src << "static __device__ __forceinline__ void pb_tile_origin(pb_u32 t, int& m0, int& n0, pb_u32& bt) {\n"
+            << (nb > 1 ? "    bt = t / " + std::to_string(tiles) + "u;\n    t -= bt * " + std::to_string(tiles) + "u;\n"
+                       : std::string("    bt = 0u;\n"))
             << "    const pb_u32 tiles_m = " << tiles_m << "u, tiles_n = " << tiles_n << "u;\n"
             << "    const pb_u32 per_group = " << group_m << "u * tiles_n;\n"
             << "    const pb_u32 g = t / per_group, first_m = g * " << group_m << "u;\n"
@@ -606,6 +626,18 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
             << "    m0 = (int)((first_m + (t % per_group) % gm) * (PB_BM * PB_CTAS));\n"
             << "    n0 = (int)(((t % per_group) / gm) * PB_BN);\n"
             << "}\n";
+        // Grouped batches: each tile's epilogue sees its batch's output and
+        // leaves (the kernel's parameters carry a _g suffix).
+        std::string batch_ptrs;
+        if (nb > 1) {
+            batch_ptrs = "            float* const out = out_g + (pb_u64)bt * " + std::to_string(M * N) + "ull;\n";
+            for (size_t i = 0; i < k.leaves.size(); ++i) {
+                const int64_t bs = i < batches->leaf_stride.size() ? batches->leaf_stride[i] : 0;
+                batch_ptrs += "            const float* const in" + std::to_string(i) + " = in" + std::to_string(i) +
+                              "_g" + (bs > 0 ? " + (pb_u64)bt * " + std::to_string(bs) + "ull" : std::string{}) +
+                              ";\n";
+            }
+        }
         std::ostringstream body;
         // Persistent CTAs (one per SM) loop over tiles t = blockIdx.x,
         // + gridDim.x, ...; the k-block counter g and the period counter run
@@ -662,9 +694,13 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
              << "            bool stop = false;\n"
              << "            for (pb_u32 t = blockIdx.x / PB_CTAS; t < tiles && !stop; t += gridDim.x / PB_CTAS) {\n"
              << "                int m0, n0;\n"
-             << "                pb_tile_origin(t / PB_SPLIT, m0, n0);\n"
+             << "                pb_u32 bt;\n"
+             << "                pb_tile_origin(t / PB_SPLIT, m0, n0, bt);\n"
              << "                m0 += (int)(rank * PB_BM);   // this CTA's rows of A\n"
              << "                n0 += (int)(rank * PB_BNH);  // and of B (N)\n"
+             << (nb > 1 ? "                m0 += (int)(bt * " + std::to_string(M) + "u);  // batch bt's rows of the stacked halves\n"
+                          "                n0 += (int)(bt * " + std::to_string(N) + "u);\n"
+                        : std::string{})
              << "                const int kbase = (int)(t % PB_SPLIT) * num_kb;\n"
              << "                for (int kb = 0; kb < num_kb; ++kb, ++g) {\n"
              << "                    const int s = g % PB_STAGES;\n"
@@ -740,8 +776,10 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
              << "        bool ok = true;\n"
              << "        for (pb_u32 t = blockIdx.x / PB_CTAS; t < tiles && ok; t += gridDim.x / PB_CTAS) {\n"
              << "            int m0, n0;\n"
-             << "            pb_tile_origin(t / PB_SPLIT, m0, n0);\n"
+             << "            pb_u32 bt;\n"
+             << "            pb_tile_origin(t / PB_SPLIT, m0, n0, bt);\n"
              << "            m0 += (int)(rank * PB_BM);  // this CTA's 128 rows of the tile\n"
+             << batch_ptrs
              << "            float acc[PB_BN / 2];\n"
              << "            #pragma unroll\n"
              << "            for (int j = 0; j < PB_BN / 2; ++j) acc[j] = 0.0f;\n"
@@ -1020,8 +1058,9 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
         src << "extern \"C\" __global__ void __launch_bounds__(320, 1) " << l.name
             << "(const __grid_constant__ pb_tmap tm_ahi, const __grid_constant__ pb_tmap tm_alo, "
                "const __grid_constant__ pb_tmap tm_bhi, const __grid_constant__ pb_tmap tm_blo, ";
-        for (size_t i = 0; i < k.leaves.size(); ++i) src << "const float* __restrict__ in" << i << ", ";
-        src << "float* __restrict__ out, " << (softmax && !softmax_split ? "float2* __restrict__ stats, " : "")
+        const std::string gsuf = nb > 1 ? "_g" : "";
+        for (size_t i = 0; i < k.leaves.size(); ++i) src << "const float* __restrict__ in" << i << gsuf << ", ";
+        src << "float* __restrict__ out" << gsuf << ", " << (softmax && !softmax_split ? "float2* __restrict__ stats, " : "")
             << (so != nullptr ? "float* __restrict__ lo_out, int* __restrict__ split_flag, " : "")
             << "int* __restrict__ err, const int* __restrict__ nf) {\n" << body.str() << "}\n";
         l.source = src.str();
@@ -1048,6 +1087,7 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
             l.schedule += ", persistent CTAs (epilogue overlaps the next tile)";
         }
         if (split > 1) l.schedule += ", split-K x" + std::to_string(split) + " (raw partial tiles)";
+        if (nb > 1) l.schedule += ", " + std::to_string(nb) + " batches grouped in one launch";
         if (softmax && !softmax_split)
             l.schedule += ", softmax epilogue (exp(y - tile row max) and per-tile row (max, sum))";
         l.block = {320, 1, 1};
@@ -1064,8 +1104,8 @@ static __device__ __forceinline__ bool pb_bar_all(bool v) {
             a.swizzle = pair ? 3 : 2; // 128B / 64B: the box's inner extent is one swizzle row
             return a;
         };
-        l.args = {tmap_arg(a_hi, M, kBM), tmap_arg(a_lo, M, kBM), tmap_arg(b_hi, N, kBN / ctas),
-                  tmap_arg(b_lo, N, kBN / ctas)};
+        l.args = {tmap_arg(a_hi, nb * M, kBM), tmap_arg(a_lo, nb * M, kBM), tmap_arg(b_hi, nb * N, kBN / ctas),
+                  tmap_arg(b_lo, nb * N, kBN / ctas)};
         for (const kernel_arg& a : k.leaves) l.args.push_back(a);
         kernel_arg out_arg = temp_arg(out);
         out_arg.elem_offset = out_off;

@@ -2275,7 +2275,11 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
             // batch's GEMM then runs the same [M, N] epilogue. Leaves whose
             // batch stride would misalign their float4 loads, or a buffer
             // read at two batch strides, are not fused.
-            if (!tensor_core_gemm(M, N, K)) return -1;
+            // The same rule as the grouped tensor-core GEMM's.
+            const bool tc = Bt == 1 ? tensor_core_gemm(M, N, K)
+                                    : N > 1 && Bt * M <= (int64_t{1} << 30) && Bt * N <= (int64_t{1} << 30) &&
+                                          tensor_core_gemm(Bt * M, N, K);
+            if (!tc) return -1;
             std::vector<box> boxes;
             try {
                 boxes = build_boxes(k, id, g_.nodes[static_cast<size_t>(id)].shape, mm);
@@ -2303,13 +2307,6 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
         const int out = new_temp(static_cast<size_t>(Bt * M * N) * sizeof(float));
         if (Bt == 0 || M == 0 || N == 0) return out;
         rank_ = 2;
-        // The epilogue's leaves as batch t reads them.
-        auto leaves_at = [&](int64_t t) {
-            kernel kt = k;
-            for (size_t i = 0; i < batch_stride.size(); ++i)
-                if (batch_stride[i] > 0) kt.leaves[i].elem_offset += batch_stride[i] * t;
-            return kt;
-        };
         auto at = [](const kernel_arg& base, int64_t off, int64_t s0) {
             gemm_operand o;
             o.arg = base;
@@ -2318,23 +2315,28 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
             o.s1 = 1;
             return o;
         };
-        // Tensor cores: one GEMM per batch, each reading its operands and
-        // writing its output block through pointer offsets, so every batch
-        // runs the same compiled kernels and reuses one set of split temps.
+        // Tensor cores: every batch's tiles in one grouped launch (A's rows
+        // of all batches split as one matrix, B's batches transposed side
+        // by side), the epilogue's leaves moved by their batch strides.
+        // Realised operands keep their splits, as a 2-D matmul's do.
         gemm_temps shared;
-        shared.reused = true;
-        for (int64_t t = 0; t < Bt; ++t) {
-            const gemm_operand ga = at(A, t * M * K, K), gb = at(B, t * K * N, N);
-            kernel kt = leaves_at(t);
-            int nonfinite = -1;
-            if (emit_gemm_tc(id, b, kt, ga, gb, M, N, K, &nonfinite, nullptr, out, t * M * N, &shared) < 0) {
-                if (t != 0 || id != mm) throw std::logic_error("batched GEMM eligibility changed between batches");
-                // CUDA cores: every batch in one launch (blockIdx.y).
-                emit_gemm_simt(b, k, at(A, 0, K), at(B, 0, N), M, N, K, out, -1, 0, Bt);
-                return out;
-            }
-            emit_gemm_simt(b, kt, ga, gb, M, N, K, out, nonfinite, t * M * N);
+        gemm_batches groups;
+        groups.count = Bt;
+        groups.leaf_stride.assign(k.leaves.size(), 0);
+        for (size_t i = 0; i < batch_stride.size() && i < k.leaves.size(); ++i)
+            if (batch_stride[i] > 0) groups.leaf_stride[i] = batch_stride[i];
+        int nonfinite = -1;
+        if (emit_gemm_tc(id, b, k, at(A, 0, K), at(B, 0, N), M, N, K, &nonfinite, nullptr, out, 0, &shared,
+                         nullptr, &groups) >= 0) {
+            // Inf or NaN in an operand: the CUDA-core GEMM over every batch
+            // (blockIdx.y) into the same output; it returns at once otherwise.
+            emit_gemm_simt(b, k, at(A, 0, K), at(B, 0, N), M, N, K, out, nonfinite, 0, Bt, nullptr,
+                           &groups.leaf_stride);
+            return out;
         }
+        if (id != mm) throw std::logic_error("batched GEMM epilogue planned for tensor cores that do not apply");
+        // CUDA cores: every batch in one launch (blockIdx.y).
+        emit_gemm_simt(b, k, at(A, 0, K), at(B, 0, N), M, N, K, out, -1, 0, Bt);
         return out;
     }
 
@@ -2469,7 +2471,8 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
 
     int lowerer::emit_gemm_simt(const box& b, kernel& k, const gemm_operand& A, const gemm_operand& B,
                                 int64_t M, int64_t N, int64_t K, int out_temp, int guard_temp, int64_t out_off,
-                                int64_t batches, const split_output* so) {
+                                int64_t batches, const split_output* so,
+                                const std::vector<int64_t>* leaf_batch_stride) {
         const int out = so != nullptr ? so->hi
                         : out_temp >= 0 ? out_temp
                                         : new_temp(static_cast<size_t>(batches * M * N) * sizeof(float));
@@ -2508,11 +2511,17 @@ static __device__ __forceinline__ float pb_get(const float4& v, int e) {
         // operand is finite it costs one short launch, not tiles' worth.
         const int64_t tiles_n = (N + 63) / 64, tiles = tiles_n * ((M + 63) / 64);
         if (guard_temp >= 0) body << "    if (*(const volatile int*)guard == 0) return;\n";
-        if (batches > 1)
+        if (batches > 1) {
             // One matrix product per blockIdx.y over contiguous [M, K] and
-            // [K, N] operands and [M, N] outputs.
+            // [K, N] operands and [M, N] outputs; epilogue leaves move by
+            // their own batch strides.
             body << "    A += (pb_u64)blockIdx.y * " << M * K << "ull;\n    B += (pb_u64)blockIdx.y * " << K * N
                  << "ull;\n    out += (pb_u64)blockIdx.y * " << M * N << "ull;\n";
+            if (leaf_batch_stride != nullptr)
+                for (size_t i = 0; i < leaf_batch_stride->size(); ++i)
+                    if ((*leaf_batch_stride)[i] > 0)
+                        body << "    in" << i << " += (pb_u64)blockIdx.y * " << (*leaf_batch_stride)[i] << "ull;\n";
+        }
         body << "    __shared__ float As[16][68];\n    __shared__ float Bs[16][68];\n";
         body << "    const pb_u32 tx = threadIdx.x & 15u, ty = threadIdx.x >> 4;\n";
         body << "    for (" << I << " tile = blockIdx.x; tile < " << lit(tiles, wide) << "; tile += gridDim.x) {\n";

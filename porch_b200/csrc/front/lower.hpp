@@ -66,16 +66,13 @@ namespace porch::detail {
 
     // A matmul operand [rows, cols] read in place: element (i, j) at
     // off + i * s0 + j * s1 of `arg` (an input slot, or a contiguous temp).
-    // Temps of one tensor-core GEMM's operand splits and flags, shared by
-    // the GEMMs of a batched matmul (they run one after another).
+    // Temps of one tensor-core GEMM's operand splits and flags (a caller may
+    // supply them, e.g. when A's halves come from the GEMM that produced A).
     struct gemm_temps {
         int a_hi = -1, a_lo = -1, b_hi = -1, b_lo = -1, nf = -1, fa = -1, fb = -1;
         // A's hi / lo / flag were written by the GEMM that produced A (its
         // split-output epilogue): no split pass for A, and fa not cleared.
         bool a_ready = false;
-        // The temps serve several GEMMs in turn (a batched matmul): their
-        // splits are not kept, since kept splits are bound by temp.
-        bool reused = false;
     };
 
     // A GEMM epilogue that writes its result as the 3xTF32 halves a
@@ -85,6 +82,15 @@ namespace porch::detail {
     struct split_output {
         int hi = -1, lo = -1, flag = -1;
         int64_t kp = 0;
+    };
+
+    // A grouped batched GEMM: `count` products [M, K] @ [K, N] of contiguous
+    // operands ([count, M, K] and [count, K, N]) into [count, M, N], every
+    // batch's tiles in one launch; leaf_stride[i] = elements between
+    // consecutive batches of epilogue leaf i (0: the same for every batch).
+    struct gemm_batches {
+        int64_t count = 1;
+        std::vector<int64_t> leaf_stride;
     };
 
     struct gemm_operand {
@@ -163,18 +169,19 @@ namespace porch::detail {
         // that many products over contiguous operands (blockIdx.y).
         int emit_gemm_simt(const box& b, kernel& k, const gemm_operand& A, const gemm_operand& B,
                            int64_t M, int64_t N, int64_t K, int out_temp = -1, int guard_temp = -1,
-                           int64_t out_off = 0, int64_t batches = 1, const split_output* so = nullptr);
+                           int64_t out_off = 0, int64_t batches = 1, const split_output* so = nullptr,
+                           const std::vector<int64_t>* leaf_batch_stride = nullptr);
         // When matmul operand `a` ([M, K]) is a GEMM-with-epilogue read by
         // nothing else, lowers it with a split-output epilogue into `t`'s A
         // temps and returns true; `op` then reads those halves.
         bool presplit_operand(int a, int64_t M, int64_t N, int64_t K, gemm_temps& t, gemm_operand& op);
         // Internal batched matmul [B, M, K] @ [B, K, N] at `mm`, with the
         // elementwise graph `id` (rank 3, the product as one leaf; id == mm
-        // for the bare product) as the epilogue: a tensor-core GEMM per batch
-        // (pointer offsets for operands, output and epilogue leaves), or one
-        // CUDA-core launch over every batch for a bare product. Returns -1
-        // when the epilogue cannot be fused (the caller then realises the
-        // product on its own).
+        // for the bare product) as the epilogue: one grouped tensor-core GEMM
+        // over every batch's tiles (epilogue leaves moved by their batch
+        // strides), or one CUDA-core launch over every batch for a bare
+        // product. Returns -1 when the epilogue cannot be fused (the caller
+        // then realises the product on its own).
         int emit_batched_gemm(int id, int mm);
         // tcgen05 3xTF32 path; returns -1 when the shape is not eligible. On
         // success *nonfinite receives a temp whose first int is set when an
@@ -186,7 +193,8 @@ namespace porch::detail {
         int emit_gemm_tc(int id, const box& b, kernel& k, const gemm_operand& A,
                          const gemm_operand& B, int64_t M, int64_t N, int64_t K, int* nonfinite,
                          int* row_partials = nullptr, int out_temp = -1, int64_t out_off = 0,
-                         gemm_temps* shared = nullptr, const split_output* so = nullptr);
+                         gemm_temps* shared = nullptr, const split_output* so = nullptr,
+                         const gemm_batches* batches = nullptr);
         // softmax(x, last axis) where x is an elementwise tree over one
         // rank-2 matmul `mm`: the GEMM's softmax epilogue plus a normalising
         // pass; -1 when the tensor-core GEMM does not apply.
