@@ -145,9 +145,10 @@ int pb_expr_concat(const pb_expr* lhs, const pb_expr* rhs, size_t axis,
 int pb_expr_permute(const pb_expr* value, const int64_t* perm, size_t rank,
                     pb_expr** out);
 /* Batched matmul: [B,M,K] @ [B,K,N] -> [B,M,N], one fp32 product per batch
- * (3xTF32 on the tensor cores when M*N*K >= 2^27, else the CUDA-core
- * GEMM). No counterpart in the reference, whose matmul is rank 2 only
- * (src/tensor.cpp:366-381); PB_MATMUL keeps that rule. */
+ * (3xTF32 on the tensor cores, every batch in one launch, when
+ * B*M*N*K >= 2^27; else the CUDA-core GEMM). No counterpart in the
+ * reference, whose matmul is rank 2 only (src/tensor.cpp:366-381);
+ * PB_MATMUL keeps that rule. */
 int pb_expr_batched_matmul(const pb_expr* lhs, const pb_expr* rhs, pb_expr** out);
 /* sum / max with keepdim (PB_SUM, PB_MAX) */
 int pb_expr_reduce(int op, const pb_expr* value, size_t axis, int keepdim,
